@@ -1,0 +1,289 @@
+// extern "C" launchers of the decode hot path (declared in include/mllb200.h).
+//
+// The whole library is this one translation unit: every kernel header is
+// included here, so device code needs no relocatable linking and each module
+// owns exactly one device error word.
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+
+#include "mllb200.h"
+#include "common.cuh"
+#include "imrope.cuh"
+#include "misc.cuh"
+#include "q4k.cuh"
+#include "q6k.cuh"
+#include "q8_1.cuh"
+
+namespace {
+
+thread_local char g_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(MLLB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  g_error[0] = '\0';
+  return MLLB_OK;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
+
+constexpr int kMaxDevices = 64;
+
+int current_device(int* dev) {
+  const cudaError_t e = cudaGetDevice(dev);
+  if (e != cudaSuccess) return fail(MLLB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (*dev < 0 || *dev >= kMaxDevices) return fail(MLLB_EUNSUPPORTED, "device index %d out of range", *dev);
+  return MLLB_OK;
+}
+
+int sm_count(int dev) {
+  static int cache[kMaxDevices] = {0};
+  if (cache[dev] == 0) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    cache[dev] = v > 0 ? v : 1;
+  }
+  return cache[dev];
+}
+
+// Per-kernel, per-device launch preparation for the streaming kernels:
+// opt in to the dynamic shared memory once and cache the resident CTAs per SM.
+struct OccupancyEntry {
+  const void* fn;
+  int dev;
+  int blocks_per_sm;
+};
+constexpr int kOccupancySlots = 256;
+OccupancyEntry g_occupancy[kOccupancySlots];
+int g_occupancy_used = 0;
+std::mutex g_occupancy_mutex;
+
+template <typename Kernel>
+int stream_grid(Kernel kernel, int smem_bytes, int dev, int tiles, int* grid) {
+  const void* fn = reinterpret_cast<const void*>(kernel);
+  int blocks_per_sm = 0;
+  {
+    std::lock_guard<std::mutex> lock(g_occupancy_mutex);
+    for (int i = 0; i < g_occupancy_used; ++i)
+      if (g_occupancy[i].fn == fn && g_occupancy[i].dev == dev) blocks_per_sm = g_occupancy[i].blocks_per_sm;
+    if (blocks_per_sm == 0) {
+      cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+      if (e != cudaSuccess) return fail(MLLB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+      int occ = 0;
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, mllb::kStreamThreads, smem_bytes);
+      if (e != cudaSuccess) return fail(MLLB_ECUDA, "occupancy query: %s", cudaGetErrorString(e));
+      blocks_per_sm = occ > 0 ? occ : 1;
+      if (g_occupancy_used < kOccupancySlots) g_occupancy[g_occupancy_used++] = {fn, dev, blocks_per_sm};
+    }
+  }
+  const int wave = sm_count(dev) * blocks_per_sm;
+  *grid = tiles < wave ? tiles : wave;
+  return MLLB_OK;
+}
+
+int check_rows(int64_t n, int64_t k, int64_t max_rows) {
+  if (n <= 0 || n > max_rows) return fail(MLLB_EINVAL, "row count %lld out of range", static_cast<long long>(n));
+  if (k <= 0 || k % 256) return fail(MLLB_EINVAL, "K=%lld is not a positive multiple of 256", static_cast<long long>(k));
+  if (k / 256 > 4096) return fail(MLLB_EUNSUPPORTED, "K=%lld too large", static_cast<long long>(k));
+  return MLLB_OK;
+}
+
+template <int NB, bool DUAL>
+int launch_q4k_stream(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
+                      int n, cudaStream_t stream) {
+  using Cfg = mllb::Q4kStreamConfig<NB, DUAL>;
+  int dev, grid, rc;
+  if ((rc = current_device(&dev))) return rc;
+  auto kernel = mllb::q4k_stream_kernel<NB, DUAL>;
+  const int tiles = (n + Cfg::G::kTileRows - 1) / Cfg::G::kTileRows;
+  if ((rc = stream_grid(kernel, Cfg::kSmemBytes, dev, tiles, &grid))) return rc;
+  kernel<<<grid, mllb::kStreamThreads, Cfg::kSmemBytes, stream>>>(w0, w1, q8, o0, o1, o2, n);
+  return check_launch(DUAL ? "q4k gate/up stream kernel" : "q4k stream kernel");
+}
+
+int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
+                 int64_t n, int64_t k, cudaStream_t stream) {
+  const int nb = static_cast<int>(k / 256);
+  const bool dual = w1 != nullptr;
+  const int rows = static_cast<int>(n);
+  switch (nb) {
+    case 8:
+      return dual ? launch_q4k_stream<8, true>(w0, w1, q8, o0, o1, o2, rows, stream)
+                  : launch_q4k_stream<8, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+    case 10:
+      return dual ? launch_q4k_stream<10, true>(w0, w1, q8, o0, o1, o2, rows, stream)
+                  : launch_q4k_stream<10, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+    case 16:
+      return dual ? launch_q4k_stream<16, true>(w0, w1, q8, o0, o1, o2, rows, stream)
+                  : launch_q4k_stream<16, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+    default:
+      mllb::q4k_rowblock_kernel<<<rows, 128, 0, stream>>>(w0, w1, q8, o0, o1, o2, nb);
+      return check_launch("q4k row kernel");
+  }
+}
+
+template <int NB>
+int launch_q6k_stream(const uint8_t* w, const uint8_t* q8, float* out, int n, cudaStream_t stream) {
+  using G = mllb::Q6kGeom<NB>;
+  int dev, grid, rc;
+  if ((rc = current_device(&dev))) return rc;
+  auto kernel = mllb::q6k_stream_kernel<NB>;
+  const int tiles = (n + G::kTileRows - 1) / G::kTileRows;
+  if ((rc = stream_grid(kernel, G::kSmemBytes, dev, tiles, &grid))) return rc;
+  kernel<<<grid, mllb::kStreamThreads, G::kSmemBytes, stream>>>(w, q8, out, n);
+  return check_launch("q6k stream kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int mllb_abi_version(void) { return MLLB_ABI_VERSION; }
+
+const char* mllb_last_error(void) { return g_error; }
+
+int mllb_device_error(uint32_t* bits, int clear) {
+  if (!bits) return fail(MLLB_EINVAL, "null pointer: bits");
+  cudaError_t e = cudaMemcpyFromSymbol(bits, g_mllb_device_error, sizeof(uint32_t));
+  if (e != cudaSuccess) return fail(MLLB_ECUDA, "reading the device error word: %s", cudaGetErrorString(e));
+  if (clear) {
+    const uint32_t zero = 0;
+    e = cudaMemcpyToSymbol(g_mllb_device_error, &zero, sizeof(uint32_t));
+    if (e != cudaSuccess) return fail(MLLB_ECUDA, "clearing the device error word: %s", cudaGetErrorString(e));
+  }
+  return MLLB_OK;
+}
+
+int mllb_q8_1_quantize(const float* x, void* q8, int64_t k, int s_mode, void* stream) {
+  if (!x || !q8) return fail(MLLB_EINVAL, "null pointer");
+  if (k <= 0 || k % 32) return fail(MLLB_EINVAL, "k=%lld is not a positive multiple of 32", static_cast<long long>(k));
+  if (s_mode != MLLB_Q8_1_S_D_SUMQ && s_mode != MLLB_Q8_1_S_SUM_X) return fail(MLLB_EINVAL, "unknown s_mode %d", s_mode);
+  if (!aligned(x, 4) || !aligned(q8, 4)) return fail(MLLB_EALIGN, "x and q8 must be 4-byte aligned");
+  const int64_t blocks = k / 32;
+  int64_t grid = (blocks + 7) / 8;
+  if (grid > 65535) grid = 65535;
+  mllb::q8_1_quantize_kernel<<<static_cast<int>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      x, static_cast<uint8_t*>(q8), blocks, s_mode);
+  return check_launch("q8_1 quantize kernel");
+}
+
+int mllb_q4k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
+  if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, q8/out 4-byte alignment");
+  return q4k_dispatch(static_cast<const uint8_t*>(weights), nullptr, static_cast<const uint8_t*>(q8), out, nullptr,
+                      nullptr, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int mllb_q4k_gate_up(const void* up_weights, const void* gate_weights, const void* q8, float* up, float* gate,
+                     float* prod, int64_t n, int64_t k, void* stream) {
+  if (!up_weights || !gate_weights || !q8) return fail(MLLB_EINVAL, "null pointer");
+  if (!up && !gate && !prod) return fail(MLLB_EINVAL, "no output requested");
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (!aligned(up_weights, 16) || !aligned(gate_weights, 16) || !aligned(q8, 4) || !aligned(up, 4) ||
+      !aligned(gate, 4) || !aligned(prod, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, q8/outputs 4-byte alignment");
+  return q4k_dispatch(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
+                      static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream));
+}
+
+int mllb_q6k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
+  if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, q8/out 4-byte alignment");
+  const uint8_t* w = static_cast<const uint8_t*>(weights);
+  const uint8_t* a = static_cast<const uint8_t*>(q8);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int nb = static_cast<int>(k / 256);
+  // Streaming tiles are whole 16-byte runs only when rows * nb % 8 == 0;
+  // the last (n % 8) rows go through the row-per-CTA kernel.
+  const int64_t main_rows = n - n % 8;
+  const int64_t tail = n - main_rows;
+  if (main_rows > 0) {
+    switch (nb) {
+      case 8: rc = launch_q6k_stream<8>(w, a, out, static_cast<int>(main_rows), s); break;
+      case 10: rc = launch_q6k_stream<10>(w, a, out, static_cast<int>(main_rows), s); break;
+      case 16: rc = launch_q6k_stream<16>(w, a, out, static_cast<int>(main_rows), s); break;
+      default:
+        mllb::q6k_rowblock_kernel<<<static_cast<int>(main_rows), 128, 0, s>>>(w, a, out, nb);
+        rc = check_launch("q6k row kernel");
+    }
+    if (rc) return rc;
+  }
+  if (tail > 0) {
+    mllb::q6k_rowblock_kernel<<<static_cast<int>(tail), 128, 0, s>>>(w + main_rows * nb * mllb::kQ6kBlockBytes, a,
+                                                                     out + main_rows, nb);
+    rc = check_launch("q6k row kernel (tail)");
+  }
+  return rc;
+}
+
+int mllb_rmsnorm_imrope_q_batched(const float* q, const float* gamma, const int32_t* positions,
+                                  const float* theta_scale, double theta_value, float* out, int64_t tokens,
+                                  int64_t heads_per_token, void* stream) {
+  if (!q || !gamma || !positions || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (tokens <= 0 || heads_per_token <= 0) return fail(MLLB_EINVAL, "empty shape");
+  if (!aligned(q, 4) || !aligned(gamma, 4) || !aligned(positions, 4) || !aligned(out, 4) ||
+      (theta_scale && !aligned(theta_scale, 4)))
+    return fail(MLLB_EALIGN, "fp32/int32 pointers must be 4-byte aligned");
+  const int64_t heads = tokens * heads_per_token;
+  int64_t grid = (heads + 3) / 4;
+  if (grid > 65535) grid = 65535;
+  mllb::imrope_q_kernel<<<static_cast<int>(grid), 128, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, gamma, positions, theta_scale, theta_value, out, heads, heads_per_token);
+  return check_launch("imrope kernel");
+}
+
+int mllb_rmsnorm_imrope_q(const float* q, const float* gamma, const int32_t* positions, const float* theta_scale,
+                          float* out, int64_t heads, void* stream) {
+  if (!theta_scale) return fail(MLLB_EINVAL, "null pointer: theta_scale");
+  return mllb_rmsnorm_imrope_q_batched(q, gamma, positions, theta_scale, 0.0, out, 1, heads, stream);
+}
+
+int mllb_q4k_subdots(const void* weights, const void* q8, int32_t* dots, int32_t* asums, int64_t n, int64_t k,
+                     void* stream) {
+  if (!weights || !q8 || !dots || !asums) return fail(MLLB_EINVAL, "null pointer");
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (!aligned(weights, 4) || !aligned(q8, 4) || !aligned(dots, 4) || !aligned(asums, 4))
+    return fail(MLLB_EALIGN, "pointers must be 4-byte aligned");
+  const int64_t total = n * (k / 32) + k / 32;
+  int64_t grid = (total + 255) / 256;
+  if (grid > 65535) grid = 65535;
+  mllb::q4k_subdots_kernel<<<static_cast<int>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(weights), static_cast<const uint8_t*>(q8), dots, asums, n,
+      static_cast<int>(k / 256));
+  return check_launch("q4k subdots kernel");
+}
+
+int mllb_stream_read(const void* data, int64_t bytes, void* out, int64_t blocks, void* stream) {
+  if (!data || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (bytes <= 0 || bytes % 16) return fail(MLLB_EINVAL, "bytes must be a positive multiple of 16");
+  if (!aligned(data, 16) || !aligned(out, 16)) return fail(MLLB_EALIGN, "data and out must be 16-byte aligned");
+  if (blocks <= 0) {
+    int dev, rc;
+    if ((rc = current_device(&dev))) return rc;
+    blocks = static_cast<int64_t>(sm_count(dev)) * 8;
+  }
+  if (blocks > 1 << 20) return fail(MLLB_EINVAL, "too many blocks");
+  mllb::stream_read_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(data), bytes / 16, static_cast<uint4*>(out));
+  return check_launch("stream read kernel");
+}
+
+}  // extern "C"

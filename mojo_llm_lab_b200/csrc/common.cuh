@@ -1,0 +1,171 @@
+// Device-side building blocks shared by the decode hot-path kernels (sm_100a).
+//
+// * mbarrier + cp.async.bulk (the TMA bulk-copy engine) for streaming weight
+//   tiles from HBM into shared memory without tying up registers;
+// * bounded waits: every wait on an mbarrier gives up after ~1 s of
+//   %globaltimer time (and an iteration cap), records an error bit in the
+//   library's device error word and lets the kernel finish, so a lost
+//   transaction can never hang the GPU;
+// * exact conversions and warp reductions used by the fp64 row accumulation.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace mllb {
+
+// Bits of the device error word (read with mllb_device_error()).
+enum : uint32_t {
+  kErrFullWaitTimeout = 1u << 0,   // consumer gave up waiting for a weight tile
+  kErrEmptyWaitTimeout = 1u << 1,  // producer gave up waiting for a free stage
+  kErrDrainTimeout = 1u << 2,      // producer gave up waiting for its last copies
+};
+
+// 1 s of wall time, and a hard iteration cap behind it.
+constexpr uint64_t kWaitLimitNs = 1000000000ull;
+constexpr uint32_t kWaitMaxIters = 1u << 28;
+
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Make mbarrier initialisation visible to the async (TMA) proxy.
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for the phase of `bar` with the given parity to complete.  Returns
+// false (after ~1 s) if it never does; the caller records the error.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 255u) == 255u && global_timer_ns() - start > kWaitLimitNs) break;
+  }
+  return false;
+}
+
+// L2 policy for data read exactly once (weights): evict first.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// TMA bulk copy global -> shared, completion signalled on `bar` (tx bytes).
+// dst and src must be 16-byte aligned and bytes a multiple of 16.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,
+                                              uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], "
+      "%4;" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+      : "memory");
+}
+
+// Named barrier over `threads` threads (id 0 is __syncthreads()).
+__device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Streaming 16-byte global load that does not allocate in L1.
+__device__ __forceinline__ uint4 ldg_stream128(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// dot of 4 unsigned bytes with 4 signed bytes, plus c.
+__device__ __forceinline__ int dp4a_us(uint32_t a, uint32_t b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ int dp4a_ss(uint32_t a, uint32_t b, int c) {
+  return __dp4a(static_cast<int>(a), static_cast<int>(b), c);
+}
+
+// Sum of the 4 signed bytes of w.
+__device__ __forceinline__ int byte_sum_s8(uint32_t w, int c) { return dp4a_us(0x01010101u, w, c); }
+
+// fp16 bit pattern -> double, exact (fp16 -> fp32 is exact, fp32 -> fp64 is exact).
+__device__ __forceinline__ double half_bits_to_double(uint32_t bits16) {
+  return static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu))));
+}
+
+__device__ __forceinline__ double warp_sum_double(double v) {
+#pragma unroll
+  for (int offset = 16; offset >= 1; offset >>= 1) v += __shfl_xor_sync(0xffffffffu, v, offset);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max_float(float v) {
+#pragma unroll
+  for (int offset = 16; offset >= 1; offset >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, offset));
+  return v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+  for (int offset = 16; offset >= 1; offset >>= 1) v += __shfl_xor_sync(0xffffffffu, v, offset);
+  return v;
+}
+
+// Sum of 32 floats in xor-butterfly order (offsets 16, 8, 4, 2, 1).
+__device__ __forceinline__ float warp_sum_float_butterfly(float v) {
+#pragma unroll
+  for (int offset = 16; offset >= 1; offset >>= 1) v += __shfl_xor_sync(0xffffffffu, v, offset);
+  return v;
+}
+
+constexpr int gcd_constexpr(int a, int b) { return b == 0 ? a : gcd_constexpr(b, a % b); }
+
+}  // namespace mllb
+
+// The device error word of this module (bounded-wait timeouts).  Each module
+// is one translation unit (the library is built from capi.cu alone), so this
+// definition exists once per module.
+__device__ uint32_t g_mllb_device_error;
+
+namespace mllb {
+__device__ __forceinline__ void record_error(uint32_t bits) { atomicOr(&g_mllb_device_error, bits); }
+}  // namespace mllb

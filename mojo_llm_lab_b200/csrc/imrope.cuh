@@ -1,0 +1,73 @@
+// Fused RMSNorm + learned gamma + IMROPE on the Q tensor, one warp per head.
+//
+// Replaces kernels/fused_q_imrope_runtime_fastpow.mojo:8-36 (and GGML's
+// rms_norm -> mul -> rope_multi chain, benchmark/bench.c:205-211):
+//   r      = 1 / sqrt(sum(x^2) / 128 + 1e-6)
+//   y_i    = x_i * r * gamma_i
+//   axis(p)= 1 if p%3==1 and p<60; 2 if p%3==2 and p<60; 0 if p%3==0 and p<72; else 3
+//   theta  = pos[axis(p)] * theta_scale^p            (pairs p < 64)
+//   out_p  = y_p cos(theta) - y_{p+64} sin(theta),  out_{p+64} = y_p sin(theta) + y_{p+64} cos(theta)
+// Lane l of the head's warp owns pairs l and l+32 (coalesced 128-byte loads
+// of x and gamma).  The norm and the angles are evaluated in fp64: at position
+// 32768 an fp32 angle carries ~4e-3 rad of rounding, 250x the 1e-5 output
+// tolerance, while pos * theta_scale^p in fp64 with fp64 sincos is accurate to
+// ~1e-11 rad.  The op moves 33 KB; it is latency-bound, not HBM-bound.
+#pragma once
+
+#include "common.cuh"
+
+namespace mllb {
+
+constexpr int kHeadDim = 128;
+
+__device__ __forceinline__ int imrope_axis(int pair) {
+  if (pair % 3 == 1 && pair < 60) return 1;
+  if (pair % 3 == 2 && pair < 60) return 2;
+  if (pair % 3 == 0 && pair < 72) return 0;
+  return 3;
+}
+
+// One head, computed by the 32 lanes of the calling warp.
+__device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                 const int32_t* __restrict__ pos, double theta_scale,
+                                                 float* __restrict__ out, int lane) {
+  const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+  double ss = static_cast<double>(x0) * x0;
+  ss = fma(static_cast<double>(x1), static_cast<double>(x1), ss);
+  ss = fma(static_cast<double>(x2), static_cast<double>(x2), ss);
+  ss = fma(static_cast<double>(x3), static_cast<double>(x3), ss);
+  ss = warp_sum_double(ss);
+  const double r = 1.0 / sqrt(ss / kHeadDim + 1e-6);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int p = lane + 32 * half;
+    const double angle = static_cast<double>(pos[imrope_axis(p)]) * pow(theta_scale, static_cast<double>(p));
+    double s, c;
+    sincos(angle, &s, &c);
+    const double ya = static_cast<double>(half ? x1 : x0) * r * static_cast<double>(gamma[p]);
+    const double yb = static_cast<double>(half ? x3 : x2) * r * static_cast<double>(gamma[p + 64]);
+    out[p] = static_cast<float>(ya * c - yb * s);
+    out[p + 64] = static_cast<float>(ya * s + yb * c);
+  }
+}
+
+// Grid-stride over heads, one warp each.  Head h belongs to token
+// h / heads_per_token and uses that token's 4 positions.  The theta scale
+// comes from device memory (fp32, the reference ABI) unless theta_ptr is null,
+// in which case theta_value is used.
+__global__ void __launch_bounds__(128) imrope_q_kernel(const float* __restrict__ q, const float* __restrict__ gamma,
+                                                       const int32_t* __restrict__ positions,
+                                                       const float* __restrict__ theta_ptr, double theta_value,
+                                                       float* __restrict__ out, int64_t heads,
+                                                       int64_t heads_per_token) {
+  const int lane = threadIdx.x & 31;
+  const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t h = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); h < heads;
+       h += warps) {
+    imrope_head_warp(q + h * kHeadDim, gamma, positions + 4 * (h / heads_per_token), theta, out + h * kHeadDim,
+                     lane);
+  }
+}
+
+}  // namespace mllb

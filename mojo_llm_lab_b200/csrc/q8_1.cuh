@@ -1,0 +1,64 @@
+// Q8_1 activation quantiser: fp32 x[k] -> k/32 blocks of 36 bytes
+// (fp16 d, fp16 s, 32 x int8 q).
+//
+// Replaces GGML's quantize_q8_1 graph node that the reference clones in front
+// of every matvec (benchmark/q4_compare.c:328-330, bytes checked at :351-357),
+// with the fixture rule of tools/generate_q4_matvec_fixtures.py:56-59.
+// Arithmetic (bit-exact with the CPU oracle):
+//   amax = max |x|          d = amax / 127           (IEEE division)
+//   q    = amax == 0 ? 0 : roundf(x / d)             (IEEE division, ties away)
+//   d16  = fp16(d) RNE
+//   s    = fp16(fp16(d) * sum(q))   [MLLB_Q8_1_S_D_SUMQ, default]
+//        = fp16(sum(x))             [MLLB_Q8_1_S_SUM_X, butterfly order]
+// One warp per block of 32 values; the quantiser is HBM/latency bound
+// (4 B in, 1.125 B out per value).
+#pragma once
+
+#include "common.cuh"
+
+namespace mllb {
+
+enum : int { kQ8SumDTimesSumQ = 0, kQ8SumX = 1 };
+
+// Quantise the 32 values held one per lane; returns this lane's int8 q and
+// fills d16 / s16 (identical in every lane).
+__device__ __forceinline__ int q8_1_quantize_lane(float x, int s_mode, uint32_t* d16, uint32_t* s16) {
+  const float amax = warp_max_float(fabsf(x));
+  const float d = __fdiv_rn(amax, 127.0f);
+  const int q = amax == 0.0f ? 0 : static_cast<int>(roundf(__fdiv_rn(x, d)));
+  const __half dh = __float2half_rn(d);
+  float s;
+  if (s_mode == kQ8SumX) {
+    s = warp_sum_float_butterfly(x);
+  } else {
+    s = __half2float(dh) * static_cast<float>(warp_sum_int(q));  // exact product
+  }
+  *d16 = __half_as_ushort(dh);
+  *s16 = __half_as_ushort(__float2half_rn(s));
+  return q;
+}
+
+// grid-stride over Q8_1 blocks, one warp each.
+__global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ out,
+                                                            int64_t blocks, int s_mode) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < blocks;
+       g += warps) {
+    const float v = x[g * 32 + lane];
+    uint32_t d16, s16;
+    const int q = q8_1_quantize_lane(v, s_mode, &d16, &s16);
+    // Pack 4 consecutive int8 per lane group and store 8 words per block.
+    const uint32_t b = static_cast<uint32_t>(q) & 0xffu;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
+    uint8_t* blk = out + g * 36;
+    if ((lane & 3) == 0) {
+      *reinterpret_cast<uint32_t*>(blk + 4 + lane) = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    }
+    if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = d16 | (s16 << 16);
+  }
+}
+
+}  // namespace mllb

@@ -1,0 +1,241 @@
+"""PyTorch-facing host API of the decode hot path.
+
+Thin wrappers over the C ABI (include/mllb200.h): they validate tensors,
+derive shapes from the byte layouts, pick the current CUDA stream and call the
+library.  Function names and argument order follow the reference's kernel
+entries, so code written against those reads the same:
+
+    fused_q_imrope_runtime_fastpow(q, gamma, positions, output, theta_scale)
+                                   kernels/fused_q_imrope_runtime_fastpow.mojo:8-14
+    q4_k_q8_1_matvec(weights, activations, output)
+                                   kernels/q4_k_q8_1_matvec_dp4a_128.mojo:8-13
+    q4_k_q8_1_gate_order(weights, gate_weights, activations, output)
+                                   kernels/q4_k_q8_1_gate_order.mojo:55-60
+    quantize_q8_1(x, out)          GGML quantize_q8_1 (benchmark/q4_compare.c:328)
+    q6_k_q8_1_matvec(weights, activations, output)    GGML mul_mat_vec_q<Q6_K>
+
+Errors: ValueError for shapes/dtypes/alignment (the reference's oracles raise
+ValueError for wrong layouts), MllbError for CUDA failures.  All tensors must
+live on the same CUDA device; nothing here copies to or from the host.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import formats as F
+from ._lib import S_D_SUMQ, S_SUM_X, check, device_error, lib  # noqa: F401
+
+__all__ = [
+    "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
+    "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
+    "S_D_SUMQ", "S_SUM_X",
+]
+
+
+def _stream(t: torch.Tensor):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype: torch.dtype) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise ValueError(f"{name} must be a torch.Tensor")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name} must be contiguous")
+
+
+def _same_device(*ts: torch.Tensor) -> None:
+    devs = {t.device for t in ts if t is not None}
+    if len(devs) > 1:
+        raise ValueError(f"tensors on different devices: {sorted(map(str, devs))}")
+
+
+def _k_from_q8(act: torch.Tensor) -> int:
+    n = act.numel()
+    if n == 0 or n % F.Q8_1_BLOCK_BYTES:
+        raise ValueError("Q8_1 activations must be whole 36-byte blocks")
+    return n // F.Q8_1_BLOCK_BYTES * F.Q8_1_GROUP
+
+
+def _rows(weights: torch.Tensor, row_bytes: int, what: str) -> int:
+    n = weights.numel()
+    if n == 0 or n % row_bytes:
+        raise ValueError(f"Mismatched {what}/Q8_1 block counts")
+    return n // row_bytes
+
+
+# ------------------------------------------------------------------- Q8_1
+
+def quantize_q8_1(x: torch.Tensor, out: torch.Tensor | None = None, s_mode: int = S_D_SUMQ) -> torch.Tensor:
+    """fp32 x[k] -> Q8_1 bytes (uint8[k/32*36])."""
+    _need(x, "x", torch.float32)
+    k = x.numel()
+    if k == 0 or k % F.Q8_1_GROUP:
+        raise ValueError("Q8_1 needs a positive multiple of 32 values")
+    if out is None:
+        out = torch.empty(k // 32 * 36, dtype=torch.uint8, device=x.device)
+    _need(out, "out", torch.uint8)
+    if out.numel() != k // 32 * 36:
+        raise ValueError("out has the wrong size")
+    _same_device(x, out)
+    check(lib().mllb_q8_1_quantize(x.data_ptr(), out.data_ptr(), k, s_mode, _stream(x)), "quantize_q8_1")
+    return out
+
+
+# ------------------------------------------------------------------- Q4_K
+
+def q4_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
+                     output: torch.Tensor | None = None) -> torch.Tensor:
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(weights, F.q4k_row_bytes(k), "Q4_K")
+    if output is None:
+        output = torch.empty(rows, dtype=torch.float32, device=weights.device)
+    _need(output, "output", torch.float32)
+    if output.numel() != rows:
+        raise ValueError("output has the wrong size")
+    _same_device(weights, activations, output)
+    check(lib().mllb_q4k_matvec(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
+                                _stream(weights)), "q4_k_q8_1_matvec")
+    return output
+
+
+def q4k_gate_up(up_weights: torch.Tensor, gate_weights: torch.Tensor, activations: torch.Tensor,
+                up: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                prod: torch.Tensor | None = None, want=("up", "gate", "prod")):
+    """Fused gate/up: returns (up, gate, prod) with prod = up * silu(gate)."""
+    _need(up_weights, "up_weights", torch.uint8)
+    _need(gate_weights, "gate_weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(up_weights, F.q4k_row_bytes(k), "Q4_K")
+    if gate_weights.numel() != up_weights.numel():
+        raise ValueError("up and gate matrices differ in size")
+    dev = up_weights.device
+    outs = {"up": up, "gate": gate, "prod": prod}
+    for name in ("up", "gate", "prod"):
+        if outs[name] is None and name in want:
+            outs[name] = torch.empty(rows, dtype=torch.float32, device=dev)
+        if outs[name] is not None:
+            _need(outs[name], name, torch.float32)
+            if outs[name].numel() != rows:
+                raise ValueError(f"{name} has the wrong size")
+    _same_device(up_weights, gate_weights, activations, *outs.values())
+    ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
+    check(lib().mllb_q4k_gate_up(up_weights.data_ptr(), gate_weights.data_ptr(), activations.data_ptr(),
+                                 ptr(outs["up"]), ptr(outs["gate"]), ptr(outs["prod"]), rows, k,
+                                 _stream(up_weights)), "q4k_gate_up")
+    return outs["up"], outs["gate"], outs["prod"]
+
+
+def q4_k_q8_1_gate_order(weights: torch.Tensor, gate_weights: torch.Tensor, activations: torch.Tensor,
+                         output: torch.Tensor | None = None) -> torch.Tensor:
+    """The reference's fused entry: output = up * silu(gate), up weights first."""
+    return q4k_gate_up(weights, gate_weights, activations, prod=output, want=("prod",))[2]
+
+
+def q4k_subdots(weights: torch.Tensor, activations: torch.Tensor):
+    """Exact int32 sub-block dots [rows, k/32] and activation quant sums [k/32]."""
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(weights, F.q4k_row_bytes(k), "Q4_K")
+    dots = torch.empty(rows, k // 32, dtype=torch.int32, device=weights.device)
+    sums = torch.empty(k // 32, dtype=torch.int32, device=weights.device)
+    check(lib().mllb_q4k_subdots(weights.data_ptr(), activations.data_ptr(), dots.data_ptr(), sums.data_ptr(),
+                                 rows, k, _stream(weights)), "q4k_subdots")
+    return dots, sums
+
+
+# ------------------------------------------------------------------- Q6_K
+
+def q6_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
+                     output: torch.Tensor | None = None) -> torch.Tensor:
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(weights, F.q6k_row_bytes(k), "Q6_K")
+    if output is None:
+        output = torch.empty(rows, dtype=torch.float32, device=weights.device)
+    _need(output, "output", torch.float32)
+    if output.numel() != rows:
+        raise ValueError("output has the wrong size")
+    _same_device(weights, activations, output)
+    check(lib().mllb_q6k_matvec(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
+                                _stream(weights)), "q6_k_q8_1_matvec")
+    return output
+
+
+# ------------------------------------------------------------------- IMROPE
+
+def fused_q_imrope_runtime_fastpow(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tensor,
+                                   output: torch.Tensor, theta_scale: torch.Tensor) -> torch.Tensor:
+    """Reference pointer list: q[heads,128], gamma[128], positions int32[4], output, theta_scale fp32[1]."""
+    _need(q, "q", torch.float32)
+    _need(gamma, "gamma", torch.float32)
+    _need(positions, "positions", torch.int32)
+    _need(output, "output", torch.float32)
+    _need(theta_scale, "theta_scale", torch.float32)
+    if q.numel() == 0 or q.numel() % F.HEAD_DIM or gamma.numel() != F.HEAD_DIM or positions.numel() != 4 \
+            or output.numel() != q.numel() or theta_scale.numel() != 1:
+        raise ValueError("wrong reference shape")
+    _same_device(q, gamma, positions, output, theta_scale)
+    check(lib().mllb_rmsnorm_imrope_q(q.data_ptr(), gamma.data_ptr(), positions.data_ptr(), theta_scale.data_ptr(),
+                                      output.data_ptr(), q.numel() // F.HEAD_DIM, _stream(q)),
+          "fused_q_imrope_runtime_fastpow")
+    return output
+
+
+def rmsnorm_imrope_q(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tensor,
+                     theta_scale: torch.Tensor | float | None = None, out: torch.Tensor | None = None,
+                     heads_per_token: int | None = None) -> torch.Tensor:
+    """Batched form: q[tokens*heads_per_token, 128], positions int32[tokens, 4].
+
+    theta_scale: a device fp32[1] tensor (reference ABI), a Python float used
+    as the exact float64 scale, or None for pow(5e6, -2/128) in float64.
+    """
+    _need(q, "q", torch.float32)
+    _need(gamma, "gamma", torch.float32)
+    _need(positions, "positions", torch.int32)
+    if q.numel() == 0 or q.numel() % F.HEAD_DIM or gamma.numel() != F.HEAD_DIM or positions.numel() % 4:
+        raise ValueError("wrong reference shape")
+    heads = q.numel() // F.HEAD_DIM
+    tokens = positions.numel() // 4
+    if heads_per_token is None:
+        if heads % tokens:
+            raise ValueError("heads do not split evenly over the tokens")
+        heads_per_token = heads // tokens
+    if heads_per_token * tokens != heads:
+        raise ValueError("heads_per_token * tokens != heads")
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, "out", torch.float32)
+    ptr, value = None, F.IMROPE_FREQ_BASE ** (-2.0 / F.HEAD_DIM)
+    if isinstance(theta_scale, torch.Tensor):
+        _need(theta_scale, "theta_scale", torch.float32)
+        ptr = theta_scale.data_ptr()
+    elif theta_scale is not None:
+        value = float(theta_scale)
+    _same_device(q, gamma, positions, out)
+    check(lib().mllb_rmsnorm_imrope_q_batched(q.data_ptr(), gamma.data_ptr(), positions.data_ptr(), ptr, value,
+                                              out.data_ptr(), tokens, heads_per_token, _stream(q)),
+          "rmsnorm_imrope_q")
+    return out
+
+
+# ------------------------------------------------------------------- probe
+
+def stream_read(data: torch.Tensor, out: torch.Tensor | None = None, blocks: int = 0) -> torch.Tensor:
+    """XOR-stream `data` once with 16-byte loads (HBM read roofline)."""
+    _need(data, "data", torch.uint8)
+    if blocks <= 0:
+        blocks = torch.cuda.get_device_properties(data.device).multi_processor_count * 8
+    if out is None:
+        out = torch.empty(blocks * 256 * 16, dtype=torch.uint8, device=data.device)
+    check(lib().mllb_stream_read(data.data_ptr(), data.numel(), out.data_ptr(), blocks, _stream(data)),
+          "stream_read")
+    return out

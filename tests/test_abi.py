@@ -1,0 +1,55 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every symbol
+the public header declares, and rejects bad arguments before touching CUDA."""
+import ctypes as C
+
+import pytest
+
+from mojo_llm_lab_b200 import _lib, build
+
+
+def test_library_exports_every_declared_symbol():
+    names = _lib.declared_symbols()
+    assert len(names) >= 11
+    handle = _lib.lib()
+    for name in names:
+        assert hasattr(handle, name), name
+    assert set(names) == set(_lib.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_abi_version_and_error_string():
+    assert _lib.lib().mllb_abi_version() == 1
+    assert isinstance(_lib.lib().mllb_last_error(), bytes)
+
+
+@pytest.mark.parametrize("call", [
+    lambda L: L.mllb_q4k_matvec(None, None, None, 4096, 2560, None),
+    lambda L: L.mllb_q4k_gate_up(None, None, None, None, None, None, 1, 2560, None),
+    lambda L: L.mllb_q6k_matvec(None, None, None, 1, 2560, None),
+    lambda L: L.mllb_q8_1_quantize(None, None, 32, 0, None),
+    lambda L: L.mllb_rmsnorm_imrope_q(None, None, None, None, None, 32, None),
+    lambda L: L.mllb_q4k_subdots(None, None, None, None, 1, 256, None),
+    lambda L: L.mllb_stream_read(None, 16, None, 0, None),
+])
+def test_null_pointers_rejected_without_cuda(call):
+    assert call(_lib.lib()) == _lib.MLLB_EINVAL
+    assert b"null" in _lib.lib().mllb_last_error()
+
+
+def test_shape_and_alignment_rejections():
+    L = _lib.lib()
+    # K not a multiple of 256, zero rows, bad s_mode, misaligned weights
+    assert L.mllb_q4k_matvec(16, 16, 16, 4, 2500, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec(16, 16, 16, 0, 2560, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q8_1_quantize(16, 16, 31, 0, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q8_1_quantize(16, 16, 32, 7, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec(8, 16, 16, 4, 2560, None) == _lib.MLLB_EALIGN
+    assert L.mllb_q6k_matvec(8, 16, 16, 4, 2560, None) == _lib.MLLB_EALIGN
+    assert L.mllb_q4k_gate_up(16, 16, 16, None, None, None, 4, 2560, None) == _lib.MLLB_EINVAL
+
+
+def test_compat_cubin_built_for_sm100a():
+    data = build.CUBIN.read_bytes()
+    assert data[:4] == b"\x7fELF"
+    for entry in (b"fused_q_imrope_runtime_fastpow", b"q4_k_q8_1_matvec_dp4a_128", b"q4_k_q8_1_gate_order",
+                  b"q4_k_q8_1_matvec_dp4a", b"stream_read_roofline", b"q6_k_q8_1_matvec"):
+        assert entry in data
