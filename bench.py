@@ -37,12 +37,27 @@ L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
-    "q4k_matvec": dict(rows=4096, k=2560),
+    # the headline metric's configuration
+    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="q4k_stream_kernel<10,false>",
+                       profile="q4k_matvec_n4096_k2560"),
+    # fused gate/up, two 9728x2560 matrices, outputs up, gate, up*silu(gate)
+    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="q4k_stream_kernel<10,true>",
+                    profile="q4k_gate_up_n9728_k2560"),
+    # Q6_K vocabulary projection 151936x2560
+    "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="q6k_stream_kernel<10>",
+                      profile="q6k_vocab_n151936_k2560"),
 }
 
 
-def algorithmic_bytes(rows: int, k: int) -> int:
-    return rows * (k // 256) * 144 + k // 32 * 36 + rows * 4
+def weight_bytes(kind: str, rows: int, k: int) -> int:
+    per_row = k // 256 * (210 if kind == "q6k" else 144)
+    return rows * per_row * (2 if kind == "gate_up" else 1)
+
+
+def algorithmic_bytes(kind: str, rows: int, k: int) -> int:
+    """Bytes one launch must move: weights + Q8_1 activation + fp32 outputs."""
+    outputs = 3 if kind == "gate_up" else 1
+    return weight_bytes(kind, rows, k) + k // 32 * 36 + outputs * rows * 4
 
 
 def measured_peak():
@@ -116,27 +131,54 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(self.samples)}
 
 
+# ----------------------------------------------------------------------------- inputs
+
+def host_weights(kind: str, rows: int, k: int, seed: int):
+    from mojo_llm_lab_b200 import fixtures as fx
+    if kind == "q6k":
+        return [fx.seeded_q6k_matrix(rows, k, seed)]
+    if kind == "gate_up":
+        return [fx.seeded_q4k_matrix(rows, k, seed), fx.seeded_q4k_matrix(rows, k, seed + 1)]
+    return [fx.seeded_q4k_matrix(rows, k, seed)]
+
+
+def oracle_outputs(kind: str, ws, act: bytes, rows: int, k: int, threads: int = 0):
+    import oracle
+    if kind == "q6k":
+        return [oracle.q6k_matvec(ws[0], act, rows, k, threads)]
+    if kind == "gate_up":
+        return list(oracle.q4k_gate_up(ws[0], ws[1], act, rows, k, threads))
+    return [oracle.q4k_matvec(ws[0], act, rows, k, threads)]
+
+
 # ----------------------------------------------------------------------------- reference arm
 
-def cpu_reference(rows: int, k: int, target_s: float = 12.0):
-    """Time the oracle (CPU restatement of dot_q4_q8) with all host threads."""
+def cpu_reference(workload: str, target_s: float = 10.0):
+    """Time the oracle (CPU restatement of the reference's path) with all host threads
+    on a bounded sample: whole operations of the workload, repeated for ~target_s."""
     import oracle
     from mojo_llm_lab_b200 import fixtures as fx
 
+    wl = WORKLOADS[workload]
+    kind, rows, k = wl["kind"], wl["rows"], wl["k"]
     threads = os.cpu_count() or 1
-    w = fx.seeded_q4k_matrix(rows, k, seed=1)
-    a = oracle.quantize_q8_1(fx.seeded_activation(k, seed=2))
-    oracle.q4k_matvec(w, a, rows, k, threads)  # warm
+    ws = host_weights(kind, rows, k, seed=1)
+    act = oracle.quantize_q8_1(fx.seeded_activation(k, seed=2))
+    t0 = time.perf_counter()
+    oracle_outputs(kind, ws, act, rows, k, threads)  # warm
+    first = time.perf_counter() - t0
     reps, t0 = 0, time.perf_counter()
     while True:
-        oracle.q4k_matvec(w, a, rows, k, threads)
+        oracle.quantize_q8_1(fx.seeded_activation(k, seed=3 + reps))
+        oracle_outputs(kind, ws, act, rows, k, threads)
         reps += 1
         el = time.perf_counter() - t0
-        if el >= target_s or reps >= 10_000:
+        if el >= target_s or reps >= 10_000 or (first > target_s / 2):
             break
-    gbs = reps * algorithmic_bytes(rows, k) / el / 1e9
-    return {"value": gbs, "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{reps} matvecs of {rows}x{k} in {el:.1f} s (oracle/oracle.c, OpenMP, fsum per row)",
+    per_op = algorithmic_bytes(kind, rows, k)
+    return {"value": reps * per_op / el / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} x ({wl['kind']} {rows}x{k} incl. Q8_1 quantise) in {el:.1f} s "
+                      f"(oracle/oracle.c, OpenMP {threads} threads, fsum per row)",
             "seconds_per_op": el / reps}
 
 
@@ -144,15 +186,23 @@ def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
     wl = WORKLOADS[args.workload]
-    ref = cpu_reference(wl["rows"], wl["k"], target_s=max(3.0, 1.5 * args.steps))
-    line = {"metric": f"{args.workload} HBM GB/s", "value": ref["value"], "unit": "GB/s", "impl": "reference",
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+    ref = cpu_reference(args.workload, target_s=max(3.0, min(30.0, 1.5 * args.steps)))
+    line = {"metric": f"{describe(args.workload)} HBM GB/s", "value": round(ref["value"], 4), "unit": "GB/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ref["seconds_per_op"] * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8 dot / f64 sum", "data": "synthetic (seeded)",
-            "config": {"workload": f"Q4_K x Q8_1 matvec N={wl['rows']} K={wl['k']}"},
-            "cpu_baseline": {k: ref[k] for k in ("value", "unit", "cores", "kind", "sample")},
-            "e2e": {"value": ref["value"], "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+            "config": {"workload": describe(args.workload), "rows": wl["rows"], "k": wl["k"]},
+            "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(ref["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def describe(workload: str) -> str:
+    wl = WORKLOADS[workload]
+    return {"q4k": f"Q4_K x Q8_1 matvec N={wl['rows']} K={wl['k']}",
+            "gate_up": f"fused gate/up Q4_K x Q8_1 2x{wl['rows']}x{wl['k']} + SwiGLU",
+            "q6k": f"Q6_K x Q8_1 vocab matvec N={wl['rows']} K={wl['k']}"}[wl["kind"]]
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -168,41 +218,73 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     wl = WORKLOADS[args.workload]
-    rows, k = wl["rows"], wl["k"]
-    per_op = algorithmic_bytes(rows, k)
-    wbytes = rows * (k // 256) * 144
-    copies = args.copies or max(8, -(-int(2.2 * L2_BYTES) // wbytes))
+    kind, rows, k = wl["kind"], wl["rows"], wl["k"]
+    # q4k stays on one GPU: N ranks are replicas.  gate/up and the
+    # vocab projection are row-sharded with an all-gather of the outputs.
+    sharded = kind in ("gate_up", "q6k") and world > 1
+    if sharded and rows % world:
+        raise SystemExit(f"{rows} rows do not split over {world} ranks")
+    my_rows = rows // world if sharded else rows
+    n_out = 3 if kind == "gate_up" else 1
+    per_op = algorithmic_bytes(kind, rows, k)              # whole operation (all ranks' rows)
+    my_bytes = algorithmic_bytes(kind, my_rows, k)          # this rank's launch
+    wbytes = weight_bytes(kind, my_rows, k)
+    copies = args.copies or max(2, -(-int(2.2 * L2_BYTES) // wbytes))
+    pdl = not args.no_pdl
 
-    # Weights: one seeded matrix, copies made distinct per copy by re-seeding on device is
-    # unnecessary for timing; the copies are different buffers, which is what L2 sees.
-    w_host = fx.seeded_q4k_matrix(rows, k, seed=1)
-    w0 = torch.from_numpy(w_host).to(device)
-    weights = [w0] + [w0.clone() for _ in range(copies - 1)]
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    torch.cuda.set_stream(stream)
+
+    full = host_weights(kind, rows, k, seed=1)
+    row_bytes = weight_bytes(kind, 1, k) // (2 if kind == "gate_up" else 1)
+    lo = rank * my_rows if sharded else 0
+    mine = [torch.from_numpy(w[lo * row_bytes:(lo + my_rows) * row_bytes].copy()).to(device) for w in full]
+    weights = [mine] + [[w.clone() for w in mine] for _ in range(copies - 1)]
     xs_host = np.stack([fx.seeded_activation(k, seed=100 + i) for i in range(copies)])
     x_dev = torch.from_numpy(xs_host).to(device)
     acts = [ops.quantize_q8_1(x_dev[i]) for i in range(copies)]
-    outs = torch.empty(copies, rows, dtype=torch.float32, device=device)
-    stream = torch.cuda.current_stream(device)
+    outs = torch.empty(copies, n_out, my_rows, dtype=torch.float32, device=device)
+    gathered = torch.empty(copies, world, n_out, my_rows, dtype=torch.float32, device=device) if sharded else None
+
+    def launch(i: int):
+        w, o = weights[i], outs[i]
+        if kind == "q6k":
+            ops.q6_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+        elif kind == "gate_up":
+            ops.q4k_gate_up(w[0], w[1], acts[i], o[0], o[1], o[2], pdl=pdl)
+        else:
+            ops.q4_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+        if sharded:
+            dist.all_gather_into_tensor(gathered[i].view(-1), o.view(-1))
 
     def step():
         for i in range(copies):
-            ops.q4_k_q8_1_matvec(weights[i], acts[i], outs[i])
+            launch(i)
 
-    # Correctness gate before timing: first copy against the oracle (rank 0).
-    if rank == 0 and not args.skip_check:
+    # Correctness gate before timing (copy 0, rank 0's rows, against the oracle).
+    if not args.skip_check:
         import oracle
         step()
         torch.cuda.synchronize()
-        ref = oracle.q4k_matvec(w_host, acts[0].cpu().numpy(), rows, k)
+        ref = oracle_outputs(kind, [w[lo * row_bytes:(lo + my_rows) * row_bytes] for w in full],
+                             acts[0].cpu().numpy().tobytes(), my_rows, k)
         got = outs[0].cpu().numpy().astype(np.float64)
-        if not np.all(np.abs(got - ref) <= 1e-5 + 1e-5 * np.abs(ref)):
-            raise SystemExit("correctness gate failed: matvec differs from the oracle")
+        for j in range(n_out):
+            if not np.all(np.abs(got[j] - ref[j]) <= 1e-5 + 1e-5 * np.abs(ref[j])):
+                raise SystemExit(f"correctness gate failed on rank {rank}: output {j} differs from the oracle")
+        if sharded:
+            g = gathered[0].cpu().numpy()
+            if not np.array_equal(g[rank], outs[0].cpu().numpy()):
+                raise SystemExit("all-gather placed this rank's rows wrongly")
 
-    # Capture the step in a CUDA graph: launch overhead out of the device timing.
-    graph = torch.cuda.CUDAGraph()
+    # Capture the step in a CUDA graph: host launch overhead out of the device timing.
     for _ in range(2):
         step()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         step()
     for _ in range(args.warmup):
@@ -220,27 +302,55 @@ def run_ours(args, rank: int, world: int):
         stop.record(stream)
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop) / args.steps
+
+    # Kernel-only timing of the same launches (no collective) for the roofline.
+    if sharded:
+        kgraph = torch.cuda.CUDAGraph()
+        saved = sharded
+        with torch.cuda.graph(kgraph, stream=stream):
+            for i in range(copies):
+                w, o = weights[i], outs[i]
+                if kind == "q6k":
+                    ops.q6_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+                else:
+                    ops.q4k_gate_up(w[0], w[1], acts[i], o[0], o[1], o[2], pdl=pdl)
+        for _ in range(args.warmup):
+            kgraph.replay()
+        ks, ke = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ks.record(stream)
+        for _ in range(args.steps):
+            kgraph.replay()
+        ke.record(stream)
+        torch.cuda.synchronize()
+        kernel_ms = ks.elapsed_time(ke) / args.steps
+        del kgraph, saved
+    else:
+        kernel_ms = ms
     if world > 1:
-        t = torch.tensor([ms], device=device)
+        t = torch.tensor([ms, kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+        ms, kernel_ms = float(t[0].item()), float(t[1].item())
         dist.barrier()
     torch.cuda.synchronize()
-    launch_ms = ms / copies
-    achieved = per_op / (launch_ms * 1e-3) / 1e9
-    value = world * copies * per_op / (ms * 1e-3) / 1e9
+    launch_ms = kernel_ms / copies
+    achieved = my_bytes / (launch_ms * 1e-3) / 1e9
+    job_ops = copies * (1 if sharded else world)
+    value = job_ops * per_op / (ms * 1e-3) / 1e9
 
-    # e2e through the public API with host buffers.
+    # e2e through the public API with host buffers: every step copies its fp32
+    # activations from pinned host memory, quantises them on the device, runs
+    # the launches (and all-gathers) and copies the gathered outputs back.
     x_pin = torch.from_numpy(xs_host).pin_memory()
-    out_pin = torch.empty(copies, rows, dtype=torch.float32).pin_memory()
+    result = gathered if sharded else outs
+    out_pin = torch.empty(result.shape, dtype=torch.float32).pin_memory()
     x_stage = torch.empty(copies, k, dtype=torch.float32, device=device)
 
     def e2e_step():
         x_stage.copy_(x_pin, non_blocking=True)
         for i in range(copies):
             ops.quantize_q8_1(x_stage[i], acts[i])
-            ops.q4_k_q8_1_matvec(weights[i], acts[i], outs[i])
-        out_pin.copy_(outs, non_blocking=True)
+            launch(i)
+        out_pin.copy_(result, non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
@@ -258,34 +368,37 @@ def run_ours(args, rank: int, world: int):
         t = torch.tensor([e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
-    e2e_value = world * copies * per_op / (e_ms * 1e-3) / 1e9
+    e2e_value = job_ops * per_op / (e_ms * 1e-3) / 1e9
     derr = ops.device_error()
     if derr:
         raise SystemExit(f"device error word set: {derr:#x}")
+    del graph
+    if world > 1:
+        dist.barrier()
 
     if rank == 0:
         peak, peak_kind = measured_peak()
-        cpu = None if args.no_cpu_baseline else cpu_reference(rows, k, target_s=10.0)
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_reference(args.workload, target_s=10.0)
         clk = clocks.summary()
         line = {
-            "metric": "Q4_K x Q8_1 matvec HBM GB/s", "value": round(value, 2), "unit": "GB/s", "n_gpus": world,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "u8 weights / s8 dp4a / f64 accumulate",
-            "data": "synthetic (seeded BASELINE distributions)",
-            "config": {"workload": f"Q4_K x Q8_1 matvec N={rows} K={k}", "rows": rows, "k": k,
-                       "launches_per_step": copies, "weight_copies": copies,
-                       "bytes_per_launch": per_op, "l2": f"{copies} distinct weight copies "
-                       f"({copies * wbytes / 2**20:.0f} MiB) > 2x L2 per step; no flush",
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
-                       "us_per_op": round(launch_ms * 1e3, 4)},
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
-                    "h2d_bytes_per_step": copies * k * 4, "d2h_bytes_per_step": copies * rows * 4,
-                    "ms_per_step": round(e_ms, 6),
-                    "path": "ops.quantize_q8_1 + ops.q4_k_q8_1_matvec per launch (ctypes C-ABI), pinned H2D/D2H"},
+            "metric": f"{describe(args.workload)} HBM GB/s", "value": round(value, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6),
+            "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
+            "dtype": "u8/s8 dp4a, f64 accumulate", "data": "synthetic (seeded BASELINE distributions)",
+            "config": {"workload": describe(args.workload), "rows": rows, "k": k, "launches_per_step": copies,
+                       "bytes_per_op": per_op, "us_per_op": round(ms * 1e3 / copies, 4),
+                       "l2": f"{copies} distinct weight copies ({copies * wbytes / 2**20:.0f} MiB per GPU) "
+                             f"> 2x L2 per step; no flush",
+                       "parallelism": (f"rows/{world} per rank + NCCL all-gather" if sharded else
+                                       (f"replicas x{world}" if world > 1 else "single GPU")),
+                       "pdl": pdl},
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": copies * k * 4,
+                    "d2h_bytes_per_step": int(result.numel() * 4), "ms_per_step": round(e_ms, 6),
+                    "path": "ops.quantize_q8_1 + ops.<matvec> per launch (ctypes C-ABI), pinned H2D/D2H, eager"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
-                         "traffic": profiled_traffic("q4k_matvec_n4096_k2560"),
-                         "kernel": "q4k_stream_kernel<10,false>"},
+                         "traffic": profiled_traffic(wl["profile"]), "kernel": wl["kernel"],
+                         "us_per_launch": round(launch_ms * 1e3, 4)},
             "cpu_baseline": None if cpu is None else {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
             "clocks": clk,
             "gpu_launches": args.steps * copies,
@@ -301,6 +414,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="q4k_matvec")
     ap.add_argument("--copies", type=int, default=0)
+    ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
@@ -318,7 +432,8 @@ def main():
         import torch
         import torch.distributed as dist
         torch.cuda.set_device(int(os.environ.get("LOCAL_RANK", "0")))
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         try:
             run_ours(args, rank, world)
         finally:

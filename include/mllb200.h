@@ -39,6 +39,18 @@ extern "C" {
 #define MLLB_ECUDA (-3)        /* CUDA launch or runtime error (reference harness exit 20) */
 #define MLLB_EUNSUPPORTED (-4) /* shape outside what this build implements */
 
+/*
+ * Launch flags of the *_ex entry points.
+ * MLLB_LAUNCH_PDL: programmatic dependent launch.  The kernel may be scheduled
+ * while the preceding kernel in `stream` is still running and starts
+ * streaming its weight matrix at once; it waits for that kernel to complete
+ * before reading the activation or writing any output.  Only valid when the
+ * preceding kernels do not write the weight matrix (model weights are
+ * constant during decode).  Chains of such launches overlap each matvec's
+ * launch and DRAM latency with the previous one's tail.
+ */
+#define MLLB_LAUNCH_PDL 1u
+
 /* Q8_1 `s` field convention (the dot products never read s). */
 #define MLLB_Q8_1_S_D_SUMQ 0 /* s = fp16(fp16(d) * sum(q)): tools/generate_q4_matvec_fixtures.py:59 */
 #define MLLB_Q8_1_S_SUM_X 1  /* s = fp16(sum(x)): GGML quantize_q8_1 */
@@ -71,6 +83,9 @@ int mllb_q8_1_quantize(const float *x, void *q8, int64_t k, int s_mode, void *st
  * and benchmark/q4_compare.c:382,389-399 as (weights, activations, output).
  */
 int mllb_q4k_matvec(const void *weights, const void *q8, float *out, int64_t n, int64_t k, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL). */
+int mllb_q4k_matvec_ex(const void *weights, const void *q8, float *out, int64_t n, int64_t k, unsigned flags,
+                       void *stream);
 
 /*
  * Fused gate/up: up[r], gate[r] and prod[r] = up[r] * silu(gate[r]) with
@@ -82,6 +97,9 @@ int mllb_q4k_matvec(const void *weights, const void *q8, float *out, int64_t n, 
  */
 int mllb_q4k_gate_up(const void *up_weights, const void *gate_weights, const void *q8, float *up, float *gate,
                      float *prod, int64_t n, int64_t k, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL). */
+int mllb_q4k_gate_up_ex(const void *up_weights, const void *gate_weights, const void *q8, float *up, float *gate,
+                        float *prod, int64_t n, int64_t k, unsigned flags, void *stream);
 
 /*
  * Q6_K x Q8_1 matvec (vocabulary projection): out[r] for n rows, k columns.
@@ -89,6 +107,9 @@ int mllb_q4k_gate_up(const void *up_weights, const void *gate_weights, const voi
  * (docs/q6k-vocab-roofline.md:7-12); the reference has no kernel of its own.
  */
 int mllb_q6k_matvec(const void *weights, const void *q8, float *out, int64_t n, int64_t k, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL). */
+int mllb_q6k_matvec_ex(const void *weights, const void *q8, float *out, int64_t n, int64_t k, unsigned flags,
+                       void *stream);
 
 /*
  * Fused RMSNorm (eps 1e-6) * gamma[128] + IMROPE (sections 24/20/20/0,

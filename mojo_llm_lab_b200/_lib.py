@@ -21,6 +21,8 @@ MLLB_EALIGN = -2
 MLLB_ECUDA = -3
 MLLB_EUNSUPPORTED = -4
 
+LAUNCH_PDL = 1
+
 S_D_SUMQ = 0
 S_SUM_X = 1
 
@@ -33,6 +35,9 @@ SIGNATURES = {
     "mllb_device_error": (C.c_int, [C.POINTER(C.c_uint32), C.c_int]),
     "mllb_q8_1_quantize": (C.c_int, [_P, _P, _I64, C.c_int, _P]),
     "mllb_q4k_matvec": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
+    "mllb_q4k_matvec_ex": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q4k_gate_up_ex": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q6k_matvec_ex": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _I64, _P]),
     "mllb_q6k_matvec": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
     "mllb_rmsnorm_imrope_q": (C.c_int, [_P, _P, _P, _P, _P, _I64, _P]),

@@ -91,6 +91,33 @@ int stream_grid(Kernel kernel, int smem_bytes, int dev, int tiles, int* grid) {
   return MLLB_OK;
 }
 
+// Launch with an optional programmatic-stream-serialisation attribute (PDL).
+template <typename... Params, typename... Args>
+cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
+int launched(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MLLB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return check_launch(what);
+}
+
+bool known_flags(unsigned flags) { return (flags & ~static_cast<unsigned>(MLLB_LAUNCH_PDL)) == 0; }
+
 int check_rows(int64_t n, int64_t k, int64_t max_rows) {
   if (n <= 0 || n > max_rows) return fail(MLLB_EINVAL, "row count %lld out of range", static_cast<long long>(n));
   if (k <= 0 || k % 256) return fail(MLLB_EINVAL, "K=%lld is not a positive multiple of 256", static_cast<long long>(k));
@@ -100,48 +127,51 @@ int check_rows(int64_t n, int64_t k, int64_t max_rows) {
 
 template <int NB, bool DUAL>
 int launch_q4k_stream(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
-                      int n, cudaStream_t stream) {
+                      int n, cudaStream_t stream, bool pdl) {
   using Cfg = mllb::Q4kStreamConfig<NB, DUAL>;
   int dev, grid, rc;
   if ((rc = current_device(&dev))) return rc;
   auto kernel = mllb::q4k_stream_kernel<NB, DUAL>;
   const int tiles = (n + Cfg::G::kTileRows - 1) / Cfg::G::kTileRows;
   if ((rc = stream_grid(kernel, Cfg::kSmemBytes, dev, tiles, &grid))) return rc;
-  kernel<<<grid, mllb::kStreamThreads, Cfg::kSmemBytes, stream>>>(w0, w1, q8, o0, o1, o2, n);
-  return check_launch(DUAL ? "q4k gate/up stream kernel" : "q4k stream kernel");
+  return launched(launch(kernel, dim3(grid), dim3(mllb::kStreamThreads), Cfg::kSmemBytes, stream, pdl, w0, w1, q8,
+                         o0, o1, o2, n),
+                  DUAL ? "q4k gate/up stream kernel" : "q4k stream kernel");
 }
 
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
-                 int64_t n, int64_t k, cudaStream_t stream) {
+                 int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
   const int nb = static_cast<int>(k / 256);
   const bool dual = w1 != nullptr;
   const int rows = static_cast<int>(n);
   switch (nb) {
     case 8:
-      return dual ? launch_q4k_stream<8, true>(w0, w1, q8, o0, o1, o2, rows, stream)
-                  : launch_q4k_stream<8, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+      return dual ? launch_q4k_stream<8, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
+                  : launch_q4k_stream<8, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
     case 10:
-      return dual ? launch_q4k_stream<10, true>(w0, w1, q8, o0, o1, o2, rows, stream)
-                  : launch_q4k_stream<10, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+      return dual ? launch_q4k_stream<10, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
+                  : launch_q4k_stream<10, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
     case 16:
-      return dual ? launch_q4k_stream<16, true>(w0, w1, q8, o0, o1, o2, rows, stream)
-                  : launch_q4k_stream<16, false>(w0, w1, q8, o0, o1, o2, rows, stream);
+      return dual ? launch_q4k_stream<16, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
+                  : launch_q4k_stream<16, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
     default:
+      // The row kernel reads its weights only after the preceding kernel is
+      // done, so it never takes the PDL attribute.
       mllb::q4k_rowblock_kernel<<<rows, 128, 0, stream>>>(w0, w1, q8, o0, o1, o2, nb);
       return check_launch("q4k row kernel");
   }
 }
 
 template <int NB>
-int launch_q6k_stream(const uint8_t* w, const uint8_t* q8, float* out, int n, cudaStream_t stream) {
+int launch_q6k_stream(const uint8_t* w, const uint8_t* q8, float* out, int n, cudaStream_t stream, bool pdl) {
   using G = mllb::Q6kGeom<NB>;
   int dev, grid, rc;
   if ((rc = current_device(&dev))) return rc;
   auto kernel = mllb::q6k_stream_kernel<NB>;
   const int tiles = (n + G::kTileRows - 1) / G::kTileRows;
   if ((rc = stream_grid(kernel, G::kSmemBytes, dev, tiles, &grid))) return rc;
-  kernel<<<grid, mllb::kStreamThreads, G::kSmemBytes, stream>>>(w, q8, out, n);
-  return check_launch("q6k stream kernel");
+  return launched(launch(kernel, dim3(grid), dim3(mllb::kStreamThreads), G::kSmemBytes, stream, pdl, w, q8, out, n),
+                  "q6k stream kernel");
 }
 
 }  // namespace
@@ -178,18 +208,30 @@ int mllb_q8_1_quantize(const float* x, void* q8, int64_t k, int s_mode, void* st
 }
 
 int mllb_q4k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
+  return mllb_q4k_matvec_ex(weights, q8, out, n, k, 0u, stream);
+}
+
+int mllb_q4k_matvec_ex(const void* weights, const void* q8, float* out, int64_t n, int64_t k, unsigned flags,
+                       void* stream) {
   if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   int rc = check_rows(n, k, 1 << 30);
   if (rc) return rc;
   if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4))
     return fail(MLLB_EALIGN, "weights need 16-byte, q8/out 4-byte alignment");
   return q4k_dispatch(static_cast<const uint8_t*>(weights), nullptr, static_cast<const uint8_t*>(q8), out, nullptr,
-                      nullptr, n, k, static_cast<cudaStream_t>(stream));
+                      nullptr, n, k, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL);
 }
 
 int mllb_q4k_gate_up(const void* up_weights, const void* gate_weights, const void* q8, float* up, float* gate,
                      float* prod, int64_t n, int64_t k, void* stream) {
+  return mllb_q4k_gate_up_ex(up_weights, gate_weights, q8, up, gate, prod, n, k, 0u, stream);
+}
+
+int mllb_q4k_gate_up_ex(const void* up_weights, const void* gate_weights, const void* q8, float* up, float* gate,
+                        float* prod, int64_t n, int64_t k, unsigned flags, void* stream) {
   if (!up_weights || !gate_weights || !q8) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   if (!up && !gate && !prod) return fail(MLLB_EINVAL, "no output requested");
   int rc = check_rows(n, k, 1 << 30);
   if (rc) return rc;
@@ -197,11 +239,19 @@ int mllb_q4k_gate_up(const void* up_weights, const void* gate_weights, const voi
       !aligned(gate, 4) || !aligned(prod, 4))
     return fail(MLLB_EALIGN, "weights need 16-byte, q8/outputs 4-byte alignment");
   return q4k_dispatch(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
-                      static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream));
+                      static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
+                      flags & MLLB_LAUNCH_PDL);
 }
 
 int mllb_q6k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
+  return mllb_q6k_matvec_ex(weights, q8, out, n, k, 0u, stream);
+}
+
+int mllb_q6k_matvec_ex(const void* weights, const void* q8, float* out, int64_t n, int64_t k, unsigned flags,
+                       void* stream) {
   if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  const bool pdl = flags & MLLB_LAUNCH_PDL;
   int rc = check_rows(n, k, 1 << 30);
   if (rc) return rc;
   if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4))
@@ -216,9 +266,9 @@ int mllb_q6k_matvec(const void* weights, const void* q8, float* out, int64_t n, 
   const int64_t tail = n - main_rows;
   if (main_rows > 0) {
     switch (nb) {
-      case 8: rc = launch_q6k_stream<8>(w, a, out, static_cast<int>(main_rows), s); break;
-      case 10: rc = launch_q6k_stream<10>(w, a, out, static_cast<int>(main_rows), s); break;
-      case 16: rc = launch_q6k_stream<16>(w, a, out, static_cast<int>(main_rows), s); break;
+      case 8: rc = launch_q6k_stream<8>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
+      case 10: rc = launch_q6k_stream<10>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
+      case 16: rc = launch_q6k_stream<16>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
       default:
         mllb::q6k_rowblock_kernel<<<static_cast<int>(main_rows), 128, 0, s>>>(w, a, out, nb);
         rc = check_launch("q6k row kernel");

@@ -96,6 +96,16 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32
       : "memory");
 }
 
+// Programmatic dependent launch (PDL).  launch_dependents lets the next
+// kernel in the stream start its prologue (e.g. streaming constant weights)
+// while this one finishes; wait_prerequisite blocks until the preceding
+// kernel has completed and its writes are visible.  Both are no-ops when the
+// launches carry no programmatic-serialisation attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait_prerequisite() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
 // Named barrier over `threads` threads (id 0 is __syncthreads()).
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");

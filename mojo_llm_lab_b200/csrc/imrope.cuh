@@ -61,6 +61,8 @@ __global__ void __launch_bounds__(128) imrope_q_kernel(const float* __restrict__
                                                        float* __restrict__ out, int64_t heads,
                                                        int64_t heads_per_token) {
   const int lane = threadIdx.x & 31;
+  pdl_wait_prerequisite();
+  pdl_launch_dependents();
   const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t h = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); h < heads;

@@ -84,7 +84,7 @@ __device__ __forceinline__ void q4k_scale_min_pair(const uint4& hd, int j, uint3
 // Outputs (any may be null): out0 = first stream (up), out1 = second (gate),
 // out2 = up * silu(gate).
 template <int NB, bool DUAL>
-__global__ void __launch_bounds__(kStreamThreads, 1)
+__global__ void __launch_bounds__(kStreamThreads, 2)
     q4k_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1,
                       const uint8_t* __restrict__ q8, float* __restrict__ out0, float* __restrict__ out1,
                       float* __restrict__ out2, int n_rows) {
@@ -114,6 +114,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
 
   if (warp == kConsumerWarps) {
     // ------------------------------------------------------------ producer
@@ -151,6 +152,9 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
   }
 
   // -------------------------------------------------------------- consumers
+  // The activation is the only input a preceding kernel may have produced
+  // (weights are constant): wait for it here, not in the producer.
+  pdl_wait_prerequisite();
   {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(q8);
     uint32_t* dst = reinterpret_cast<uint32_t*>(act);

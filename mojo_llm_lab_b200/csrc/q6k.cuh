@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     fence_mbar_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
 
   if (warp == kConsumerWarps) {
     if (lane == 0) {
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1)
     return;
   }
 
+  pdl_wait_prerequisite();  // the activation may come from the preceding kernel
   {
     const uint32_t* src = reinterpret_cast<const uint32_t*>(q8);
     uint32_t* dst = reinterpret_cast<uint32_t*>(act);

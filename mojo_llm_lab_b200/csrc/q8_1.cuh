@@ -42,6 +42,8 @@ __device__ __forceinline__ int q8_1_quantize_lane(float x, int s_mode, uint32_t*
 __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ out,
                                                             int64_t blocks, int s_mode) {
   const int lane = threadIdx.x & 31;
+  pdl_wait_prerequisite();
+  pdl_launch_dependents();
   const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < blocks;
        g += warps) {

@@ -23,7 +23,7 @@ from __future__ import annotations
 import torch
 
 from . import formats as F
-from ._lib import S_D_SUMQ, S_SUM_X, check, device_error, lib  # noqa: F401
+from ._lib import LAUNCH_PDL, S_D_SUMQ, S_SUM_X, check, device_error, lib  # noqa: F401
 
 __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
@@ -88,7 +88,9 @@ def quantize_q8_1(x: torch.Tensor, out: torch.Tensor | None = None, s_mode: int 
 # ------------------------------------------------------------------- Q4_K
 
 def q4_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
-                     output: torch.Tensor | None = None) -> torch.Tensor:
+                     output: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """out = W @ a.  pdl=True: programmatic dependent launch (MLLB_LAUNCH_PDL) --
+    only when no preceding kernel in the stream writes `weights`."""
     _need(weights, "weights", torch.uint8)
     _need(activations, "activations", torch.uint8)
     k = _k_from_q8(activations)
@@ -99,14 +101,14 @@ def q4_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
     if output.numel() != rows:
         raise ValueError("output has the wrong size")
     _same_device(weights, activations, output)
-    check(lib().mllb_q4k_matvec(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
-                                _stream(weights)), "q4_k_q8_1_matvec")
+    check(lib().mllb_q4k_matvec_ex(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
+                                   LAUNCH_PDL if pdl else 0, _stream(weights)), "q4_k_q8_1_matvec")
     return output
 
 
 def q4k_gate_up(up_weights: torch.Tensor, gate_weights: torch.Tensor, activations: torch.Tensor,
                 up: torch.Tensor | None = None, gate: torch.Tensor | None = None,
-                prod: torch.Tensor | None = None, want=("up", "gate", "prod")):
+                prod: torch.Tensor | None = None, want=("up", "gate", "prod"), pdl: bool = False):
     """Fused gate/up: returns (up, gate, prod) with prod = up * silu(gate)."""
     _need(up_weights, "up_weights", torch.uint8)
     _need(gate_weights, "gate_weights", torch.uint8)
@@ -126,9 +128,9 @@ def q4k_gate_up(up_weights: torch.Tensor, gate_weights: torch.Tensor, activation
                 raise ValueError(f"{name} has the wrong size")
     _same_device(up_weights, gate_weights, activations, *outs.values())
     ptr = lambda t: t.data_ptr() if t is not None else None  # noqa: E731
-    check(lib().mllb_q4k_gate_up(up_weights.data_ptr(), gate_weights.data_ptr(), activations.data_ptr(),
-                                 ptr(outs["up"]), ptr(outs["gate"]), ptr(outs["prod"]), rows, k,
-                                 _stream(up_weights)), "q4k_gate_up")
+    check(lib().mllb_q4k_gate_up_ex(up_weights.data_ptr(), gate_weights.data_ptr(), activations.data_ptr(),
+                                    ptr(outs["up"]), ptr(outs["gate"]), ptr(outs["prod"]), rows, k,
+                                    LAUNCH_PDL if pdl else 0, _stream(up_weights)), "q4k_gate_up")
     return outs["up"], outs["gate"], outs["prod"]
 
 
@@ -154,7 +156,7 @@ def q4k_subdots(weights: torch.Tensor, activations: torch.Tensor):
 # ------------------------------------------------------------------- Q6_K
 
 def q6_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
-                     output: torch.Tensor | None = None) -> torch.Tensor:
+                     output: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
     _need(weights, "weights", torch.uint8)
     _need(activations, "activations", torch.uint8)
     k = _k_from_q8(activations)
@@ -165,8 +167,8 @@ def q6_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor,
     if output.numel() != rows:
         raise ValueError("output has the wrong size")
     _same_device(weights, activations, output)
-    check(lib().mllb_q6k_matvec(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
-                                _stream(weights)), "q6_k_q8_1_matvec")
+    check(lib().mllb_q6k_matvec_ex(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
+                                   LAUNCH_PDL if pdl else 0, _stream(weights)), "q6_k_q8_1_matvec")
     return output
 
 
