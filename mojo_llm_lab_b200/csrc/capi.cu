@@ -5,6 +5,7 @@
 // owns exactly one device error word.
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 
@@ -15,6 +16,41 @@
 #include "q4k.cuh"
 #include "q6k.cuh"
 #include "q8_1.cuh"
+#include "stream.cuh"
+
+// Streaming-kernel configurations: V (row groups per tile), S (stages),
+// TEAMS (consumer teams per CTA) per format, matrices and K/256.  Each can
+// be overridden at build time (-DMLLB_CFG_...) for tuning sweeps.
+#ifndef MLLB_CFG_Q4K_8
+#define MLLB_CFG_Q4K_8 8, 8, 6
+#endif
+#ifndef MLLB_CFG_Q4K_10
+#define MLLB_CFG_Q4K_10 4, 7, 2
+#endif
+#ifndef MLLB_CFG_Q4K_16
+#define MLLB_CFG_Q4K_16 8, 4, 3
+#endif
+#ifndef MLLB_CFG_Q4K_38
+#define MLLB_CFG_Q4K_38 4, 2, 1
+#endif
+#ifndef MLLB_CFG_Q4K_DUAL_8
+#define MLLB_CFG_Q4K_DUAL_8 8, 4, 4
+#endif
+#ifndef MLLB_CFG_Q4K_DUAL_10
+#define MLLB_CFG_Q4K_DUAL_10 8, 3, 3
+#endif
+#ifndef MLLB_CFG_Q4K_DUAL_16
+#define MLLB_CFG_Q4K_DUAL_16 4, 4, 2
+#endif
+#ifndef MLLB_CFG_Q6K_8
+#define MLLB_CFG_Q6K_8 4, 8, 6
+#endif
+#ifndef MLLB_CFG_Q6K_10
+#define MLLB_CFG_Q6K_10 8, 5, 4
+#endif
+#ifndef MLLB_CFG_Q6K_16
+#define MLLB_CFG_Q6K_16 4, 6, 3
+#endif
 
 namespace {
 
@@ -34,6 +70,33 @@ int check_launch(const char* what) {
   g_error[0] = '\0';
   return MLLB_OK;
 }
+
+// Launch with an optional programmatic-stream-serialisation attribute (PDL).
+template <typename... Params, typename... Args>
+cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
+                   Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+}
+
+int launched(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return fail(MLLB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return check_launch(what);
+}
+
+bool known_flags(unsigned flags) { return (flags & ~static_cast<unsigned>(MLLB_LAUNCH_PDL)) == 0; }
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -69,7 +132,7 @@ int g_occupancy_used = 0;
 std::mutex g_occupancy_mutex;
 
 template <typename Kernel>
-int stream_grid(Kernel kernel, int smem_bytes, int dev, int tiles, int* grid) {
+int stream_grid(Kernel kernel, int smem_bytes, int threads, int dev, int tiles, int* grid, int* per_sm) {
   const void* fn = reinterpret_cast<const void*>(kernel);
   int blocks_per_sm = 0;
   {
@@ -80,7 +143,7 @@ int stream_grid(Kernel kernel, int smem_bytes, int dev, int tiles, int* grid) {
       cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
       if (e != cudaSuccess) return fail(MLLB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
       int occ = 0;
-      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, mllb::kStreamThreads, smem_bytes);
+      e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kernel, threads, smem_bytes);
       if (e != cudaSuccess) return fail(MLLB_ECUDA, "occupancy query: %s", cudaGetErrorString(e));
       blocks_per_sm = occ > 0 ? occ : 1;
       if (g_occupancy_used < kOccupancySlots) g_occupancy[g_occupancy_used++] = {fn, dev, blocks_per_sm};
@@ -88,35 +151,43 @@ int stream_grid(Kernel kernel, int smem_bytes, int dev, int tiles, int* grid) {
   }
   const int wave = sm_count(dev) * blocks_per_sm;
   *grid = tiles < wave ? tiles : wave;
+  *per_sm = blocks_per_sm;
   return MLLB_OK;
 }
 
-// Launch with an optional programmatic-stream-serialisation attribute (PDL).
-template <typename... Params, typename... Args>
-cudaError_t launch(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream, bool pdl,
-                   Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = pdl ? attr : nullptr;
-  cfg.numAttrs = pdl ? 1 : 0;
-  return cudaLaunchKernelEx(&cfg, kernel, static_cast<Params>(args)...);
+// Resident CTAs per SM a PDL launch may take: leaving room on every SM lets
+// the next kernel of a chain start streaming its weights before this one
+// ends.  Default: all but one of the CTAs that fit; tuning knob
+// MLLB_PDL_CTAS_PER_SM overrides it.
+// One persistent CTA per SM: every SM takes an equal share of the tiles, and
+// a second CTA slot stays free so that the next kernel of a stream can start
+// (and stream its weights) while this one finishes.  Tuning knob
+// MLLB_CTAS_PER_SM overrides the 1.
+int grid_cap(int dev, int grid, int per_sm) {
+  static const int env_cap = [] {
+    const char* env = getenv("MLLB_CTAS_PER_SM");
+    return env ? atoi(env) : 0;
+  }();
+  int ctas = env_cap > 0 ? env_cap : 1;
+  if (ctas > per_sm) ctas = per_sm;
+  const int cap = sm_count(dev) * ctas;
+  return grid < cap ? grid : cap;
 }
 
-int launched(cudaError_t e, const char* what) {
-  if (e != cudaSuccess) {
-    cudaGetLastError();
-    return fail(MLLB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
-  }
-  return check_launch(what);
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
+int launch_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2, int n,
+                cudaStream_t stream, bool pdl) {
+  using C = mllb::TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
+  int dev, grid, per_sm, rc;
+  if ((rc = current_device(&dev))) return rc;
+  auto kernel = mllb::team_stream_kernel<Fmt, NB, MATS, V, S, TEAMS>;
+  const int tiles = (n + C::kT - 1) / C::kT;
+  if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, tiles, &grid, &per_sm))) return rc;
+  grid = grid_cap(dev, grid, per_sm);
+  return launched(launch(kernel, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, pdl, w0, w1, q8, o0, o1, o2,
+                         n, pdl ? 1 : 0),
+                  "streaming matvec kernel");
 }
-
-bool known_flags(unsigned flags) { return (flags & ~static_cast<unsigned>(MLLB_LAUNCH_PDL)) == 0; }
 
 int check_rows(int64_t n, int64_t k, int64_t max_rows) {
   if (n <= 0 || n > max_rows) return fail(MLLB_EINVAL, "row count %lld out of range", static_cast<long long>(n));
@@ -125,56 +196,45 @@ int check_rows(int64_t n, int64_t k, int64_t max_rows) {
   return MLLB_OK;
 }
 
-template <int NB, bool DUAL>
-int launch_q4k_stream(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
-                      int n, cudaStream_t stream, bool pdl) {
-  using Cfg = mllb::Q4kStreamConfig<NB, DUAL>;
-  int dev, grid, rc;
-  if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::q4k_stream_kernel<NB, DUAL>;
-  const int tiles = (n + Cfg::G::kTileRows - 1) / Cfg::G::kTileRows;
-  if ((rc = stream_grid(kernel, Cfg::kSmemBytes, dev, tiles, &grid))) return rc;
-  return launched(launch(kernel, dim3(grid), dim3(mllb::kStreamThreads), Cfg::kSmemBytes, stream, pdl, w0, w1, q8,
-                         o0, o1, o2, n),
-                  DUAL ? "q4k gate/up stream kernel" : "q4k stream kernel");
-}
-
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
                  int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
+  using F = mllb::Q4kFormat;
   const int nb = static_cast<int>(k / 256);
-  const bool dual = w1 != nullptr;
   const int rows = static_cast<int>(n);
-  switch (nb) {
-    case 8:
-      return dual ? launch_q4k_stream<8, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
-                  : launch_q4k_stream<8, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-    case 10:
-      return dual ? launch_q4k_stream<10, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
-                  : launch_q4k_stream<10, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-    case 16:
-      return dual ? launch_q4k_stream<16, true>(w0, w1, q8, o0, o1, o2, rows, stream, pdl)
-                  : launch_q4k_stream<16, false>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-    default:
-      // The row kernel reads its weights only after the preceding kernel is
-      // done, so it never takes the PDL attribute.
-      mllb::q4k_rowblock_kernel<<<rows, 128, 0, stream>>>(w0, w1, q8, o0, o1, o2, nb);
-      return check_launch("q4k row kernel");
+  if (w1 == nullptr) {
+    switch (nb) {
+      case 8: return launch_team<F, 8, 1, MLLB_CFG_Q4K_8>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 10: return launch_team<F, 10, 1, MLLB_CFG_Q4K_10>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 16: return launch_team<F, 16, 1, MLLB_CFG_Q4K_16>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 38: return launch_team<F, 38, 1, MLLB_CFG_Q4K_38>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      default: break;
+    }
+  } else {
+    switch (nb) {
+      case 8: return launch_team<F, 8, 2, MLLB_CFG_Q4K_DUAL_8>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 10: return launch_team<F, 10, 2, MLLB_CFG_Q4K_DUAL_10>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 16: return launch_team<F, 16, 2, MLLB_CFG_Q4K_DUAL_16>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      default: break;
+    }
   }
-}
-
-template <int NB>
-int launch_q6k_stream(const uint8_t* w, const uint8_t* q8, float* out, int n, cudaStream_t stream, bool pdl) {
-  using G = mllb::Q6kGeom<NB>;
-  int dev, grid, rc;
-  if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::q6k_stream_kernel<NB>;
-  const int tiles = (n + G::kTileRows - 1) / G::kTileRows;
-  if ((rc = stream_grid(kernel, G::kSmemBytes, dev, tiles, &grid))) return rc;
-  return launched(launch(kernel, dim3(grid), dim3(mllb::kStreamThreads), G::kSmemBytes, stream, pdl, w, q8, out, n),
-                  "q6k stream kernel");
+  // The row kernel reads its weights only after the preceding kernel is done,
+  // so it never takes the PDL attribute.
+  mllb::q4k_rowblock_kernel<<<rows, 128, 0, stream>>>(w0, w1, q8, o0, o1, o2, nb);
+  return check_launch("q4k row kernel");
 }
 
 }  // namespace
+
+#ifdef MLLB_TRACE
+// Debug-build accessors of the timeline buffer (not part of the public ABI).
+extern "C" int mllb_trace_read(unsigned long long* out) {
+  return cudaMemcpyFromSymbol(out, g_mllb_trace, sizeof(g_mllb_trace)) == cudaSuccess ? MLLB_OK : MLLB_ECUDA;
+}
+extern "C" int mllb_trace_clear(void) {
+  static unsigned long long zeros[4096 * 8];
+  return cudaMemcpyToSymbol(g_mllb_trace, zeros, sizeof(zeros)) == cudaSuccess ? MLLB_OK : MLLB_ECUDA;
+}
+#endif
 
 extern "C" {
 
@@ -265,10 +325,12 @@ int mllb_q6k_matvec_ex(const void* weights, const void* q8, float* out, int64_t 
   const int64_t main_rows = n - n % 8;
   const int64_t tail = n - main_rows;
   if (main_rows > 0) {
+    using F = mllb::Q6kFormat;
+    const int mr = static_cast<int>(main_rows);
     switch (nb) {
-      case 8: rc = launch_q6k_stream<8>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
-      case 10: rc = launch_q6k_stream<10>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
-      case 16: rc = launch_q6k_stream<16>(w, a, out, static_cast<int>(main_rows), s, pdl); break;
+      case 8: rc = launch_team<F, 8, 1, MLLB_CFG_Q6K_8>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
+      case 10: rc = launch_team<F, 10, 1, MLLB_CFG_Q6K_10>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
+      case 16: rc = launch_team<F, 16, 1, MLLB_CFG_Q6K_16>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
       default:
         mllb::q6k_rowblock_kernel<<<static_cast<int>(main_rows), 128, 0, s>>>(w, a, out, nb);
         rc = check_launch("q6k row kernel");

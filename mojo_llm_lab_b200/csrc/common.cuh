@@ -142,6 +142,15 @@ __device__ __forceinline__ double half_bits_to_double(uint32_t bits16) {
   return static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(bits16 & 0xffffu))));
 }
 
+// int32 -> double, exact, on the fp64 pipe: the double with high word
+// 0x43300000 and low word (x ^ 2^31) is 2^52 + 2^31 + x; subtracting
+// 2^52 + 2^31 leaves x (every int32 is representable).  Avoids the
+// conversion unit, which the inner loops would otherwise saturate.
+__device__ __forceinline__ double i2d_exact(int x) {
+  return __hiloint2double(0x43300000, static_cast<int>(static_cast<uint32_t>(x) ^ 0x80000000u)) -
+         4503601774854144.0;
+}
+
 __device__ __forceinline__ double warp_sum_double(double v) {
 #pragma unroll
   for (int offset = 16; offset >= 1; offset >>= 1) v += __shfl_xor_sync(0xffffffffu, v, offset);
@@ -179,3 +188,20 @@ __device__ uint32_t g_mllb_device_error;
 namespace mllb {
 __device__ __forceinline__ void record_error(uint32_t bits) { atomicOr(&g_mllb_device_error, bits); }
 }  // namespace mllb
+
+// Timeline instrumentation, compiled in only with -DMLLB_TRACE (a debug
+// build): thread 0 of CTA b records %globaltimer at point p in
+// g_mllb_trace[b][p].  Points of the streaming kernels: 0 start, 1 after the
+// PDL wait, 2 activation staged, 3/5 first/second tile ready, 4/6 first/second
+// tile computed, 7 exit.
+#ifdef MLLB_TRACE
+__device__ unsigned long long g_mllb_trace[4096][8];
+#define MLLB_TRACE_POINT(p)                                                                  \
+  do {                                                                                       \
+    if (threadIdx.x == 0 && blockIdx.x < 4096) g_mllb_trace[blockIdx.x][p] = mllb::global_timer_ns(); \
+  } while (0)
+#else
+#define MLLB_TRACE_POINT(p) \
+  do {                      \
+  } while (0)
+#endif

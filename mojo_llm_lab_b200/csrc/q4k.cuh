@@ -28,6 +28,8 @@
 //   per-slot fp64 accumulator.  The row sum is therefore the exactly rounded
 //   value up to ~1e-16 relative, independent of reduction order, before the
 //   single final rounding to fp32.
+// The streaming (TMA) kernels are in stream.cuh; this file holds the block
+// decode helpers and the row-per-CTA kernels.
 #pragma once
 
 #include "common.cuh"
@@ -36,34 +38,11 @@ namespace mllb {
 
 constexpr int kQ4kBlockBytes = 144;
 constexpr int kQ8BlockBytes = 36;
-constexpr int kConsumerWarps = 8;
-constexpr int kStreamThreads = (kConsumerWarps + 1) * 32;
 
-template <int NB>
-struct Q4kGeom {
-  static constexpr int kRowBytes = NB * kQ4kBlockBytes;
-  static constexpr int kChunks = NB * 8;                                 // P
-  static constexpr int kRowsPerWarp = 32 / gcd_constexpr(kChunks, 32);   // RG
-  static constexpr int kSlots = kChunks * kRowsPerWarp / 32;
-  static constexpr int kTileRows = kConsumerWarps * kRowsPerWarp;
-  static constexpr int kActBytes = NB * 8 * kQ8BlockBytes;
-  static constexpr int kActBytesPadded = (kActBytes + 15) / 16 * 16;
-};
-
-template <int NB, bool DUAL>
-struct Q4kStreamConfig {
-  using G = Q4kGeom<NB>;
-  static constexpr int kStages = DUAL ? 2 : 4;
-  static constexpr int kStageBytes = G::kTileRows * G::kRowBytes * (DUAL ? 2 : 1);
-  static constexpr int kActOffset = kStages * kStageBytes;
-  static constexpr int kBarOffset = kActOffset + G::kActBytesPadded;
-  static constexpr int kSmemBytes = kBarOffset + 2 * kStages * 8;
-};
-
-// Scale and min of group (2j + h) of a block from the packed 12-byte field
-// (header words y, z, w = bytes 4..15).  Groups 0-3 keep 6 bits in bytes
-// 0-3 / 4-7; groups 4-7 combine a nibble of bytes 8-11 with the top two bits
-// of bytes 0-7 (tests/q4_reference.py:57-62).
+// Scale and min of groups 2j and 2j+1 (bytes 0 and 1 of *sc2 / *mn2) from
+// the packed 12-byte field (header words y, z, w = bytes 4..15).  Groups 0-3
+// keep 6 bits in bytes 0-3 / 4-7; groups 4-7 combine a nibble of bytes 8-11
+// with the top two bits of bytes 0-7 (tests/q4_reference.py:57-62).
 __device__ __forceinline__ void q4k_scale_min_pair(const uint4& hd, int j, uint32_t* sc2, uint32_t* mn2) {
   const int shift = (j & 1) * 16;
   const uint32_t a = (hd.y >> shift) & 0xffffu;
@@ -78,187 +57,44 @@ __device__ __forceinline__ void q4k_scale_min_pair(const uint4& hd, int j, uint3
   }
 }
 
-// ----------------------------------------------------------------------------
-// Persistent TMA-pipelined kernel.  DUAL: two weight streams (up, gate) over
-// the same activation, SwiGLU epilogue.
-// Outputs (any may be null): out0 = first stream (up), out1 = second (gate),
-// out2 = up * silu(gate).
-template <int NB, bool DUAL>
-__global__ void __launch_bounds__(kStreamThreads, 2)
-    q4k_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1,
-                      const uint8_t* __restrict__ q8, float* __restrict__ out0, float* __restrict__ out1,
-                      float* __restrict__ out2, int n_rows) {
-  using G = Q4kGeom<NB>;
-  using Cfg = Q4kStreamConfig<NB, DUAL>;
-  constexpr int S = Cfg::kStages;
-  constexpr int SLOTS = G::kSlots;
-  constexpr int RG = G::kRowsPerWarp;
-  constexpr int TILE = G::kTileRows;
-  constexpr int ROWB = G::kRowBytes;
-  constexpr int P = G::kChunks;
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* act = smem + Cfg::kActOffset;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::kBarOffset);
-  uint64_t* empty = full + S;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int ntiles = (n_rows + TILE - 1) / TILE;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      int k = 0;
-      bool ok = true;
-      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
-        const int s = k % S;
-        if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1)) {
-          record_error(kErrEmptyWaitTimeout);
-          ok = false;
-          break;
-        }
-        const int rows = min(TILE, n_rows - tile * TILE);
-        const uint32_t bytes = static_cast<uint32_t>(rows * ROWB);
-        uint8_t* stage = smem + s * Cfg::kStageBytes;
-        const size_t goff = static_cast<size_t>(tile) * TILE * ROWB;
-        mbar_arrive_expect_tx(&full[s], DUAL ? 2 * bytes : bytes);
-        bulk_copy_g2s(stage, w0 + goff, bytes, &full[s], policy);
-        if (DUAL) bulk_copy_g2s(stage + TILE * ROWB, w1 + goff, bytes, &full[s], policy);
-      }
-      // Never leave the CTA with copies in flight: wait for the last fill of
-      // every stage (already complete in the normal path).
-      const int issued = k;
-      for (int u = issued - 1; u >= 0 && u >= issued - S; --u) {
-        if (!mbar_wait_bounded(&full[u % S], (u / S) & 1)) {
-          record_error(kErrDrainTimeout);
-          break;
-        }
-      }
-      (void)ok;
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
-  // The activation is the only input a preceding kernel may have produced
-  // (weights are constant): wait for it here, not in the producer.
-  pdl_wait_prerequisite();
-  {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(q8);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(act);
-    for (int i = threadIdx.x; i < G::kActBytes / 4; i += kConsumerWarps * 32) dst[i] = __ldg(src + i);
-  }
-  named_barrier(1, kConsumerWarps * 32);
-
-  const int h = lane & 1;  // which 16-byte half of the 32-weight groups
-  uint32_t a_lo[SLOTS][4], a_hi[SLOTS][4];
-  double delta[SLOTS];
-  int asum[SLOTS];
-  int slot_row[SLOTS], slot_j[SLOTS], slot_block[SLOTS], slot_chunk[SLOTS];
+// Re-lay K/32 Q8_1 blocks at `q8` (global) into shared memory for the
+// streaming kernels: int8 quants of group G at [32G, 32G+32) (16-byte
+// aligned), then GROUPS fp64 deltas, then GROUPS int32 quant sums.  One
+// thread per group.
+template <int GROUPS>
+__device__ __forceinline__ void stage_q8_1(const uint8_t* __restrict__ q8, uint8_t* act, int tid, int nthreads) {
+  for (int g = tid; g < GROUPS; g += nthreads) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(q8 + g * kQ8BlockBytes);
+    uint32_t w[9];
 #pragma unroll
-  for (int i = 0; i < SLOTS; ++i) {
-    const int vp = lane + 32 * i;
-    const int p = vp % P;
-    const int b = p >> 3, s = p & 7, j = s >> 1;
-    slot_row[i] = vp / P;
-    slot_j[i] = j;
-    slot_block[i] = b;
-    slot_chunk[i] = s;
-    const uint8_t* glo = act + (b * 8 + 2 * j) * kQ8BlockBytes;
-    const uint8_t* ghi = glo + kQ8BlockBytes;
-    const uint8_t* gme = act + (b * 8 + s) * kQ8BlockBytes;
-#pragma unroll
-    for (int t = 0; t < 4; ++t) {
-      a_lo[i][t] = lds32(glo + 4 + 16 * h + 4 * t);
-      a_hi[i][t] = lds32(ghi + 4 + 16 * h + 4 * t);
-    }
+    for (int t = 0; t < 9; ++t) w[t] = __ldg(src + t);
     int sum = 0;
 #pragma unroll
-    for (int t = 0; t < 8; ++t) sum = byte_sum_s8(lds32(gme + 4 + 4 * t), sum);
-    asum[i] = sum;
-    delta[i] = half_bits_to_double(lds32(gme) & 0xffffu);
+    for (int t = 1; t < 9; ++t) sum = byte_sum_s8(w[t], sum);
+    uint4* qdst = reinterpret_cast<uint4*>(act + g * 32);
+    qdst[0] = make_uint4(w[1], w[2], w[3], w[4]);
+    qdst[1] = make_uint4(w[5], w[6], w[7], w[8]);
+    reinterpret_cast<double*>(act + GROUPS * 32)[g] = half_bits_to_double(w[0] & 0xffffu);
+    reinterpret_cast<int*>(act + GROUPS * 40)[g] = sum;
   }
+}
 
-  int k = 0;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
-    const int s = k % S;
-    if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
-      record_error(kErrFullWaitTimeout);
-      break;
-    }
-    const uint8_t* stage = smem + s * Cfg::kStageBytes;
-    double acc0[SLOTS], acc1[SLOTS];
-#pragma unroll
-    for (int i = 0; i < SLOTS; ++i) {
-      const uint8_t* rowp = stage + (warp * RG + slot_row[i]) * ROWB + slot_block[i] * kQ4kBlockBytes;
-#pragma unroll
-      for (int m = 0; m < (DUAL ? 2 : 1); ++m) {
-        const uint8_t* bp = rowp + m * TILE * ROWB;
-        const uint4 hd = lds128(bp);
-        const uint4 wq = lds128(bp + 16 + 16 * slot_chunk[i]);
-        int dlo = 0, dhi = 0;
-        dlo = dp4a_ss(wq.x & 0x0f0f0f0fu, a_lo[i][0], dlo);
-        dhi = dp4a_ss((wq.x >> 4) & 0x0f0f0f0fu, a_hi[i][0], dhi);
-        dlo = dp4a_ss(wq.y & 0x0f0f0f0fu, a_lo[i][1], dlo);
-        dhi = dp4a_ss((wq.y >> 4) & 0x0f0f0f0fu, a_hi[i][1], dhi);
-        dlo = dp4a_ss(wq.z & 0x0f0f0f0fu, a_lo[i][2], dlo);
-        dhi = dp4a_ss((wq.z >> 4) & 0x0f0f0f0fu, a_hi[i][2], dhi);
-        dlo = dp4a_ss(wq.w & 0x0f0f0f0fu, a_lo[i][3], dlo);
-        dhi = dp4a_ss((wq.w >> 4) & 0x0f0f0f0fu, a_hi[i][3], dhi);
-        // Lane h keeps group 2j+h; its partner holds the other 16 weights.
-        const int mine = h ? dhi : dlo;
-        const int send = h ? dlo : dhi;
-        const int dot = mine + __shfl_xor_sync(0xffffffffu, send, 1);
-        uint32_t sc2, mn2;
-        q4k_scale_min_pair(hd, slot_j[i], &sc2, &mn2);
-        const int sc = static_cast<int>((sc2 >> (8 * h)) & 0xffu);
-        const int mn = static_cast<int>((mn2 >> (8 * h)) & 0xffu);
-        const double d = half_bits_to_double(hd.x);
-        const double dmin = half_bits_to_double(hd.x >> 16);
-        const double term = fma(d, static_cast<double>(sc * dot), -dmin * static_cast<double>(mn * asum[i]));
-        if (m == 0)
-          acc0[i] = delta[i] * term;
-        else
-          acc1[i] = delta[i] * term;
-      }
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      double v0 = 0.0, v1 = 0.0;
-#pragma unroll
-      for (int i = 0; i < SLOTS; ++i) {
-        if (slot_row[i] == r) {
-          v0 += acc0[i];
-          if (DUAL) v1 += acc1[i];
-        }
-      }
-      v0 = warp_sum_double(v0);
-      if (DUAL) v1 = warp_sum_double(v1);
-      const int row = tile * TILE + warp * RG + r;
-      if (lane == 0 && row < n_rows) {
-        if (out0) out0[row] = static_cast<float>(v0);
-        if (DUAL) {
-          if (out1) out1[row] = static_cast<float>(v1);
-          if (out2) out2[row] = static_cast<float>(v0 * (v1 / (1.0 + exp(-v1))));
-        }
-      }
-    }
-  }
+// Decode one 144-byte super-block header (raw, in shared memory) into
+//   [0,8) fp64 d   [8,16) fp64 dmin   [16,32) (scale, min) byte pairs of groups 0..7
+// Groups 0-3 keep their 6 bits in packed bytes 0-3 / 4-7; groups 4-7 take a
+// nibble of bytes 8-11 and the top two bits of bytes 0-3 / 4-7
+// (tests/q4_reference.py:57-62).
+__device__ __forceinline__ void q4k_decode_header(const uint8_t* raw, uint8_t* dst) {
+  const uint4 hd = lds128(raw);
+  const uint32_t lo_sc = hd.y & 0x3f3f3f3fu;
+  const uint32_t lo_mn = hd.z & 0x3f3f3f3fu;
+  const uint32_t hi_sc = (hd.w & 0x0f0f0f0fu) | ((hd.y >> 2) & 0x30303030u);
+  const uint32_t hi_mn = ((hd.w >> 4) & 0x0f0f0f0fu) | ((hd.z >> 2) & 0x30303030u);
+  double2* f = reinterpret_cast<double2*>(dst);
+  *f = make_double2(half_bits_to_double(hd.x), half_bits_to_double(hd.x >> 16));
+  *reinterpret_cast<uint4*>(dst + 16) =
+      make_uint4(__byte_perm(lo_sc, lo_mn, 0x5140), __byte_perm(lo_sc, lo_mn, 0x7362),
+                 __byte_perm(hi_sc, hi_mn, 0x5140), __byte_perm(hi_sc, hi_mn, 0x7362));
 }
 
 // ----------------------------------------------------------------------------

@@ -29,22 +29,6 @@ namespace mllb {
 
 constexpr int kQ6kBlockBytes = 210;
 
-template <int NB>
-struct Q6kGeom {
-  static constexpr int kRowBytes = NB * kQ6kBlockBytes;
-  static constexpr int kUnits = NB * 8;  // 32-weight units per row
-  static constexpr int kRowsPerWarp = 32 / gcd_constexpr(kUnits, 32);
-  static constexpr int kSlots = kUnits * kRowsPerWarp / 32;
-  static constexpr int kTileRows = kConsumerWarps * kRowsPerWarp;  // multiple of 8 -> 16-byte tiles
-  static constexpr int kActBytes = NB * 8 * kQ8BlockBytes;
-  static constexpr int kActBytesPadded = (kActBytes + 15) / 16 * 16;
-  static constexpr int kStages = 3;
-  static constexpr int kStageBytes = kTileRows * kRowBytes;
-  static constexpr int kActOffset = kStages * kStageBytes;
-  static constexpr int kBarOffset = kActOffset + kActBytesPadded;
-  static constexpr int kSmemBytes = kBarOffset + 2 * kStages * 8;
-};
-
 // Two words from an 8-byte field that starts 0 or 2 bytes past a word
 // boundary (sh = 0 or 16 bits).
 __device__ __forceinline__ void load_field8(const uint8_t* p, uint32_t sh, uint32_t* x0, uint32_t* x1) {
@@ -73,135 +57,6 @@ __device__ __forceinline__ void q6k_unit_ints(const uint8_t* blk, int h, int l0,
   t[1] = static_cast<int>(sc[2]) * dp4a_us(q11, a[1][1], dp4a_us(q10, a[1][0], c[1]));
   t[2] = static_cast<int>(sc[4]) * dp4a_us(q21, a[2][1], dp4a_us(q20, a[2][0], c[2]));
   t[3] = static_cast<int>(sc[6]) * dp4a_us(q31, a[3][1], dp4a_us(q30, a[3][0], c[3]));
-}
-
-template <int NB>
-__global__ void __launch_bounds__(kStreamThreads, 1)
-    q6k_stream_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8, float* __restrict__ out,
-                      int n_rows) {
-  using G = Q6kGeom<NB>;
-  constexpr int S = G::kStages;
-  constexpr int SLOTS = G::kSlots;
-  constexpr int RG = G::kRowsPerWarp;
-  constexpr int TILE = G::kTileRows;
-  constexpr int ROWB = G::kRowBytes;
-  constexpr int P = G::kUnits;
-
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* act = smem + G::kActOffset;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + G::kBarOffset);
-  uint64_t* empty = full + S;
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int ntiles = (n_rows + TILE - 1) / TILE;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < S; ++s) {
-      mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kConsumerWarps);
-    }
-    fence_mbar_init();
-  }
-  __syncthreads();
-  pdl_launch_dependents();
-
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      int k = 0;
-      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
-        const int s = k % S;
-        if (k >= S && !mbar_wait_bounded(&empty[s], ((k / S) - 1) & 1)) {
-          record_error(kErrEmptyWaitTimeout);
-          break;
-        }
-        const int rows = min(TILE, n_rows - tile * TILE);
-        const uint32_t bytes = static_cast<uint32_t>(rows * ROWB);
-        mbar_arrive_expect_tx(&full[s], bytes);
-        bulk_copy_g2s(smem + s * G::kStageBytes, w + static_cast<size_t>(tile) * TILE * ROWB, bytes, &full[s],
-                      policy);
-      }
-      const int issued = k;
-      for (int u = issued - 1; u >= 0 && u >= issued - S; --u) {
-        if (!mbar_wait_bounded(&full[u % S], (u / S) & 1)) {
-          record_error(kErrDrainTimeout);
-          break;
-        }
-      }
-    }
-    return;
-  }
-
-  pdl_wait_prerequisite();  // the activation may come from the preceding kernel
-  {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(q8);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(act);
-    for (int i = threadIdx.x; i < G::kActBytes / 4; i += kConsumerWarps * 32) dst[i] = __ldg(src + i);
-  }
-  named_barrier(1, kConsumerWarps * 32);
-
-  const int odd = lane & 1;
-  uint32_t a[SLOTS][4][2];
-  int c[SLOTS][4];
-  double da[SLOTS], db[SLOTS];
-  int slot_row[SLOTS], slot_block[SLOTS], slot_h[SLOTS], slot_l0[SLOTS];
-#pragma unroll
-  for (int i = 0; i < SLOTS; ++i) {
-    const int vp = lane + 32 * i;
-    const int p = vp % P;
-    const int b = p >> 3, u8 = p & 7;
-    const int h = u8 >> 2, l0 = ((u8 >> 1) & 1) * 16 + (u8 & 1) * 8;
-    slot_row[i] = vp / P;
-    slot_block[i] = b;
-    slot_h[i] = h;
-    slot_l0[i] = l0;
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint8_t* g = act + (b * 8 + 4 * h + kk) * kQ8BlockBytes + 4 + l0;
-      a[i][kk][0] = lds32(g);
-      a[i][kk][1] = lds32(g + 4);
-      c[i][kk] = -32 * byte_sum_s8(a[i][kk][1], byte_sum_s8(a[i][kk][0], 0));
-    }
-    const uint8_t* ga = act + (b * 8 + 4 * h + 2 * odd) * kQ8BlockBytes;
-    da[i] = half_bits_to_double(lds32(ga) & 0xffffu);
-    db[i] = half_bits_to_double(lds32(ga + kQ8BlockBytes) & 0xffffu);
-  }
-
-  int k = 0;
-  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++k) {
-    const int s = k % S;
-    if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
-      record_error(kErrFullWaitTimeout);
-      break;
-    }
-    const uint8_t* stage = smem + s * G::kStageBytes;
-    double acc[SLOTS];
-#pragma unroll
-    for (int i = 0; i < SLOTS; ++i) {
-      const uint8_t* blk = stage + (warp * RG + slot_row[i]) * ROWB + slot_block[i] * kQ6kBlockBytes;
-      int t[4];
-      q6k_unit_ints(blk, slot_h[i], slot_l0[i], a[i], c[i], t);
-      const int send0 = odd ? t[0] : t[2];
-      const int send1 = odd ? t[1] : t[3];
-      const int m0 = (odd ? t[2] : t[0]) + __shfl_xor_sync(0xffffffffu, send0, 1);
-      const int m1 = (odd ? t[3] : t[1]) + __shfl_xor_sync(0xffffffffu, send1, 1);
-      const double d = half_bits_to_double(*reinterpret_cast<const unsigned short*>(blk + 208));
-      acc[i] = d * fma(static_cast<double>(m0), da[i], static_cast<double>(m1) * db[i]);
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      double v = 0.0;
-#pragma unroll
-      for (int i = 0; i < SLOTS; ++i)
-        if (slot_row[i] == r) v += acc[i];
-      v = warp_sum_double(v);
-      const int row = tile * TILE + warp * RG + r;
-      if (lane == 0 && row < n_rows) out[row] = static_cast<float>(v);
-    }
-  }
 }
 
 // Row-per-CTA fallback for any K and any row count (plain global loads; the

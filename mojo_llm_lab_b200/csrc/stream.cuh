@@ -1,0 +1,403 @@
+// Persistent streaming matvec kernels of the decode hot path (sm_100a).
+//
+// One HBM pass over the weights, everything else on chip:
+//
+// * A CTA = one producer warp + a "team" of W consumer warps.  The producer's
+//   lane 0 streams tiles of T weight rows HBM -> shared memory with
+//   cp.async.bulk (the TMA bulk engine, L2 evict-first) through an S-stage ring
+//   guarded by mbarriers (full: bytes landed; ready: decoded; empty: consumed).
+//   All producer lanes then decode the tile's super-block headers (Q4_K 6-bit
+//   scales/mins and fp16 d/dmin -> fp64; Q6_K fp16 d -> fp64) into a side
+//   buffer, so the consumers never repeat that work per lane.
+// * Column-stationary lanes: a row is P = 8*NB units of 32 weights; the team
+//   covers RG = 32/gcd(P,32) rows x P units with exactly W = P*RG/32 warps, so
+//   every consumer lane owns ONE unit position (and row-in-group) for the
+//   whole kernel and keeps that position's Q8_1 activation in registers.  Per
+//   tile a lane computes V rows (its position in V row groups).
+// * Lanes 2c and 2c+1 hold two halves of the same sub-block; one shuffle joins
+//   their integer partial sums, after which each lane forms the fp64 terms of
+//   its share (every product exact: int32 sums times fp16-derived scales).
+// * Row totals: lane l visits its row groups in the order q ^ f(l), f(l) =
+//   (l >> 1) & (V-1), which makes the cross-lane transpose-reduction
+//   select-free (v[t] += shfl_xor(v[t + half], offset)); team partials meet in
+//   shared memory and one lane per row adds them in a fixed order.  The fp64
+//   row sum is therefore deterministic and exact up to ~1e-16 relative before
+//   the single rounding to fp32.
+// * Every mbarrier wait is bounded (~1 s, csrc/common.cuh).  A consumer warp
+//   that gives up still reaches the team barrier with an abort flag set, so no
+//   warp can be left waiting on a barrier.
+// * PDL: the loader streams the (constant) weights at once; the consumers wait
+//   for the preceding kernel only before reading the activation, and the CTA
+//   signals launch_dependents once that activation is staged, so the next
+//   kernel's prefetch cannot delay this kernel's activation read.
+#pragma once
+
+#include "common.cuh"
+#include "q4k.cuh"
+#include "q6k.cuh"
+
+namespace mllb {
+
+// ============================================================== formats
+
+// Q4_K: unit = 16 nibble bytes (halves h of groups 2j, 2j+1 of a super-block).
+struct Q4kFormat {
+  static constexpr int kBlockBytes = kQ4kBlockBytes;
+  static constexpr int kDecBytes = 32;  // per super-block: fp64 d, dmin, (scale,min) x 8
+
+  template <int NB>
+  struct ActLayout {  // shared-memory activation: quants, fp64 deltas, int sums
+    static constexpr int kGroups = NB * 8;
+    static constexpr int kBytes = (kGroups * (32 + 8 + 4) + 15) / 16 * 16;
+  };
+
+  struct Slot {
+    uint4 a_lo, a_hi;
+    double delta;
+    int asum;
+    int raw_off, dec_off;
+    int s;
+  };
+
+  template <int NB>
+  __device__ static void stage_activation(const uint8_t* q8, uint8_t* act, int tid, int nthreads) {
+    stage_q8_1<NB * 8>(q8, act, tid, nthreads);
+  }
+
+  template <int NB>
+  __device__ static Slot load_slot(const uint8_t* act, int p) {
+    constexpr int G = NB * 8;
+    Slot sl;
+    const int b = p >> 3, s = p & 7, j = s >> 1, h = s & 1;
+    sl.a_lo = *reinterpret_cast<const uint4*>(act + (b * 8 + 2 * j) * 32 + 16 * h);
+    sl.a_hi = *reinterpret_cast<const uint4*>(act + (b * 8 + 2 * j + 1) * 32 + 16 * h);
+    // High nibbles enter dp4a unshifted (16x): pre-scale delta and the sum.
+    sl.delta = reinterpret_cast<const double*>(act + G * 32)[b * 8 + s] * (h ? 0.0625 : 1.0);
+    sl.asum = reinterpret_cast<const int*>(act + G * 40)[b * 8 + s] << (4 * h);
+    sl.raw_off = b * kBlockBytes + 16 + 16 * s;
+    sl.dec_off = b * kDecBytes;
+    sl.s = s;
+    return sl;
+  }
+
+  __device__ static void decode(const uint8_t* raw_block, uint8_t* dec) { q4k_decode_header(raw_block, dec); }
+
+  // fp64 contribution of this lane's unit in one row.  Must be called by all
+  // 32 lanes (pair shuffle).
+  __device__ static double term(const uint8_t* row_raw, const uint8_t* row_dec, const Slot& sl) {
+    const uint4 wq = lds128(row_raw + sl.raw_off);
+    const double2 dd = *reinterpret_cast<const double2*>(row_dec + sl.dec_off);
+    const uint32_t scmn = *reinterpret_cast<const unsigned short*>(row_dec + sl.dec_off + 16 + 2 * sl.s);
+    int dlo = dp4a_us(wq.x & 0x0f0f0f0fu, sl.a_lo.x, 0);
+    int dhi = dp4a_us(wq.x & 0xf0f0f0f0u, sl.a_hi.x, 0);
+    dlo = dp4a_us(wq.y & 0x0f0f0f0fu, sl.a_lo.y, dlo);
+    dhi = dp4a_us(wq.y & 0xf0f0f0f0u, sl.a_hi.y, dhi);
+    dlo = dp4a_us(wq.z & 0x0f0f0f0fu, sl.a_lo.z, dlo);
+    dhi = dp4a_us(wq.z & 0xf0f0f0f0u, sl.a_hi.z, dhi);
+    dlo = dp4a_us(wq.w & 0x0f0f0f0fu, sl.a_lo.w, dlo);
+    dhi = dp4a_us(wq.w & 0xf0f0f0f0u, sl.a_hi.w, dhi);
+    const bool h = sl.s & 1;  // keep group 2j+h; the partner holds its other 16 weights
+    const int dot = (h ? dhi : dlo) + __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
+    const int sc = static_cast<int>(scmn & 0xffu), mn = static_cast<int>(scmn >> 8);
+    return sl.delta * fma(dd.x, i2d_exact(sc * dot), -dd.y * i2d_exact(mn * sl.asum));
+  }
+};
+
+// Q6_K: unit = 8 consecutive l of one (half, 16-column run): 32 weights in
+// four Q8_1 groups; lane pairs hold the two 8-column halves of a run.
+struct Q6kFormat {
+  static constexpr int kBlockBytes = kQ6kBlockBytes;
+  static constexpr int kDecBytes = 8;  // per super-block: fp64 d
+
+  template <int NB>
+  struct ActLayout {  // raw Q8_1 copy
+    static constexpr int kBytes = (NB * 8 * kQ8BlockBytes + 15) / 16 * 16;
+  };
+
+  struct Slot {
+    uint32_t a[4][2];
+    int c[4];
+    double da, db;
+    int blk_off, h, l0, odd;
+  };
+
+  template <int NB>
+  __device__ static void stage_activation(const uint8_t* q8, uint8_t* act, int tid, int nthreads) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(q8);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(act);
+    for (int i = tid; i < NB * 8 * kQ8BlockBytes / 4; i += nthreads) dst[i] = __ldg(src + i);
+  }
+
+  template <int NB>
+  __device__ static Slot load_slot(const uint8_t* act, int p) {
+    Slot sl;
+    const int b = p >> 3, u8 = p & 7;
+    sl.h = u8 >> 2;
+    sl.l0 = ((u8 >> 1) & 1) * 16 + (u8 & 1) * 8;
+    sl.odd = u8 & 1;
+    sl.blk_off = b * kBlockBytes;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const uint8_t* g = act + (b * 8 + 4 * sl.h + k) * kQ8BlockBytes + 4 + sl.l0;
+      sl.a[k][0] = lds32(g);
+      sl.a[k][1] = lds32(g + 4);
+      sl.c[k] = -32 * byte_sum_s8(sl.a[k][1], byte_sum_s8(sl.a[k][0], 0));
+    }
+    const uint8_t* ga = act + (b * 8 + 4 * sl.h + 2 * sl.odd) * kQ8BlockBytes;
+    sl.da = half_bits_to_double(lds32(ga) & 0xffffu);
+    sl.db = half_bits_to_double(lds32(ga + kQ8BlockBytes) & 0xffffu);
+    return sl;
+  }
+
+  __device__ static void decode(const uint8_t* raw_block, uint8_t* dec) {
+    *reinterpret_cast<double*>(dec) = half_bits_to_double(*reinterpret_cast<const unsigned short*>(raw_block + 208));
+  }
+
+  __device__ static double term(const uint8_t* row_raw, const uint8_t* row_dec, const Slot& sl) {
+    int t[4];
+    q6k_unit_ints(row_raw + sl.blk_off, sl.h, sl.l0, sl.a, sl.c, t);
+    // Even lanes finish groups 0,1 of the unit, odd lanes groups 2,3.
+    const int m0 = (sl.odd ? t[2] : t[0]) + __shfl_xor_sync(0xffffffffu, sl.odd ? t[0] : t[2], 1);
+    const int m1 = (sl.odd ? t[3] : t[1]) + __shfl_xor_sync(0xffffffffu, sl.odd ? t[1] : t[3], 1);
+    const double d = *reinterpret_cast<const double*>(row_dec + (sl.blk_off / kBlockBytes) * kDecBytes);
+    return d * fma(i2d_exact(m0), sl.da, i2d_exact(m1) * sl.db);
+  }
+};
+
+// ============================================================== geometry
+
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
+struct TeamConfig {
+  static constexpr int kP = NB * 8;                          // units per row
+  static constexpr int kRG = 32 / gcd_constexpr(kP, 32);     // rows per row group
+  static constexpr int kW = kP * kRG / 32;                   // consumer warps per team
+  static constexpr int kConsumers = TEAMS * kW * 32;
+  static constexpr int kThreads = kConsumers + 64;  // + loader warp + decoder warp
+  static constexpr int kT = V * kRG;                         // rows per tile
+  static constexpr int kRowBytes = NB * Fmt::kBlockBytes;
+  static constexpr int kTileBytes = kT * kRowBytes;          // per matrix
+  static constexpr int kStageBytes = kTileBytes * MATS;
+  static constexpr int kDecStage = MATS * kT * NB * Fmt::kDecBytes;
+  static constexpr int kSegs = 2 * kW;                       // half-warp partial segments
+  static constexpr int kTeamPartials = 2 * MATS * kT * kSegs;  // doubles, double-buffered
+  static constexpr int kDecOffset = S * kStageBytes;
+  static constexpr int kActOffset = kDecOffset + S * kDecStage;
+  static constexpr int kPartOffset = kActOffset + Fmt::template ActLayout<NB>::kBytes;
+  static constexpr int kBarOffset = kPartOffset + TEAMS * kTeamPartials * 8;
+  static constexpr int kAbortOffset = kBarOffset + (3 * S + 1) * 8;
+  static constexpr int kSmemBytes = kAbortOffset + 16;
+  // Two resident CTAs (this kernel + the next of a stream) when the ring is
+  // small enough; deep rings take the whole SM.
+  static constexpr int kMinBlocks = kSmemBytes <= 112 * 1024 ? 2 : 1;
+  static_assert(kStageBytes % 16 == 0 && kTileBytes % 16 == 0, "TMA tiles must be whole 16-byte runs");
+  static_assert(V == 4 || V == 8, "row groups per tile");
+  static_assert(kT <= 32, "one lane per row in the final combine");
+  static_assert(kThreads <= 1024 && TEAMS + 1 < 16, "CTA size / named barriers");
+  // A team waits on the ready barrier of tile k only after its previous tile
+  // k - TEAMS, so with TEAMS <= S the barrier is never more than one phase
+  // behind and the parity wait is unambiguous.  With TEAMS > S a wait could
+  // pass on a stale phase and corrupt the stage accounting.
+  static_assert(TEAMS <= S, "more consumer teams than pipeline stages");
+};
+
+// ============================================================== kernel
+// out0 = first matrix, out1 = second (DUAL), out2 = out0 * silu(out1) (DUAL).
+// Tile k of a CTA (global tile blockIdx.x + k*gridDim.x) goes to team k % TEAMS;
+// the teams of a CTA share one producer and stage ring, so an SM's teams take
+// their work from one queue.  pdl: launched with programmatic serialisation --
+// the producer streams every stage at once; otherwise it sends one stage, then
+// holds the rest until the activation is staged so that the activation read
+// does not queue behind a flood of weight requests.
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
+__global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThreads,
+                                  TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kMinBlocks)
+    team_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1,
+                       const uint8_t* __restrict__ q8, float* __restrict__ out0, float* __restrict__ out1,
+                       float* __restrict__ out2, int n_rows, int pdl) {
+  using C = TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
+  constexpr int W = C::kW, RG = C::kRG, T = C::kT, P = C::kP, ROWB = C::kRowBytes;
+  constexpr int DECB = Fmt::kDecBytes;
+
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* act = smem + C::kActOffset;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* ready = full + S;
+  uint64_t* empty = ready + S;
+  uint64_t* act_ready = empty + S;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + C::kAbortOffset);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int ntiles = (n_rows + T - 1) / T;
+  const int my_tiles = blockIdx.x < ntiles ? (ntiles - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&ready[s], 1);
+      mbar_init(&empty[s], W);
+    }
+    mbar_init(act_ready, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  {
+    double* partials = reinterpret_cast<double*>(smem + C::kPartOffset);
+    for (int i = threadIdx.x; i < TEAMS * C::kTeamPartials; i += blockDim.x) partials[i] = 0.0;
+  }
+  __syncthreads();
+  MLLB_TRACE_POINT(0);
+
+  if (warp == TEAMS * W) {
+    // ================================================= loader warp (lane 0)
+    // Prefetch (all stages under PDL, one otherwise), then hold further
+    // requests until the teams have their activation: the activation read
+    // must not queue behind weight traffic.  Only then may the next kernel of
+    // the stream start and send its own prefetch.
+    if (lane == 0) {
+      const uint64_t policy = l2_evict_first_policy();
+      auto issue = [&](int k) {
+        const int s = k % S;
+        const int tile = blockIdx.x + k * gridDim.x;
+        const int rows = min(T, n_rows - tile * T);
+        const uint32_t bytes = static_cast<uint32_t>(rows * ROWB);
+        const size_t goff = static_cast<size_t>(tile) * T * ROWB;
+        mbar_arrive_expect_tx(&full[s], MATS * bytes);
+        bulk_copy_g2s(smem + s * C::kStageBytes, w0 + goff, bytes, &full[s], policy);
+        if (MATS == 2) bulk_copy_g2s(smem + s * C::kStageBytes + C::kTileBytes, w1 + goff, bytes, &full[s], policy);
+      };
+      int k = 0;
+      const int first_batch = pdl ? S : 1;
+      for (; k < first_batch && k < my_tiles; ++k) issue(k);
+      bool ok = mbar_wait_bounded(act_ready, 0);
+      if (!ok) record_error(kErrEmptyWaitTimeout);
+      pdl_launch_dependents();
+      for (; ok && k < my_tiles; ++k) {
+        if (k >= S && !mbar_wait_bounded(&empty[k % S], ((k / S) - 1) & 1)) {
+          record_error(kErrEmptyWaitTimeout);
+          break;
+        }
+        issue(k);
+      }
+      // Never leave with copies in flight (normally all consumed already).
+      for (int u = k - 1; u >= 0 && u >= k - S; --u) {
+        if (!mbar_wait_bounded(&full[u % S], (u / S) & 1)) {
+          record_error(kErrDrainTimeout);
+          break;
+        }
+      }
+    }
+    return;
+  }
+  if (warp == TEAMS * W + 1) {
+    // ================================================= decoder warp
+    // Decodes each tile's super-block headers as soon as it lands, in order,
+    // independently of which team consumes it.
+    for (int k = 0; k < my_tiles; ++k) {
+      const int s = k % S;
+      if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
+        record_error(kErrFullWaitTimeout);
+        break;
+      }
+      const uint8_t* stage = smem + s * C::kStageBytes;
+      uint8_t* dec = smem + C::kDecOffset + s * C::kDecStage;
+      const int tile = blockIdx.x + k * gridDim.x;
+      const int rows = min(T, n_rows - tile * T);
+      for (int e = lane; e < MATS * T * NB; e += 32) {
+        const int m = e / (T * NB), rest = e % (T * NB), row = rest / NB, b = rest % NB;
+        if (row < rows) Fmt::decode(stage + m * C::kTileBytes + row * ROWB + b * Fmt::kBlockBytes, dec + e * DECB);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&ready[s]);
+    }
+    return;
+  }
+
+  // =================================================== consumer teams
+  const int team = warp / W;
+  const int twarp = warp % W;  // warp index inside the team
+  pdl_wait_prerequisite();     // the activation may come from the preceding kernel
+  MLLB_TRACE_POINT(1);
+  Fmt::template stage_activation<NB>(q8, act, threadIdx.x, C::kConsumers);
+  named_barrier(1, C::kConsumers);
+  if (threadIdx.x == 0) mbar_arrive(act_ready);
+  pdl_launch_dependents();  // with the loader's: the CTA triggers once staged
+  MLLB_TRACE_POINT(2);
+
+  const int vp = twarp * 32 + lane;
+  const int r_in_group = vp / P;
+  const typename Fmt::Slot slot = Fmt::template load_slot<NB>(act, vp % P);
+  const int f = (lane >> 1) & (V - 1);  // row-group visiting order
+  // Half-warps with the same row-in-group are combined before the partials.
+  const bool merge_halves = (twarp * 32) / P == (twarp * 32 + 16) / P;
+  const int seg = 2 * twarp + (merge_halves ? 0 : (lane >> 4));
+  // One lane per (row, segment) writes: bit 0 and the lane bits outside f(l)
+  // must be zero; bit 4 selects the half unless the halves were merged.
+  const bool writer = (lane & 1) == 0 && (lane & (0x0e & ~((V - 1) << 1))) == 0 && (!merge_halves || lane < 16);
+  double* partials = reinterpret_cast<double*>(smem + C::kPartOffset) + team * C::kTeamPartials;
+  const int team_barrier = 2 + team;
+
+  for (int k = team; k < my_tiles; k += TEAMS) {
+    const int s = k % S;
+    const int tile = blockIdx.x + k * gridDim.x;
+    const bool have = mbar_wait_bounded(&ready[s], (k / S) & 1);
+    if (!have) {
+      record_error(kErrFullWaitTimeout);
+      *abort_flag = 1;
+    }
+    if (k < 2) MLLB_TRACE_POINT(3 + 2 * k);
+    const int parity = (k / TEAMS) & 1;
+    double* part = partials + parity * (MATS * T * C::kSegs);
+    if (have) {
+      const uint8_t* stage = smem + s * C::kStageBytes;
+      const uint8_t* dec = smem + C::kDecOffset + s * C::kDecStage;
+      double v[MATS][V];
+#pragma unroll
+      for (int q = 0; q < V; ++q) {
+        const int row = (q ^ f) * RG + r_in_group;  // tile row visited at step q
+#pragma unroll
+        for (int m = 0; m < MATS; ++m)
+          v[m][q] = Fmt::term(stage + m * C::kTileBytes + row * ROWB, dec + (m * T + row) * NB * DECB, slot);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+      if (k < 2) MLLB_TRACE_POINT(4 + 2 * k);
+#pragma unroll
+      for (int m = 0; m < MATS; ++m) {
+        // select-free transpose reduction over lane bits log2(V)..1
+#pragma unroll
+        for (int half = V / 2, off = V; half >= 1; half >>= 1, off >>= 1)
+#pragma unroll
+          for (int t = 0; t < half; ++t) v[m][t] += __shfl_xor_sync(0xffffffffu, v[m][t + half], off);
+        double x = v[m][0];
+        x += __shfl_xor_sync(0xffffffffu, x, 1);
+        if (V == 4) x += __shfl_xor_sync(0xffffffffu, x, 8);
+        if (merge_halves) x += __shfl_xor_sync(0xffffffffu, x, 16);
+        if (writer) part[(m * T + f * RG + r_in_group) * C::kSegs + seg] = x;
+      }
+    }
+    named_barrier(team_barrier, W * 32);
+    if (*abort_flag) break;
+    if (twarp == 0 && lane < T) {
+      const int row = tile * T + lane;
+      double tot[MATS];
+#pragma unroll
+      for (int m = 0; m < MATS; ++m) {
+        double acc = 0.0;
+#pragma unroll
+        for (int g = 0; g < C::kSegs; ++g) acc += part[(m * T + lane) * C::kSegs + g];
+        tot[m] = acc;
+      }
+      if (row < n_rows) {
+        if (out0) out0[row] = static_cast<float>(tot[0]);
+        if (MATS == 2) {
+          if (out1) out1[row] = static_cast<float>(tot[MATS - 1]);
+          if (out2) out2[row] = static_cast<float>(tot[0] * (tot[MATS - 1] / (1.0 + exp(-tot[MATS - 1]))));
+        }
+      }
+    }
+  }
+  MLLB_TRACE_POINT(7);
+}
+
+}  // namespace mllb
