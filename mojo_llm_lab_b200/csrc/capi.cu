@@ -25,7 +25,7 @@
 #define MLLB_CFG_Q4K_8 8, 8, 6
 #endif
 #ifndef MLLB_CFG_Q4K_10
-#define MLLB_CFG_Q4K_10 4, 7, 2
+#define MLLB_CFG_Q4K_10 4, 6, 4
 #endif
 #ifndef MLLB_CFG_Q4K_16
 #define MLLB_CFG_Q4K_16 8, 4, 3
@@ -37,7 +37,7 @@
 #define MLLB_CFG_Q4K_DUAL_8 8, 4, 4
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_10
-#define MLLB_CFG_Q4K_DUAL_10 8, 3, 3
+#define MLLB_CFG_Q4K_DUAL_10 8, 3, 2
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_16
 #define MLLB_CFG_Q4K_DUAL_16 4, 4, 2
@@ -46,7 +46,7 @@
 #define MLLB_CFG_Q6K_8 4, 8, 6
 #endif
 #ifndef MLLB_CFG_Q6K_10
-#define MLLB_CFG_Q6K_10 8, 5, 4
+#define MLLB_CFG_Q6K_10 4, 8, 6
 #endif
 #ifndef MLLB_CFG_Q6K_16
 #define MLLB_CFG_Q6K_16 4, 6, 3

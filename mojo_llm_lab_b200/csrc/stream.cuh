@@ -2,13 +2,14 @@
 //
 // One HBM pass over the weights, everything else on chip:
 //
-// * A CTA = one producer warp + a "team" of W consumer warps.  The producer's
-//   lane 0 streams tiles of T weight rows HBM -> shared memory with
-//   cp.async.bulk (the TMA bulk engine, L2 evict-first) through an S-stage ring
-//   guarded by mbarriers (full: bytes landed; ready: decoded; empty: consumed).
-//   All producer lanes then decode the tile's super-block headers (Q4_K 6-bit
-//   scales/mins and fp16 d/dmin -> fp64; Q6_K fp16 d -> fp64) into a side
-//   buffer, so the consumers never repeat that work per lane.
+// * A CTA = a loader warp, a forwarder warp and TEAMS consumer teams of W
+//   warps.  The loader's lane 0 streams tiles of T weight rows HBM -> shared
+//   memory with cp.async.bulk (the TMA bulk engine, L2 evict-first) through an
+//   S-stage ring guarded by mbarriers (full: bytes landed; ready: re-signalled
+//   in tile order by the forwarder; empty: consumed).  Tile k goes to team
+//   k % TEAMS, which first decodes the tile's super-block headers once, one
+//   per lane (Q4_K 6-bit scales/mins and fp16 d/dmin -> fp64; Q6_K fp16 d ->
+//   fp64), so the lanes never repeat that work per unit.
 // * Column-stationary lanes: a row is P = 8*NB units of 32 weights; the team
 //   covers RG = 32/gcd(P,32) rows x P units with exactly W = P*RG/32 warps, so
 //   every consumer lane owns ONE unit position (and row-in-group) for the
@@ -177,11 +178,11 @@ struct TeamConfig {
   static constexpr int kRowBytes = NB * Fmt::kBlockBytes;
   static constexpr int kTileBytes = kT * kRowBytes;          // per matrix
   static constexpr int kStageBytes = kTileBytes * MATS;
-  static constexpr int kDecStage = MATS * kT * NB * Fmt::kDecBytes;
+  static constexpr int kDecTile = MATS * kT * NB * Fmt::kDecBytes;  // decoded headers of one tile
   static constexpr int kSegs = 2 * kW;                       // half-warp partial segments
   static constexpr int kTeamPartials = 2 * MATS * kT * kSegs;  // doubles, double-buffered
-  static constexpr int kDecOffset = S * kStageBytes;
-  static constexpr int kActOffset = kDecOffset + S * kDecStage;
+  static constexpr int kDecOffset = S * kStageBytes;                 // one decode buffer per team
+  static constexpr int kActOffset = kDecOffset + TEAMS * kDecTile;
   static constexpr int kPartOffset = kActOffset + Fmt::template ActLayout<NB>::kBytes;
   static constexpr int kBarOffset = kPartOffset + TEAMS * kTeamPartials * 8;
   static constexpr int kAbortOffset = kBarOffset + (3 * S + 1) * 8;
@@ -290,25 +291,22 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     return;
   }
   if (warp == TEAMS * W + 1) {
-    // ================================================= decoder warp
-    // Decodes each tile's super-block headers as soon as it lands, in order,
-    // independently of which team consumes it.
-    for (int k = 0; k < my_tiles; ++k) {
-      const int s = k % S;
-      if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
-        record_error(kErrFullWaitTimeout);
-        break;
+    // ================================================= forwarder warp
+    // Observes the tiles landing strictly in order and re-signals each on
+    // `ready`.  Teams wait on `ready`, never on `full` directly: a team's
+    // previous tile is k - TEAMS, which says nothing about whether tile k - S
+    // (the previous user of the stage) has landed, while the forwarder only
+    // waits for tile k after tile k - 1, so every parity wait here and in the
+    // teams is at most one phase ahead.
+    if (lane == 0) {
+      for (int k = 0; k < my_tiles; ++k) {
+        const int s = k % S;
+        if (!mbar_wait_bounded(&full[s], (k / S) & 1)) {
+          record_error(kErrFullWaitTimeout);
+          break;
+        }
+        mbar_arrive(&ready[s]);
       }
-      const uint8_t* stage = smem + s * C::kStageBytes;
-      uint8_t* dec = smem + C::kDecOffset + s * C::kDecStage;
-      const int tile = blockIdx.x + k * gridDim.x;
-      const int rows = min(T, n_rows - tile * T);
-      for (int e = lane; e < MATS * T * NB; e += 32) {
-        const int m = e / (T * NB), rest = e % (T * NB), row = rest / NB, b = rest % NB;
-        if (row < rows) Fmt::decode(stage + m * C::kTileBytes + row * ROWB + b * Fmt::kBlockBytes, dec + e * DECB);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&ready[s]);
     }
     return;
   }
@@ -335,6 +333,7 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
   // must be zero; bit 4 selects the half unless the halves were merged.
   const bool writer = (lane & 1) == 0 && (lane & (0x0e & ~((V - 1) << 1))) == 0 && (!merge_halves || lane < 16);
   double* partials = reinterpret_cast<double*>(smem + C::kPartOffset) + team * C::kTeamPartials;
+  uint8_t* dec = smem + C::kDecOffset + team * C::kDecTile;
   const int team_barrier = 2 + team;
 
   for (int k = team; k < my_tiles; k += TEAMS) {
@@ -348,9 +347,17 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     if (k < 2) MLLB_TRACE_POINT(3 + 2 * k);
     const int parity = (k / TEAMS) & 1;
     double* part = partials + parity * (MATS * T * C::kSegs);
+    const uint8_t* stage = smem + s * C::kStageBytes;
     if (have) {
-      const uint8_t* stage = smem + s * C::kStageBytes;
-      const uint8_t* dec = smem + C::kDecOffset + s * C::kDecStage;
+      // The team decodes this tile's super-block headers (about one per lane).
+      const int rows = min(T, n_rows - tile * T);
+      for (int e = vp; e < MATS * T * NB; e += W * 32) {
+        const int m = e / (T * NB), rest = e % (T * NB), row = rest / NB, b = rest % NB;
+        if (row < rows) Fmt::decode(stage + m * C::kTileBytes + row * ROWB + b * Fmt::kBlockBytes, dec + e * DECB);
+      }
+    }
+    named_barrier(team_barrier, W * 32);
+    if (have) {
       double v[MATS][V];
 #pragma unroll
       for (int q = 0; q < V; ++q) {
