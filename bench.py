@@ -38,13 +38,13 @@ FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
     # the headline metric's configuration
-    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="q4k_stream_kernel<10,false>",
+    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="team_stream_kernel<Q4kFormat,10,1,4,6,4>",
                        profile="q4k_matvec_n4096_k2560"),
     # fused gate/up, two 9728x2560 matrices, outputs up, gate, up*silu(gate)
-    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="q4k_stream_kernel<10,true>",
+    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,8,3,2>",
                     profile="q4k_gate_up_n9728_k2560"),
     # Q6_K vocabulary projection 151936x2560
-    "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="q6k_stream_kernel<10>",
+    "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,8,6>",
                       profile="q6k_vocab_n151936_k2560"),
 }
 
@@ -86,7 +86,10 @@ def profiled_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi samples during the timed region."""
+    """nvidia-smi clock / throttle-reason samples (every 100 ms) around the timed region.
+
+    Started under load shortly before the timed region and stopped right after
+    it (the recipe's `nvidia-smi ... -lms` line)."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -94,41 +97,45 @@ class ClockSampler:
 
     def __init__(self, index: int):
         self.index = index
-        self.samples = []
-        self._stop = threading.Event()
-        self._thread = None
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
-                                     timeout=5).stdout.strip()
-                if out:
-                    self.samples.append([c.strip() for c in out.split(",")])
-            except Exception:  # noqa: BLE001
-                pass
-            self._stop.wait(0.2)
+        self.proc = None
+        self.lines = []
 
     def __enter__(self):
-        self._thread = threading.Thread(target=self._run, daemon=True)
-        self._thread.start()
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self._stop.set()
-        if self._thread:
-            self._thread.join(timeout=10)
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=10)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
 
     def summary(self):
-        if not self.samples:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
-        smax = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        samples = [[c.strip() for c in ln.split(",")] for ln in self.lines]
+        samples = [s for s in samples if len(s) >= 9]
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [v for v in (num(s[1]) for s in samples) if v is not None]
+        smax = [v for v in (num(s[2]) for s in samples) if v is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for s in self.samples for i in range(4) if len(s) > 5 + i and s[5 + i] == "Active"})
+        reasons = sorted({names[i] for s in samples for i in range(4) if s[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(self.samples)}
+                "reasons": reasons, "samples": len(samples)}
 
 
 # ----------------------------------------------------------------------------- inputs
@@ -295,7 +302,25 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize()
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # ~0.5 s of the same load before the timed region (untimed) so that the
+    # clock samples describe it; every rank replays the same number of times
+    # (the graph may hold collectives).
+    t0 = time.perf_counter()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    n_load = max(1, int(0.5 / max((time.perf_counter() - t0) / 3, 1e-6)))
+    if world > 1:
+        t = torch.tensor([n_load], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        n_load = int(t.item())
     with ClockSampler(local) as clocks:
+        for _ in range(n_load):
+            graph.replay()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
