@@ -243,10 +243,12 @@ def run_ours(args, rank: int, world: int):
     stream.wait_stream(torch.cuda.current_stream(device))
     torch.cuda.set_stream(stream)
 
+    from mojo_llm_lab_b200.shard import RowShard, all_gather_rows
+    shard = RowShard(rows, world if sharded else 1, rank if sharded else 0)
     full = host_weights(kind, rows, k, seed=1)
     row_bytes = weight_bytes(kind, 1, k) // (2 if kind == "gate_up" else 1)
-    lo = rank * my_rows if sharded else 0
-    mine = [torch.from_numpy(w[lo * row_bytes:(lo + my_rows) * row_bytes].copy()).to(device) for w in full]
+    lo = shard.start
+    mine = [shard.slice_weights(torch.from_numpy(w), row_bytes).to(device) for w in full]
     weights = [mine] + [[w.clone() for w in mine] for _ in range(copies - 1)]
     xs_host = np.stack([fx.seeded_activation(k, seed=100 + i) for i in range(copies)])
     x_dev = torch.from_numpy(xs_host).to(device)
@@ -263,7 +265,7 @@ def run_ours(args, rank: int, world: int):
         else:
             ops.q4_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
         if sharded:
-            dist.all_gather_into_tensor(gathered[i].view(-1), o.view(-1))
+            dist.all_gather_into_tensor(gathered[i].view(-1), o.view(-1))  # = shard.all_gather_rows layout
 
     def step():
         for i in range(copies):

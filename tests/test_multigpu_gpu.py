@@ -1,0 +1,78 @@
+"""Row-sharded gate/up and vocab matvecs across GPUs (NCCL all-gather).
+
+Runs as one process per GPU (spawned here); skipped with fewer than 2 GPUs.
+Rank 0 checks the gathered outputs against the unsharded oracle."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, kind, rows, k, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    ok = False
+    try:
+        import oracle
+        from mojo_llm_lab_b200 import fixtures as fx
+        from mojo_llm_lab_b200 import ops
+        from mojo_llm_lab_b200.shard import RowShard, all_gather_rows, assemble
+        gen = fx.seeded_q6k_matrix if kind == "q6k" else fx.seeded_q4k_matrix
+        row_bytes = k // 256 * (210 if kind == "q6k" else 144)
+        host = [gen(rows, k, seed=3 + m) for m in range(1 if kind == "q6k" else 2)]
+        x = fx.seeded_activation(k, seed=9)
+        act = ops.quantize_q8_1(torch.from_numpy(x).cuda())
+        shard = RowShard(rows, world, rank)
+        mine = [shard.slice_weights(torch.from_numpy(w), row_bytes).cuda() for w in host]
+        if kind == "q6k":
+            local = ops.q6_k_q8_1_matvec(mine[0], act).view(1, -1)
+        else:
+            local = torch.stack(ops.q4k_gate_up(mine[0], mine[1], act))
+        full = assemble(all_gather_rows(local, shard), shard).cpu().numpy().astype(np.float64)
+        if rank == 0:
+            a = oracle.quantize_q8_1(x)
+            ref = [oracle.q6k_matvec(host[0], a, rows, k)] if kind == "q6k" else \
+                list(oracle.q4k_gate_up(host[0], host[1], a, rows, k))
+            ref = np.stack(ref)
+            ok = bool(np.all(np.abs(full - ref) <= 1e-5 + 1e-5 * np.abs(ref)))
+            q.put(ok)
+        torch.cuda.synchronize()
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("kind,rows", [("gate_up", 9728), ("q6k", 151936)])
+def test_sharded_over_all_gpus(kind, rows):
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, kind, rows, 2560, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0] * world, codes
+    assert q.get(timeout=10) is True
