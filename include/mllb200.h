@@ -62,8 +62,11 @@ const char *mllb_last_error(void);
 
 /*
  * Device error word: bit 0/1/2 = a kernel gave up a bounded (~1 s) wait on
- * its TMA pipeline (see csrc/common.cuh).  Copies the word of the current
- * device to *bits (synchronising), optionally clearing it.  0 in normal runs.
+ * its TMA pipeline (see csrc/common.cuh); bit 3 = decode next-token key out
+ * of range; bit 4 = decode position outside the KV cache; bit 5 = decode
+ * attention gave up waiting for its K/V copies.  Copies the word of the
+ * current device to *bits (synchronising), optionally clearing it.  0 in
+ * normal runs.
  */
 int mllb_device_error(uint32_t *bits, int clear);
 
@@ -74,6 +77,8 @@ int mllb_device_error(uint32_t *bits, int clear);
  * matvec (benchmark/q4_compare.c:328-330; bytes checked at :351-357).
  */
 int mllb_q8_1_quantize(const float *x, void *q8, int64_t k, int s_mode, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL). */
+int mllb_q8_1_quantize_ex(const float *x, void *q8, int64_t k, int s_mode, unsigned flags, void *stream);
 
 /*
  * out[r] = sum_k W[r,k] * a[k] for Q4_K weights (n rows, k columns) and a
@@ -150,6 +155,109 @@ int mllb_q4k_subdots(const void *weights, const void *q8, int32_t *dots, int32_t
  * (tools/run_bandwidth_roofline.py:96-110), which used 8-byte loads.
  */
 int mllb_stream_read(const void *data, int64_t bytes, void *out, int64_t blocks, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Single-token decode step of a Qwen3-style stack (36 layers, hidden 2560,
+ * 32 Q / 8 KV heads of 128, SwiGLU 9728, vocab 151936): the GGML ops that
+ * the reference's decode runs around its kernels (llama.cpp graph driven by
+ * integration/resident_decode.cpp; op shares in docs/decode-profile.md:5-11).
+ * The matvecs above plus these entries make one step; all of them can be
+ * captured into one CUDA graph and replayed per token, because everything
+ * that changes between tokens lives in device memory (mllb_decode_state).
+ *
+ * Numerics: fp64 inside each kernel, rounded once to the fp32 (or fp16 / Q8_1)
+ * value that leaves it.
+ *
+ * PDL: with MLLB_LAUNCH_PDL the attention copies the K/V rows below
+ * state->pos before waiting on the preceding kernel, so neither those rows
+ * nor state->pos may be written by the kernels launched just before it (in
+ * the decode step only the final norm moves pos).
+ * ---------------------------------------------------------------------- */
+
+/* Device-resident state of a decode loop (32 bytes, 8-byte aligned). */
+typedef struct mllb_decode_state {
+    int64_t next_token_key; /* greedy next token, packed (see mllb_token_key) */
+    int32_t pos;            /* position and KV row of the token being decoded */
+    int32_t token;          /* token being decoded (written by mllb_decode_embed) */
+    int32_t steps;          /* decode steps completed (advanced by the final norm) */
+    int32_t reserved[3];
+} mllb_decode_state;
+
+/* Host helpers for the packed next-token key: high 32 bits order the fp32
+ * value, low 32 bits are 0xffffffff - index (ties go to the lower index).
+ * mllb_token_key(t) is a key that selects token t (to seed a decode loop);
+ * mllb_key_token() returns -1 for the "no token" key INT64_MIN. */
+int64_t mllb_token_key(int32_t token);
+int64_t mllb_key_token(int64_t key);
+
+/*
+ * hidden[0..k) = the dequantised row (token) of a Q6_K matrix of `vocab`
+ * rows x k (the output projection, tied to the token embedding), token taken
+ * from state->next_token_key.  Records state->token and, when tokens is not
+ * NULL, tokens[state->steps] (if steps < capacity).  An out-of-range key
+ * sets device error bit 8 and embeds row 0.  GGML get_rows on the token
+ * embedding (no reference kernel).
+ */
+int mllb_decode_embed(const void *q6k_weights, int64_t vocab, int64_t k, mllb_decode_state *state, int32_t *tokens,
+                      int64_t capacity, float *hidden, unsigned flags, void *stream);
+
+/*
+ * Residual + RMSNorm + gamma + Q8_1 in one kernel:
+ *   h = x + delta (fp32; delta may be NULL), stored to x_out when not NULL
+ *   (x_out may equal x);  y = fp32(h / sqrt(mean(h^2) + eps) * gamma);
+ *   q8 = Q8_1(y) (s_mode as mllb_q8_1_quantize).  k: multiple of 32, <= 32768.
+ * GGML add -> rms_norm -> mul -> quantize_q8_1 (benchmark/q4_compare.c:328-330
+ * is the quantise node this absorbs).
+ */
+int mllb_rmsnorm_q8_1(const float *x, const float *delta, float *x_out, const float *gamma, double eps, void *q8,
+                      int64_t k, int s_mode, unsigned flags, void *stream);
+
+/* The step's final norm: mllb_rmsnorm_q8_1 that also resets
+ * state->next_token_key to INT64_MIN and advances state->pos and state->steps. */
+int mllb_decode_final_norm(const float *x, const float *delta, float *x_out, const float *gamma, double eps,
+                           void *q8, int64_t k, mllb_decode_state *state, unsigned flags, void *stream);
+
+/*
+ * qkv: fp32 output of the fused QKV projection, (q_heads + 2 kv_heads) x 128
+ * (Q heads, then K heads, then V heads).  Q heads: RMSNorm (eps 1e-6) *
+ * q_gamma + IMROPE -> q_out.  K heads: RMSNorm * k_gamma + IMROPE, then fp16
+ * at row state->pos of k_cache.  V heads: fp16 at row state->pos of v_cache.
+ * IMROPE axis positions (pos, pos, pos, 0), theta scale theta_scale (host
+ * double; the reference's runtime value is the fp32 0x3f492c27).
+ * Caches: fp16 [kv_heads][ctx][128].  pos outside [0, ctx) sets device error
+ * bit 16 and appends nothing.  The q part is the reference's
+ * kernels/fused_q_imrope_runtime_fastpow.mojo:8-36 per head.
+ */
+int mllb_decode_qk_rope_append(const float *qkv, const float *q_gamma, const float *k_gamma,
+                               const mllb_decode_state *state, double theta_scale, float *q_out, void *k_cache,
+                               void *v_cache, int64_t q_heads, int64_t kv_heads, int64_t ctx, unsigned flags,
+                               void *stream);
+
+/* Scratch (in doubles) that mllb_decode_attention needs for these shapes on
+ * the current device, or a negative MLLB_E* code. */
+int64_t mllb_decode_attention_scratch(int64_t q_heads, int64_t kv_heads, int64_t ctx);
+
+/*
+ * Attention of the token at state->pos over cache rows 0..pos (grouped
+ * query heads: q head h reads kv head h / (q_heads / kv_heads); ratio 1, 2,
+ * 4 or 8): softmax(q . k / sqrt(128)) . v per q head, fp64 throughout,
+ * split over context chunks into `scratch` and merged.  Writes out (fp32
+ * q_heads x 128, may be NULL) and q8 (its Q8_1, the O projection input, may
+ * be NULL).  Two kernels.  GGML flash_attn_ext on the fp16 cache (the
+ * reference enables flash attention: integration/resident_decode.cpp:71).
+ */
+int mllb_decode_attention(const float *q, const void *k_cache, const void *v_cache, const mllb_decode_state *state,
+                          double *scratch, int64_t scratch_doubles, float *out, void *q8, int64_t q_heads,
+                          int64_t kv_heads, int64_t ctx, unsigned flags, void *stream);
+
+/*
+ * *key = max(*key, max over i of key(x[i], index_offset + i)) with the packed
+ * key of mllb_token_key (the greedy argmax; for a row shard pass the shard's
+ * first row as index_offset).  *key must hold INT64_MIN or an earlier
+ * maximum.  GGML argmax / the reference's LogitValidation top-1
+ * (integration/logit_validation.h:76-80).
+ */
+int mllb_argmax_f32(const float *x, int64_t n, int64_t index_offset, int64_t *key, unsigned flags, void *stream);
 
 #ifdef __cplusplus
 }

@@ -44,6 +44,17 @@ SIGNATURES = {
     "mllb_rmsnorm_imrope_q_batched": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _I64, _I64, _P]),
     "mllb_q4k_subdots": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _P]),
     "mllb_stream_read": (C.c_int, [_P, _I64, _P, _I64, _P]),
+    "mllb_q8_1_quantize_ex": (C.c_int, [_P, _P, _I64, C.c_int, C.c_uint, _P]),
+    "mllb_token_key": (_I64, [C.c_int32]),
+    "mllb_key_token": (_I64, [_I64]),
+    "mllb_decode_embed": (C.c_int, [_P, _I64, _I64, _P, _P, _I64, _P, C.c_uint, _P]),
+    "mllb_rmsnorm_q8_1": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _I64, C.c_int, C.c_uint, _P]),
+    "mllb_decode_final_norm": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _I64, _P, C.c_uint, _P]),
+    "mllb_decode_qk_rope_append": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _P, _P, _I64, _I64, _I64, C.c_uint,
+                                             _P]),
+    "mllb_decode_attention_scratch": (_I64, [_I64, _I64, _I64]),
+    "mllb_decode_attention": (C.c_int, [_P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, C.c_uint, _P]),
+    "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
 }
 
 _lock = threading.Lock()

@@ -17,6 +17,7 @@
 #include "q6k.cuh"
 #include "q8_1.cuh"
 #include "stream.cuh"
+#include "decode.cuh"
 
 // Streaming-kernel configurations: V (row groups per tile), S (stages),
 // TEAMS (consumer teams per CTA) per format, matrices and K/256.  Each can
@@ -255,16 +256,22 @@ int mllb_device_error(uint32_t* bits, int clear) {
 }
 
 int mllb_q8_1_quantize(const float* x, void* q8, int64_t k, int s_mode, void* stream) {
+  return mllb_q8_1_quantize_ex(x, q8, k, s_mode, 0u, stream);
+}
+
+int mllb_q8_1_quantize_ex(const float* x, void* q8, int64_t k, int s_mode, unsigned flags, void* stream) {
   if (!x || !q8) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   if (k <= 0 || k % 32) return fail(MLLB_EINVAL, "k=%lld is not a positive multiple of 32", static_cast<long long>(k));
   if (s_mode != MLLB_Q8_1_S_D_SUMQ && s_mode != MLLB_Q8_1_S_SUM_X) return fail(MLLB_EINVAL, "unknown s_mode %d", s_mode);
   if (!aligned(x, 4) || !aligned(q8, 4)) return fail(MLLB_EALIGN, "x and q8 must be 4-byte aligned");
   const int64_t blocks = k / 32;
   int64_t grid = (blocks + 7) / 8;
   if (grid > 65535) grid = 65535;
-  mllb::q8_1_quantize_kernel<<<static_cast<int>(grid), 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      x, static_cast<uint8_t*>(q8), blocks, s_mode);
-  return check_launch("q8_1 quantize kernel");
+  return launched(launch(mllb::q8_1_quantize_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, static_cast<uint8_t*>(q8),
+                         blocks, s_mode),
+                  "q8_1 quantize kernel");
 }
 
 int mllb_q4k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
@@ -396,6 +403,201 @@ int mllb_stream_read(const void* data, int64_t bytes, void* out, int64_t blocks,
   mllb::stream_read_kernel<<<static_cast<int>(blocks), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint4*>(data), bytes / 16, static_cast<uint4*>(out));
   return check_launch("stream read kernel");
+}
+
+}  // extern "C"
+
+// ------------------------------------------------------------------ decode
+
+namespace {
+
+constexpr int kAttnMaxChunk = 256;
+
+// Context chunks per KV head: enough CTAs for one per SM, and chunks of at
+// most kAttnMaxChunk keys.
+int64_t attention_splits(int dev, int64_t kv_heads, int64_t ctx) {
+  int64_t base = sm_count(dev) / kv_heads;
+  if (base < 1) base = 1;
+  const int64_t need = (ctx + kAttnMaxChunk - 1) / kAttnMaxChunk;
+  return base > need ? base : need;
+}
+
+int check_attention_shape(int64_t q_heads, int64_t kv_heads, int64_t ctx) {
+  if (q_heads <= 0 || kv_heads <= 0 || q_heads % kv_heads)
+    return fail(MLLB_EINVAL, "q_heads=%lld is not a positive multiple of kv_heads=%lld",
+                static_cast<long long>(q_heads), static_cast<long long>(kv_heads));
+  const int64_t g = q_heads / kv_heads;
+  if (g != 1 && g != 2 && g != 4 && g != 8)
+    return fail(MLLB_EUNSUPPORTED, "query heads per KV head must be 1, 2, 4 or 8 (got %lld)", static_cast<long long>(g));
+  if (ctx <= 0 || ctx > (1 << 24)) return fail(MLLB_EINVAL, "ctx=%lld out of range", static_cast<long long>(ctx));
+  if (kv_heads > 65535) return fail(MLLB_EUNSUPPORTED, "too many KV heads");
+  return MLLB_OK;
+}
+
+template <int G>
+int launch_attention(const float* q, const uint8_t* k_cache, const uint8_t* v_cache, const mllb::DecodeState* state,
+                     double* part_acc, double* part_ml, int64_t splits, int64_t kv_heads, int64_t ctx,
+                     cudaStream_t stream, bool pdl) {
+  using C = mllb::AttnConfig<G>;
+  int dev, rc, grid, per_sm;
+  if ((rc = current_device(&dev))) return rc;
+  auto kernel = mllb::attn_split_kernel<G>;
+  if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, 1, &grid, &per_sm))) return rc;
+  return launched(launch(kernel, dim3(static_cast<unsigned>(splits), static_cast<unsigned>(kv_heads)),
+                         dim3(C::kThreads), C::kSmemBytes, stream, pdl, q, k_cache, v_cache, state, part_acc, part_ml,
+                         static_cast<int>(ctx), static_cast<int>(splits), 1.0 / sqrt(128.0)),
+                  "decode attention kernel");
+}
+
+int rmsnorm_q8_1_launch(const float* x, const float* delta, float* x_out, const float* gamma, double eps, void* q8,
+                        int64_t k, int s_mode, mllb::DecodeState* advance, unsigned flags, void* stream) {
+  if (!x || !gamma || !q8) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (k <= 0 || k % 32 || k > 32768)
+    return fail(MLLB_EINVAL, "k=%lld is not a positive multiple of 32 up to 32768", static_cast<long long>(k));
+  if (s_mode != MLLB_Q8_1_S_D_SUMQ && s_mode != MLLB_Q8_1_S_SUM_X) return fail(MLLB_EINVAL, "unknown s_mode %d", s_mode);
+  if (!(eps >= 0.0)) return fail(MLLB_EINVAL, "eps must be >= 0");
+  if (!aligned(x, 4) || !aligned(delta, 4) || !aligned(x_out, 4) || !aligned(gamma, 4) || !aligned(q8, 4))
+    return fail(MLLB_EALIGN, "fp32 and Q8_1 pointers must be 4-byte aligned");
+  int dev, rc, grid, per_sm;
+  if ((rc = current_device(&dev))) return rc;
+  const int smem = static_cast<int>(k) * 4;
+  if ((rc = stream_grid(mllb::rmsnorm_q8_1_kernel, 32768 * 4, 1024, dev, 1, &grid, &per_sm))) return rc;
+  return launched(launch(mllb::rmsnorm_q8_1_kernel, dim3(1), dim3(1024), smem, static_cast<cudaStream_t>(stream),
+                         flags & MLLB_LAUNCH_PDL, x, delta, x_out, gamma, eps, static_cast<uint8_t*>(q8),
+                         static_cast<int>(k), s_mode, advance),
+                  "rmsnorm q8_1 kernel");
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t mllb_token_key(int32_t token) {
+  return static_cast<int64_t>(0xffffffffull - static_cast<uint32_t>(token));
+}
+
+int64_t mllb_key_token(int64_t key) {
+  if (key == INT64_MIN) return -1;
+  return static_cast<int64_t>(0xffffffffull - (static_cast<uint64_t>(key) & 0xffffffffull));
+}
+
+int mllb_decode_embed(const void* q6k_weights, int64_t vocab, int64_t k, mllb_decode_state* state, int32_t* tokens,
+                      int64_t capacity, float* hidden, unsigned flags, void* stream) {
+  if (!q6k_weights || !state || !hidden) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (vocab <= 0 || vocab > 0xffffffffll) return fail(MLLB_EINVAL, "vocab=%lld out of range", static_cast<long long>(vocab));
+  if (k <= 0 || k % 256 || k > (1 << 20))
+    return fail(MLLB_EINVAL, "k=%lld is not a positive multiple of 256", static_cast<long long>(k));
+  if (tokens && capacity < 0) return fail(MLLB_EINVAL, "negative capacity");
+  if (!aligned(state, 8) || !aligned(hidden, 4) || (tokens && !aligned(tokens, 4)))
+    return fail(MLLB_EALIGN, "state needs 8-byte, hidden/tokens 4-byte alignment");
+  const int grid = static_cast<int>((k + 255) / 256);
+  return launched(launch(mllb::embed_q6k_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                         flags & MLLB_LAUNCH_PDL, static_cast<const uint8_t*>(q6k_weights),
+                         static_cast<int>(k / 256), vocab, reinterpret_cast<mllb::DecodeState*>(state), tokens,
+                         tokens ? capacity : 0, hidden),
+                  "embedding kernel");
+}
+
+int mllb_rmsnorm_q8_1(const float* x, const float* delta, float* x_out, const float* gamma, double eps, void* q8,
+                      int64_t k, int s_mode, unsigned flags, void* stream) {
+  return rmsnorm_q8_1_launch(x, delta, x_out, gamma, eps, q8, k, s_mode, nullptr, flags, stream);
+}
+
+int mllb_decode_final_norm(const float* x, const float* delta, float* x_out, const float* gamma, double eps,
+                           void* q8, int64_t k, mllb_decode_state* state, unsigned flags, void* stream) {
+  if (!state) return fail(MLLB_EINVAL, "null pointer: state");
+  if (!aligned(state, 8)) return fail(MLLB_EALIGN, "state needs 8-byte alignment");
+  return rmsnorm_q8_1_launch(x, delta, x_out, gamma, eps, q8, k, MLLB_Q8_1_S_D_SUMQ,
+                             reinterpret_cast<mllb::DecodeState*>(state), flags, stream);
+}
+
+int mllb_decode_qk_rope_append(const float* qkv, const float* q_gamma, const float* k_gamma,
+                               const mllb_decode_state* state, double theta_scale, float* q_out, void* k_cache,
+                               void* v_cache, int64_t q_heads, int64_t kv_heads, int64_t ctx, unsigned flags,
+                               void* stream) {
+  if (!qkv || !q_gamma || !k_gamma || !state || !q_out || !k_cache || !v_cache) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (q_heads <= 0 || kv_heads <= 0 || q_heads + 2 * kv_heads > (1 << 20))
+    return fail(MLLB_EINVAL, "head counts out of range");
+  if (ctx <= 0 || ctx > (1 << 24)) return fail(MLLB_EINVAL, "ctx=%lld out of range", static_cast<long long>(ctx));
+  if (!(theta_scale > 0.0)) return fail(MLLB_EINVAL, "theta_scale must be positive");
+  if (!aligned(qkv, 4) || !aligned(q_gamma, 4) || !aligned(k_gamma, 4) || !aligned(state, 8) || !aligned(q_out, 4) ||
+      !aligned(k_cache, 2) || !aligned(v_cache, 2))
+    return fail(MLLB_EALIGN, "fp32 pointers need 4-byte, caches 2-byte, state 8-byte alignment");
+  const int64_t warps = q_heads + 2 * kv_heads;
+  const int grid = static_cast<int>((warps + 7) / 8);
+  return launched(launch(mllb::qk_rope_append_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+                         flags & MLLB_LAUNCH_PDL, qkv, q_gamma, k_gamma,
+                         reinterpret_cast<const mllb::DecodeState*>(state), theta_scale, q_out,
+                         static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), static_cast<int>(q_heads),
+                         static_cast<int>(kv_heads), static_cast<int>(ctx)),
+                  "q/k rope + KV append kernel");
+}
+
+int64_t mllb_decode_attention_scratch(int64_t q_heads, int64_t kv_heads, int64_t ctx) {
+  int rc = check_attention_shape(q_heads, kv_heads, ctx);
+  if (rc) return rc;
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  return q_heads * attention_splits(dev, kv_heads, ctx) * (128 + 2);
+}
+
+int mllb_decode_attention(const float* q, const void* k_cache, const void* v_cache, const mllb_decode_state* state,
+                          double* scratch, int64_t scratch_doubles, float* out, void* q8, int64_t q_heads,
+                          int64_t kv_heads, int64_t ctx, unsigned flags, void* stream) {
+  if (!q || !k_cache || !v_cache || !state || !scratch) return fail(MLLB_EINVAL, "null pointer");
+  if (!out && !q8) return fail(MLLB_EINVAL, "no output requested");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_attention_shape(q_heads, kv_heads, ctx);
+  if (rc) return rc;
+  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(state, 8) ||
+      !aligned(scratch, 8) || !aligned(out, 4) || !aligned(q8, 4))
+    return fail(MLLB_EALIGN, "q and caches need 16-byte, state/scratch 8-byte, out/q8 4-byte alignment");
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  const int64_t splits = attention_splits(dev, kv_heads, ctx);
+  const int64_t need = q_heads * splits * (128 + 2);
+  if (scratch_doubles < need)
+    return fail(MLLB_EINVAL, "scratch holds %lld doubles, %lld needed", static_cast<long long>(scratch_doubles),
+                static_cast<long long>(need));
+  if (splits > 65535) return fail(MLLB_EUNSUPPORTED, "context too long");
+  double* part_acc = scratch;
+  double* part_ml = scratch + q_heads * splits * 128;
+  const auto* st = reinterpret_cast<const mllb::DecodeState*>(state);
+  const auto* kc = static_cast<const uint8_t*>(k_cache);
+  const auto* vc = static_cast<const uint8_t*>(v_cache);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = flags & MLLB_LAUNCH_PDL;
+  switch (q_heads / kv_heads) {
+    case 1: rc = launch_attention<1>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
+    case 2: rc = launch_attention<2>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
+    case 4: rc = launch_attention<4>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
+    default: rc = launch_attention<8>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
+  }
+  if (rc) return rc;
+  return launched(launch(mllb::attn_combine_kernel, dim3(static_cast<unsigned>(q_heads)), dim3(128), 0, s, pdl,
+                         static_cast<const double*>(part_acc), static_cast<const double*>(part_ml),
+                         static_cast<int>(splits), out, static_cast<uint8_t*>(q8), MLLB_Q8_1_S_D_SUMQ),
+                  "attention combine kernel");
+}
+
+int mllb_argmax_f32(const float* x, int64_t n, int64_t index_offset, int64_t* key, unsigned flags, void* stream) {
+  if (!x || !key) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (n <= 0 || index_offset < 0 || index_offset + n > 0xffffffffll)
+    return fail(MLLB_EINVAL, "indices must lie in [0, 2^32 - 1)");
+  if (!aligned(x, 4) || !aligned(key, 8)) return fail(MLLB_EALIGN, "x needs 4-byte, key 8-byte alignment");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  int64_t grid = (n + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(sm_count(dev)) * 2;
+  if (grid > cap) grid = cap;
+  return launched(launch(mllb::argmax_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, n, index_offset,
+                         reinterpret_cast<long long*>(key)),
+                  "argmax kernel");
 }
 
 }  // extern "C"

@@ -20,6 +20,9 @@ enum : uint32_t {
   kErrFullWaitTimeout = 1u << 0,   // consumer gave up waiting for a weight tile
   kErrEmptyWaitTimeout = 1u << 1,  // producer gave up waiting for a free stage
   kErrDrainTimeout = 1u << 2,      // producer gave up waiting for its last copies
+  kErrBadToken = 1u << 3,          // decode: next-token key outside the vocabulary (row 0 used)
+  kErrKvOverflow = 1u << 4,        // decode: position at or past the KV capacity (nothing written)
+  kErrKvWaitTimeout = 1u << 5,     // decode attention gave up waiting for its K/V copies
 };
 
 // 1 s of wall time, and a hard iteration cap behind it.

@@ -27,10 +27,13 @@ __device__ __forceinline__ int imrope_axis(int pair) {
   return 3;
 }
 
-// One head, computed by the 32 lanes of the calling warp.
-__device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                 const int32_t* __restrict__ pos, double theta_scale,
-                                                 float* __restrict__ out, int lane) {
+// One head, computed by the 32 lanes of the calling warp: lane l returns
+// o[0] = out[l], o[1] = out[l + 64] (pair l) and o[2] = out[l + 32],
+// o[3] = out[l + 96] (pair l + 32), in fp64.  p0..p3 are the head's 4 axis
+// positions.
+__device__ __forceinline__ void imrope_head_values(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                   int32_t p0, int32_t p1, int32_t p2, int32_t p3,
+                                                   double theta_scale, int lane, double (&o)[4]) {
   const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
   double ss = static_cast<double>(x0) * x0;
   ss = fma(static_cast<double>(x1), static_cast<double>(x1), ss);
@@ -41,14 +44,28 @@ __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, co
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     const int p = lane + 32 * half;
-    const double angle = static_cast<double>(pos[imrope_axis(p)]) * pow(theta_scale, static_cast<double>(p));
+    const int axis = imrope_axis(p);
+    const int32_t position = axis == 0 ? p0 : axis == 1 ? p1 : axis == 2 ? p2 : p3;
+    const double angle = static_cast<double>(position) * pow(theta_scale, static_cast<double>(p));
     double s, c;
     sincos(angle, &s, &c);
     const double ya = static_cast<double>(half ? x1 : x0) * r * static_cast<double>(gamma[p]);
     const double yb = static_cast<double>(half ? x3 : x2) * r * static_cast<double>(gamma[p + 64]);
-    out[p] = static_cast<float>(ya * c - yb * s);
-    out[p + 64] = static_cast<float>(ya * s + yb * c);
+    o[2 * half] = ya * c - yb * s;
+    o[2 * half + 1] = ya * s + yb * c;
   }
+}
+
+// One head, computed by the 32 lanes of the calling warp, stored as fp32.
+__device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                 const int32_t* __restrict__ pos, double theta_scale,
+                                                 float* __restrict__ out, int lane) {
+  double o[4];
+  imrope_head_values(x, gamma, pos[0], pos[1], pos[2], pos[3], theta_scale, lane, o);
+  out[lane] = static_cast<float>(o[0]);
+  out[lane + 64] = static_cast<float>(o[1]);
+  out[lane + 32] = static_cast<float>(o[2]);
+  out[lane + 96] = static_cast<float>(o[3]);
 }
 
 // Grid-stride over heads, one warp each.  Head h belongs to token

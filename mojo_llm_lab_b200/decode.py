@@ -1,0 +1,438 @@
+"""Synthetic Qwen3-style single-token decode on the B200 kernels.
+
+The whole-model context of the reference's hot path (its PRD shapes,
+docs/PRDs/11-06-2026-quantized-matvec.md:7, and the llama.cpp decode it
+profiles, docs/decode-profile.md:5-11): a stack of ``layers`` blocks
+
+    h = embed(token)                                  tied Q6_K output rows
+    per layer:
+      a   = Q8_1(rmsnorm(h) * attn_gamma)
+      qkv = Wqkv a                                    Q4_K, one fused matrix
+      q, k = rmsnorm(head) * q/k_gamma + IMROPE;  k, v -> fp16 KV cache
+      o   = Wo Q8_1(attention(q, K, V))               Q4_K
+      h  += o;  a = Q8_1(rmsnorm(h) * ffn_gamma)
+      f   = up(a) * silu(gate(a))                     fused Q4_K gate/up
+      h  += Wdown Q8_1(f)                             Q4_K
+    logits = Wout Q8_1(rmsnorm(h) * out_gamma)        Q6_K
+    next   = argmax(logits)                           greedy
+
+Everything that changes from token to token (the token, its position, the
+KV rows) lives in device memory, so one step is captured once as a CUDA
+graph of PDL-chained launches and replayed per token.  Weights and the
+prefilled KV cache are random (seeded) in the distributions of the
+reference's fixtures; there is no checkpoint.
+
+Multi-GPU (one process per GPU, ``torch.distributed`` over NCCL): the
+gate/up and vocabulary matvecs are row-sharded.  Each rank quantises its
+slice of the SwiGLU product and an all-gather of the Q8_1 bytes gives every
+rank the down projection's input; each rank takes the argmax of its logit
+rows and an all-reduce MAX of the packed (value, index) keys gives every rank
+the next token.  Everything else is replicated.
+"""
+from __future__ import annotations
+
+import struct
+from dataclasses import dataclass, field
+
+import numpy as np
+import torch
+
+from . import formats as F
+from ._lib import LAUNCH_PDL, check, lib
+from .shard import RowShard
+
+HEAD_DIM = 128
+STATE_BYTES = 32
+
+
+@dataclass(frozen=True)
+class DecodeConfig:
+    """Shapes of the synthetic stack (defaults: the 36-layer decode config)."""
+
+    layers: int = 36
+    hidden: int = 2560
+    q_heads: int = 32
+    kv_heads: int = 8
+    ffn: int = 9728
+    vocab: int = 151936
+    context: int = 4096        # prefilled KV rows
+    new_tokens: int = 128      # decode steps the KV cache has room for
+    eps: float = 1e-6
+    theta_bits: int = 0x3F492C27
+    seed: int = 20260611
+
+    def validate(self) -> None:
+        if self.layers < 1:
+            raise ValueError("layers must be >= 1")
+        for name in ("hidden", "ffn"):
+            if getattr(self, name) <= 0 or getattr(self, name) % 256:
+                raise ValueError(f"{name} must be a positive multiple of 256")
+        if self.q_heads <= 0 or self.kv_heads <= 0 or self.q_heads % self.kv_heads:
+            raise ValueError("q_heads must be a positive multiple of kv_heads")
+        if self.q_heads // self.kv_heads not in (1, 2, 4, 8):
+            raise ValueError("q_heads / kv_heads must be 1, 2, 4 or 8")
+        if (self.q_heads * HEAD_DIM) % 256:
+            raise ValueError("q_heads * 128 must be a multiple of 256 (O projection width)")
+        if self.vocab <= 0 or self.context < 0 or self.new_tokens <= 0:
+            raise ValueError("vocab, new_tokens must be positive and context >= 0")
+
+    @property
+    def qkv_rows(self) -> int:
+        return (self.q_heads + 2 * self.kv_heads) * HEAD_DIM
+
+    @property
+    def attn_width(self) -> int:
+        return self.q_heads * HEAD_DIM
+
+    @property
+    def ctx_capacity(self) -> int:
+        return self.context + self.new_tokens
+
+    @property
+    def theta_scale(self) -> float:
+        return struct.unpack("<f", struct.pack("<I", self.theta_bits))[0]
+
+    def q4k_bytes(self) -> int:
+        """Q4_K weight bytes of the whole stack."""
+        per_layer = (self.qkv_rows * self.hidden + self.hidden * self.attn_width + 2 * self.ffn * self.hidden +
+                     self.hidden * self.ffn) // 256 * F.Q4K_BLOCK_BYTES
+        return per_layer * self.layers
+
+    def q6k_bytes(self) -> int:
+        return self.vocab * self.hidden // 256 * F.Q6K_BLOCK_BYTES
+
+    def kv_bytes_read(self, n_keys: int) -> int:
+        """fp16 K and V bytes one step reads over n_keys cache rows."""
+        return self.layers * 2 * self.kv_heads * n_keys * HEAD_DIM * 2
+
+    def bytes_per_token(self, n_keys: int) -> int:
+        """Algorithmic HBM bytes of one step: every weight once, the KV rows once."""
+        return self.q4k_bytes() + self.q6k_bytes() + self.kv_bytes_read(n_keys)
+
+
+def _seed(cfg: DecodeConfig, layer: int, slot: int) -> int:
+    return (cfg.seed * 1_000_003 + (layer + 1) * 1009 + slot) % (1 << 62)
+
+
+def _generator(device: torch.device, seed: int) -> torch.Generator:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    return g
+
+
+def _fp16_field(n: int, low: float, high: float, g: torch.Generator, device) -> torch.Tensor:
+    v = torch.empty(n, dtype=torch.float32, device=device).uniform_(low, high, generator=g)
+    return v.half().view(torch.uint8).view(n, 2)
+
+
+def random_q4k(rows: int, k: int, seed: int, device, signed_scales: bool = True) -> torch.Tensor:
+    """Q4_K rows: fp16 |d| ~ U(1e-3, 1e-2), |dmin| ~ U(0, 5e-3), uniform 6-bit
+    scales / mins (every bit of the 12 packed bytes belongs to exactly one of
+    them, so uniform bytes are uniform fields) and uniform nibbles.
+
+    signed_scales gives each block's d and dmin independent random signs.
+    With both positive every weight d*sc*q - dmin*m has mean ~ +1.2, each
+    projection output carries a common mode of ~1.2 * sum(input) that RMSNorm
+    turns into an all-positive input of the next layer, and within two layers
+    the SwiGLU product passes 127 * 65504, the largest activation a Q8_1
+    block's fp16 scale can hold: the scale becomes inf and the logits NaN (as
+    in GGML).  A random sign of d alone still leaves the -dmin*m bias, whose
+    common mode builds up along the residual stream until the same overflow
+    (layer 32 of 36).  With both signs random the rows are zero-mean and the
+    36-layer stack stays finite."""
+    g = _generator(torch.device(device), seed)
+    n = rows * (k // 256)
+    blocks = torch.randint(0, 256, (n, F.Q4K_BLOCK_BYTES), dtype=torch.uint8, generator=g, device=device)
+    blocks[:, 0:2] = _fp16_field(n, 1e-3, 1e-2, g, device)
+    blocks[:, 2:4] = _fp16_field(n, 0.0, 5e-3, g, device)
+    if signed_scales:
+        signs = torch.randint(0, 4, (n,), dtype=torch.uint8, generator=g, device=device)
+        blocks[:, 1] |= (signs & 1) << 7
+        blocks[:, 3] |= (signs & 2) << 6
+    return blocks.view(-1)
+
+
+def random_q6k(rows: int, k: int, seed: int, device) -> torch.Tensor:
+    """Q6_K rows: uniform ql / qh bytes, int8 scales ~ U{-32..31}, fp16 d ~ U(1e-3, 1e-2)."""
+    g = _generator(torch.device(device), seed)
+    n = rows * (k // 256)
+    blocks = torch.randint(0, 256, (n, F.Q6K_BLOCK_BYTES), dtype=torch.uint8, generator=g, device=device)
+    blocks[:, 192:208] = torch.randint(-32, 32, (n, 16), dtype=torch.int8, generator=g,
+                                       device=device).view(torch.uint8)
+    blocks[:, 208:210] = _fp16_field(n, 1e-3, 1e-2, g, device)
+    return blocks.view(-1)
+
+
+def random_gamma(n: int, seed: int, device) -> torch.Tensor:
+    g = _generator(torch.device(device), seed)
+    return torch.empty(n, dtype=torch.float32, device=device).uniform_(0.5, 1.5, generator=g)
+
+
+@dataclass
+class LayerWeights:
+    qkv: torch.Tensor         # Q4_K [(q_heads + 2 kv_heads) * 128, hidden]
+    o: torch.Tensor           # Q4_K [hidden, q_heads * 128]
+    up: torch.Tensor          # Q4_K [ffn rows of this rank, hidden]
+    gate: torch.Tensor        # Q4_K [ffn rows of this rank, hidden]
+    down: torch.Tensor        # Q4_K [hidden, ffn]
+    attn_norm: torch.Tensor   # fp32 [hidden]
+    q_norm: torch.Tensor      # fp32 [128]
+    k_norm: torch.Tensor      # fp32 [128]
+    ffn_norm: torch.Tensor    # fp32 [hidden]
+
+
+@dataclass
+class DecodeWeights:
+    cfg: DecodeConfig
+    layers: list[LayerWeights]
+    out_norm: torch.Tensor    # fp32 [hidden]
+    output: torch.Tensor      # Q6_K [vocab rows of this rank, hidden]
+    embedding: torch.Tensor   # Q6_K [vocab, hidden] (full; tied to the output projection)
+    ffn_shard: RowShard
+    vocab_shard: RowShard
+
+    def nbytes(self) -> int:
+        n = self.output.numel() + self.out_norm.numel() * 4
+        if self.embedding.data_ptr() != self.output.data_ptr():
+            n += self.embedding.numel()
+        for lw in self.layers:
+            n += sum(t.numel() * t.element_size() for t in vars(lw).values())
+        return n
+
+
+def generate_weights(cfg: DecodeConfig, device, world: int = 1, rank: int = 0) -> DecodeWeights:
+    """Seeded random weights; with world > 1 only this rank's gate/up and
+    output rows are kept (the same bytes every layout would give)."""
+    cfg.validate()
+    ffn_shard = RowShard(cfg.ffn, world, rank)
+    vocab_shard = RowShard(cfg.vocab, world, rank)
+    row_bytes = cfg.hidden // 256 * F.Q4K_BLOCK_BYTES
+    layers = []
+    for layer in range(cfg.layers):
+        up = random_q4k(cfg.ffn, cfg.hidden, _seed(cfg, layer, 2), device)
+        gate = random_q4k(cfg.ffn, cfg.hidden, _seed(cfg, layer, 3), device)
+        if world > 1:
+            up = up[ffn_shard.start * row_bytes:ffn_shard.stop * row_bytes].clone()
+            gate = gate[ffn_shard.start * row_bytes:ffn_shard.stop * row_bytes].clone()
+        layers.append(LayerWeights(
+            qkv=random_q4k(cfg.qkv_rows, cfg.hidden, _seed(cfg, layer, 0), device),
+            o=random_q4k(cfg.hidden, cfg.attn_width, _seed(cfg, layer, 1), device),
+            up=up,
+            gate=gate,
+            down=random_q4k(cfg.hidden, cfg.ffn, _seed(cfg, layer, 4), device),
+            attn_norm=random_gamma(cfg.hidden, _seed(cfg, layer, 5), device),
+            q_norm=random_gamma(HEAD_DIM, _seed(cfg, layer, 6), device),
+            k_norm=random_gamma(HEAD_DIM, _seed(cfg, layer, 7), device),
+            ffn_norm=random_gamma(cfg.hidden, _seed(cfg, layer, 8), device),
+        ))
+    embedding = random_q6k(cfg.vocab, cfg.hidden, _seed(cfg, -1, 0), device)
+    out_row = cfg.hidden // 256 * F.Q6K_BLOCK_BYTES
+    output = embedding if world == 1 else \
+        embedding[vocab_shard.start * out_row:vocab_shard.stop * out_row].clone()
+    return DecodeWeights(cfg=cfg, layers=layers, out_norm=random_gamma(cfg.hidden, _seed(cfg, -1, 1), device),
+                         output=output, embedding=embedding, ffn_shard=ffn_shard, vocab_shard=vocab_shard)
+
+
+def generate_kv_cache(cfg: DecodeConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """fp16 caches [layers, kv_heads, ctx_capacity, 128]: rows < context are
+    N(0, 1) (seeded), the rest zero until decode appends them."""
+    shape = (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, HEAD_DIM)
+    k = torch.zeros(shape, dtype=torch.float16, device=device)
+    v = torch.zeros(shape, dtype=torch.float16, device=device)
+    for layer in range(cfg.layers):
+        for slot, cache in ((9, k), (10, v)):
+            g = _generator(torch.device(device), _seed(cfg, layer, slot))
+            cache[layer, :, :cfg.context] = torch.randn((cfg.kv_heads, cfg.context, HEAD_DIM), generator=g,
+                                                        device=device, dtype=torch.float32).half()
+    return k, v
+
+
+def state_bytes(token: int, pos: int, steps: int = 0) -> bytes:
+    """Host image of mllb_decode_state seeded to decode `token` at `pos`."""
+    key = int(lib().mllb_token_key(token))
+    return struct.pack("<qiii12x", key, pos, token, steps)
+
+
+def parse_state(raw: bytes) -> dict:
+    key, pos, token, steps = struct.unpack("<qiii12x", raw)
+    return {"next_token": int(lib().mllb_key_token(key)), "pos": pos, "token": token, "steps": steps}
+
+
+@dataclass
+class _Buffers:
+    hidden: torch.Tensor
+    q8_hidden: torch.Tensor
+    qkv: torch.Tensor
+    q_rot: torch.Tensor
+    attn: torch.Tensor
+    q8_attn: torch.Tensor
+    o_out: torch.Tensor
+    prod: torch.Tensor
+    q8_prod: torch.Tensor
+    down_out: torch.Tensor
+    logits: torch.Tensor
+    state: torch.Tensor
+    tokens: torch.Tensor
+    scratch: torch.Tensor
+    extra: dict = field(default_factory=dict)
+
+
+class Decoder:
+    """One decode step as a chain of C-ABI launches on one stream.
+
+    ``step()`` launches it eagerly; ``capture()`` records it once into a CUDA
+    graph that ``generate()`` replays per token.  With ``group`` (a NCCL
+    process group of ``world`` ranks) the gate/up and vocabulary matvecs are
+    row-sharded as the module docstring describes.
+    """
+
+    def __init__(self, weights: DecodeWeights, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pdl: bool = True,
+                 group=None):
+        cfg = weights.cfg
+        cfg.validate()
+        self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
+        self.device = k_cache.device
+        self.flags = LAUNCH_PDL if pdl else 0
+        self.group = group
+        self.world = weights.ffn_shard.world
+        if self.world > 1:
+            if group is None:
+                raise ValueError("a sharded decoder needs a process group")
+            if weights.ffn_shard.per_rank % 32 or weights.ffn_shard.per_rank * self.world != cfg.ffn:
+                raise ValueError("gate/up shards must be equal and a multiple of 32 rows")
+        if k_cache.shape != (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, HEAD_DIM) or k_cache.dtype != torch.float16:
+            raise ValueError("k_cache must be fp16 [layers, kv_heads, ctx_capacity, 128]")
+        if v_cache.shape != k_cache.shape or v_cache.dtype != torch.float16:
+            raise ValueError("v_cache must match k_cache")
+        dev = self.device
+        f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)  # noqa: E731
+        u8 = lambda n: torch.zeros(n, dtype=torch.uint8, device=dev)  # noqa: E731
+        with torch.cuda.device(dev):
+            scratch_n = int(lib().mllb_decode_attention_scratch(cfg.q_heads, cfg.kv_heads, cfg.ctx_capacity))
+        if scratch_n < 0:
+            raise ValueError(f"attention shape rejected: {lib().mllb_last_error().decode()}")
+        ffn_local = weights.ffn_shard.local_rows
+        self.b = _Buffers(
+            hidden=f32(cfg.hidden), q8_hidden=u8(cfg.hidden // 32 * 36), qkv=f32(cfg.qkv_rows),
+            q_rot=f32(cfg.attn_width), attn=f32(cfg.attn_width), q8_attn=u8(cfg.attn_width // 32 * 36),
+            o_out=f32(cfg.hidden), prod=f32(ffn_local), q8_prod=u8(cfg.ffn // 32 * 36), down_out=f32(cfg.hidden),
+            logits=f32(weights.vocab_shard.local_rows),
+            state=u8(STATE_BYTES), tokens=torch.zeros(cfg.new_tokens, dtype=torch.int32, device=dev),
+            scratch=torch.zeros(scratch_n, dtype=torch.float64, device=dev))
+        self.graph = None
+
+    # -- state ------------------------------------------------------------
+    def reset(self, token: int, pos: int | None = None, stream=None) -> None:
+        """Seed the state to decode `token` at `pos` (default: the first free KV row)."""
+        pos = self.cfg.context if pos is None else pos
+        host = torch.frombuffer(bytearray(state_bytes(token, pos)), dtype=torch.uint8)
+        self.b.state.copy_(host, non_blocking=False)
+
+    def read_state(self) -> dict:
+        return parse_state(bytes(self.b.state.cpu().numpy().tobytes()))
+
+    # -- one step -----------------------------------------------------------
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def step(self) -> None:
+        """Launch one decode step on the current stream."""
+        cfg, w, b, L = self.cfg, self.w, self.b, lib()
+        s, fl = self._stream(), self.flags
+        P = lambda t: t.data_ptr()  # noqa: E731
+        state = P(b.state)
+        check(L.mllb_decode_embed(P(w.embedding), cfg.vocab, cfg.hidden, state, P(b.tokens), cfg.new_tokens,
+                                  P(b.hidden), fl, s), "decode_embed")
+        ffn_local = w.ffn_shard.local_rows
+        for layer, lw in enumerate(w.layers):
+            delta = None if layer == 0 else P(b.down_out)
+            check(L.mllb_rmsnorm_q8_1(P(b.hidden), delta, P(b.hidden), P(lw.attn_norm), cfg.eps, P(b.q8_hidden),
+                                      cfg.hidden, 0, fl, s), "attn_norm")
+            check(L.mllb_q4k_matvec_ex(P(lw.qkv), P(b.q8_hidden), P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s),
+                  "qkv")
+            check(L.mllb_decode_qk_rope_append(P(b.qkv), P(lw.q_norm), P(lw.k_norm), state, cfg.theta_scale,
+                                               P(b.q_rot), P(self.k_cache[layer]), P(self.v_cache[layer]),
+                                               cfg.q_heads, cfg.kv_heads, cfg.ctx_capacity, fl, s), "qk_rope")
+            check(L.mllb_decode_attention(P(b.q_rot), P(self.k_cache[layer]), P(self.v_cache[layer]), state,
+                                          P(b.scratch), b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads,
+                                          cfg.kv_heads, cfg.ctx_capacity, fl, s), "attention")
+            check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
+            check(L.mllb_rmsnorm_q8_1(P(b.hidden), P(b.o_out), P(b.hidden), P(lw.ffn_norm), cfg.eps,
+                                      P(b.q8_hidden), cfg.hidden, 0, fl, s), "ffn_norm")
+            check(L.mllb_q4k_gate_up_ex(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod), ffn_local,
+                                        cfg.hidden, fl, s), "gate_up")
+            if self.world == 1:
+                check(L.mllb_q8_1_quantize_ex(P(b.prod), P(b.q8_prod), cfg.ffn, 0, fl, s), "quantize prod")
+            else:
+                self._gather_prod(s, fl)
+            check(L.mllb_q4k_matvec_ex(P(lw.down), P(b.q8_prod), P(b.down_out), cfg.hidden, cfg.ffn, fl, s),
+                  "down")
+        check(L.mllb_decode_final_norm(P(b.hidden), P(b.down_out), P(b.hidden), P(w.out_norm), cfg.eps,
+                                       P(b.q8_hidden), cfg.hidden, state, fl, s), "final_norm")
+        check(L.mllb_q6k_matvec_ex(P(w.output), P(b.q8_hidden), P(b.logits), w.vocab_shard.local_rows, cfg.hidden,
+                                   fl, s), "logits")
+        if self.world == 1:
+            check(L.mllb_argmax_f32(P(b.logits), cfg.vocab, 0, state, fl, s), "argmax")
+        else:
+            self._reduce_argmax(s, fl)
+
+    # -- sharded pieces -----------------------------------------------------
+    def _gather_prod(self, s: int, fl: int) -> None:
+        import torch.distributed as dist
+
+        b, L, shard = self.b, lib(), self.w.ffn_shard
+        local = b.extra.get("q8_prod_local")
+        if local is None:
+            local = b.extra["q8_prod_local"] = torch.zeros(shard.per_rank // 32 * 36, dtype=torch.uint8,
+                                                           device=self.device)
+        check(L.mllb_q8_1_quantize_ex(b.prod.data_ptr(), local.data_ptr(), shard.per_rank, 0, fl, s),
+              "quantize prod shard")
+        dist.all_gather_into_tensor(b.q8_prod, local, group=self.group)
+
+    def _reduce_argmax(self, s: int, fl: int) -> None:
+        import torch.distributed as dist
+
+        b, L, shard = self.b, lib(), self.w.vocab_shard
+        # The final norm reset the key in the state; each rank folds in its
+        # rows, then MAX over ranks leaves the global (value, lowest index).
+        key = b.state[:8].view(torch.int64)
+        check(L.mllb_argmax_f32(b.logits.data_ptr(), shard.local_rows, shard.start, key.data_ptr(), fl, s),
+              "argmax shard")
+        dist.all_reduce(key, op=dist.ReduceOp.MAX, group=self.group)
+
+    # -- graphs -------------------------------------------------------------
+    def capture(self) -> torch.cuda.CUDAGraph:
+        """Record one step into a CUDA graph on the current (non-default)
+        stream.  One eager step runs first, so that every kernel's launch
+        attributes are set outside the capture; it leaves the KV row at the
+        state's position written, which the first replay rewrites, and the
+        state is restored afterwards."""
+        stream = torch.cuda.current_stream(self.device)
+        if stream == torch.cuda.default_stream(self.device):
+            raise RuntimeError("capture on a non-default stream (torch.cuda.stream(...))")
+        saved = self.b.state.clone()
+        self.step()
+        self.b.state.copy_(saved)
+        stream.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            self.step()
+        self.graph = g
+        return g
+
+    def replay(self) -> None:
+        if self.graph is None:
+            raise RuntimeError("capture() first")
+        self.graph.replay()
+
+    def generate(self, token: int, n: int, pos: int | None = None) -> list[int]:
+        """Decode n tokens greedily after `token` (public API; H2D of the seed
+        state, D2H of the tokens).  Uses the captured graph when there is one."""
+        if n > self.cfg.new_tokens:
+            raise ValueError("n exceeds the KV capacity reserved for new tokens")
+        self.reset(token, pos)
+        for _ in range(n):
+            self.replay() if self.graph is not None else self.step()
+        st = self.read_state()
+        seen = self.b.tokens[:n].cpu().tolist()
+        return seen[1:] + [st["next_token"]]

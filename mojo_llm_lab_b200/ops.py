@@ -28,7 +28,8 @@ from ._lib import LAUNCH_PDL, S_D_SUMQ, S_SUM_X, check, device_error, lib  # noq
 __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
     "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
-    "S_D_SUMQ", "S_SUM_X",
+    "rmsnorm_q8_1", "decode_embed", "decode_final_norm", "decode_qk_rope_append", "decode_attention",
+    "argmax_key", "token_key", "key_token", "S_D_SUMQ", "S_SUM_X",
 ]
 
 
@@ -241,3 +242,148 @@ def stream_read(data: torch.Tensor, out: torch.Tensor | None = None, blocks: int
     check(lib().mllb_stream_read(data.data_ptr(), data.numel(), out.data_ptr(), blocks, _stream(data)),
           "stream_read")
     return out
+
+
+# ------------------------------------------------------------------ decode
+# The ops of one decode step around the matvecs (mojo_llm_lab_b200.decode
+# chains them).  `state` is the 32-byte mllb_decode_state as a uint8 tensor.
+
+def _flags(pdl: bool) -> int:
+    return LAUNCH_PDL if pdl else 0
+
+
+def _ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def token_key(token: int) -> int:
+    """Packed next-token key that selects `token`."""
+    return int(lib().mllb_token_key(token))
+
+
+def key_token(key: int) -> int:
+    """Token index of a packed key (-1 for the empty key INT64_MIN)."""
+    return int(lib().mllb_key_token(key))
+
+
+def _need_state(state: torch.Tensor) -> None:
+    _need(state, "state", torch.uint8)
+    if state.numel() != 32:
+        raise ValueError("state must be the 32-byte mllb_decode_state")
+
+
+def rmsnorm_q8_1(x: torch.Tensor, gamma: torch.Tensor, delta: torch.Tensor | None = None,
+                 x_out: torch.Tensor | None = None, q8: torch.Tensor | None = None, eps: float = 1e-6,
+                 s_mode: int = S_D_SUMQ, pdl: bool = False) -> torch.Tensor:
+    """q8 = Q8_1(fp32(h * rsqrt(mean(h^2) + eps) * gamma)), h = x + delta (stored to x_out)."""
+    for name, t in (("x", x), ("gamma", gamma), ("delta", delta), ("x_out", x_out)):
+        if t is not None:
+            _need(t, name, torch.float32)
+            if t.numel() != x.numel():
+                raise ValueError(f"{name} must have {x.numel()} values")
+    k = x.numel()
+    if q8 is None:
+        q8 = torch.empty(F.q8_1_bytes(k), dtype=torch.uint8, device=x.device)
+    _need(q8, "q8", torch.uint8)
+    _same_device(x, gamma, delta, x_out, q8)
+    check(lib().mllb_rmsnorm_q8_1(x.data_ptr(), _ptr(delta), _ptr(x_out), gamma.data_ptr(), eps, q8.data_ptr(), k,
+                                  s_mode, _flags(pdl), _stream(x)), "rmsnorm_q8_1")
+    return q8
+
+
+def decode_final_norm(x: torch.Tensor, gamma: torch.Tensor, state: torch.Tensor, delta: torch.Tensor | None = None,
+                      x_out: torch.Tensor | None = None, q8: torch.Tensor | None = None, eps: float = 1e-6,
+                      pdl: bool = False) -> torch.Tensor:
+    """rmsnorm_q8_1 that also resets the next-token key and advances pos / steps."""
+    _need_state(state)
+    k = x.numel()
+    if q8 is None:
+        q8 = torch.empty(F.q8_1_bytes(k), dtype=torch.uint8, device=x.device)
+    _same_device(x, gamma, delta, x_out, q8, state)
+    check(lib().mllb_decode_final_norm(x.data_ptr(), _ptr(delta), _ptr(x_out), gamma.data_ptr(), eps, q8.data_ptr(),
+                                       k, state.data_ptr(), _flags(pdl), _stream(x)), "decode_final_norm")
+    return q8
+
+
+def decode_embed(q6k_weights: torch.Tensor, vocab: int, state: torch.Tensor, hidden: torch.Tensor,
+                 tokens: torch.Tensor | None = None, pdl: bool = False) -> torch.Tensor:
+    """hidden = dequantised row (token of the state's key) of the Q6_K matrix."""
+    _need(q6k_weights, "q6k_weights", torch.uint8)
+    _need(hidden, "hidden", torch.float32)
+    _need_state(state)
+    k = hidden.numel()
+    if q6k_weights.numel() != vocab * F.q6k_row_bytes(k):
+        raise ValueError("Q6_K matrix size does not match vocab x hidden")
+    if tokens is not None:
+        _need(tokens, "tokens", torch.int32)
+    _same_device(q6k_weights, state, hidden, tokens)
+    check(lib().mllb_decode_embed(q6k_weights.data_ptr(), vocab, k, state.data_ptr(), _ptr(tokens),
+                                  0 if tokens is None else tokens.numel(), hidden.data_ptr(), _flags(pdl),
+                                  _stream(hidden)), "decode_embed")
+    return hidden
+
+
+def decode_qk_rope_append(qkv: torch.Tensor, q_gamma: torch.Tensor, k_gamma: torch.Tensor, state: torch.Tensor,
+                          k_cache: torch.Tensor, v_cache: torch.Tensor, q_heads: int, kv_heads: int,
+                          theta_scale: float | None = None, q_out: torch.Tensor | None = None,
+                          pdl: bool = False) -> torch.Tensor:
+    """q/k RMSNorm + gamma + IMROPE at state.pos; K, V appended to the fp16 caches [kv_heads, ctx, 128]."""
+    _need(qkv, "qkv", torch.float32)
+    _need(q_gamma, "q_gamma", torch.float32)
+    _need(k_gamma, "k_gamma", torch.float32)
+    _need(k_cache, "k_cache", torch.float16)
+    _need(v_cache, "v_cache", torch.float16)
+    _need_state(state)
+    if qkv.numel() != (q_heads + 2 * kv_heads) * F.HEAD_DIM:
+        raise ValueError("qkv must hold (q_heads + 2 kv_heads) x 128 values")
+    if k_cache.dim() != 3 or k_cache.shape[0] != kv_heads or k_cache.shape[2] != F.HEAD_DIM:
+        raise ValueError("caches must be [kv_heads, ctx, 128]")
+    if v_cache.shape != k_cache.shape:
+        raise ValueError("v_cache must match k_cache")
+    if q_out is None:
+        q_out = torch.empty(q_heads * F.HEAD_DIM, dtype=torch.float32, device=qkv.device)
+    theta = F.theta_scale_f32() if theta_scale is None else float(theta_scale)
+    _same_device(qkv, q_gamma, k_gamma, state, k_cache, v_cache, q_out)
+    check(lib().mllb_decode_qk_rope_append(qkv.data_ptr(), q_gamma.data_ptr(), k_gamma.data_ptr(), state.data_ptr(),
+                                           theta, q_out.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), q_heads,
+                                           kv_heads, k_cache.shape[1], _flags(pdl), _stream(qkv)),
+          "decode_qk_rope_append")
+    return q_out
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor, state: torch.Tensor,
+                     out: torch.Tensor | None = None, q8: torch.Tensor | None = None,
+                     scratch: torch.Tensor | None = None, pdl: bool = False):
+    """Attention of the token at state.pos over cache rows 0..pos -> (out fp32, Q8_1 of out)."""
+    _need(q, "q", torch.float32)
+    _need(k_cache, "k_cache", torch.float16)
+    _need(v_cache, "v_cache", torch.float16)
+    _need_state(state)
+    kv_heads, ctx = k_cache.shape[0], k_cache.shape[1]
+    q_heads = q.numel() // F.HEAD_DIM
+    with torch.cuda.device(q.device):
+        need = int(lib().mllb_decode_attention_scratch(q_heads, kv_heads, ctx))
+    if need < 0:
+        check(int(need), "decode_attention_scratch")
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.float64, device=q.device)
+    _need(scratch, "scratch", torch.float64)
+    if out is None:
+        out = torch.empty(q.numel(), dtype=torch.float32, device=q.device)
+    if q8 is None:
+        q8 = torch.empty(F.q8_1_bytes(q.numel()), dtype=torch.uint8, device=q.device)
+    _same_device(q, k_cache, v_cache, state, out, q8, scratch)
+    check(lib().mllb_decode_attention(q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), state.data_ptr(),
+                                      scratch.data_ptr(), scratch.numel(), out.data_ptr(), q8.data_ptr(), q_heads,
+                                      kv_heads, ctx, _flags(pdl), _stream(q)), "decode_attention")
+    return out, q8
+
+
+def argmax_key(x: torch.Tensor, key: torch.Tensor, index_offset: int = 0, pdl: bool = False) -> torch.Tensor:
+    """key[0] = max(key[0], packed (x[i], index_offset + i) over i); key: int64[1]."""
+    _need(x, "x", torch.float32)
+    _need(key, "key", torch.int64)
+    _same_device(x, key)
+    check(lib().mllb_argmax_f32(x.data_ptr(), x.numel(), index_offset, key.data_ptr(), _flags(pdl), _stream(x)),
+          "argmax")
+    return key

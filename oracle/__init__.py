@@ -78,6 +78,11 @@ def lib() -> C.CDLL:
             "orc_imrope": (C.c_int, [P, P, P, C.c_double, C.c_int, P]),
             "orc_reference_theta_scale": (C.c_double, []),
             "orc_rmsnorm": (C.c_int, [P, P, i64, C.c_double, P]),
+            "orc_embed_q6k": (C.c_int, [P, i64, i64, P]),
+            "orc_rmsnorm_q8_1": (C.c_int, [P, P, i64, P, C.c_double, P, P]),
+            "orc_qk_rope_append": (C.c_int, [P, C.c_int, C.c_int, P, P, C.c_int32, C.c_double, P, P, P]),
+            "orc_attention": (C.c_int, [P, P, P, i64, i64, C.c_int, C.c_int, P, C.c_int]),
+            "orc_argmax": (i64, [P, i64]),
             "orc_version": (C.c_int, []),
         }
         for name, (res, args) in sigs.items():
@@ -249,3 +254,60 @@ def rmsnorm(x, gamma, eps: float = 1e-6) -> np.ndarray:
     out = np.zeros(x.size, dtype=np.float64)
     _check(lib().orc_rmsnorm(_ptr(x), _ptr(gamma), x.size, eps, _ptr(out)), "rmsnorm")
     return out
+
+
+# ------------------------------------------------------------ decode step
+
+def _f32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.float32).reshape(-1))
+
+
+def embed_q6k(weights, k: int, token: int) -> np.ndarray:
+    """Row ``token`` of a Q6_K matrix, dequantised to fp32."""
+    w = _bytes(weights)
+    out = np.empty(k, dtype=np.float32)
+    _check(lib().orc_embed_q6k(_ptr(w), k, token, _ptr(out)), "embed_q6k")
+    return out
+
+
+def rmsnorm_q8_1(x, delta, gamma, eps: float = 1e-6):
+    """(h, q8): h = x + delta in fp32, q8 = Q8_1(fp32(h * rsqrt(mean h^2 + eps) * gamma))."""
+    x = _f32(x)
+    g = _f32(gamma)
+    d = None if delta is None else _f32(delta)
+    h = np.empty_like(x)
+    q8 = np.empty(x.size // 32 * 36, dtype=np.uint8)
+    _check(lib().orc_rmsnorm_q8_1(_ptr(x), None if d is None else _ptr(d), x.size, _ptr(g), eps, _ptr(h), _ptr(q8)),
+           "rmsnorm_q8_1")
+    return h, q8
+
+
+def qk_rope_append(qkv, q_heads: int, kv_heads: int, q_gamma, k_gamma, pos: int, theta_scale: float):
+    """(q_out fp32, k_row fp16 bits, v_row fp16 bits) of one token's fused QKV output."""
+    qkv = _f32(qkv)
+    q_out = np.empty(q_heads * HEAD_DIM, dtype=np.float32)
+    k_row = np.empty(kv_heads * HEAD_DIM, dtype=np.uint16)
+    v_row = np.empty(kv_heads * HEAD_DIM, dtype=np.uint16)
+    qg, kg = _f32(q_gamma), _f32(k_gamma)
+    _check(lib().orc_qk_rope_append(_ptr(qkv), q_heads, kv_heads, _ptr(qg), _ptr(kg), pos, theta_scale,
+                                    _ptr(q_out), _ptr(k_row), _ptr(v_row)), "qk_rope_append")
+    return q_out, k_row, v_row
+
+
+def attention(q, k_cache: np.ndarray, v_cache: np.ndarray, n: int, q_heads: int, kv_heads: int,
+              threads: int = 0) -> np.ndarray:
+    """Grouped-query softmax attention over cache rows [0, n); caches fp16 bits [kv][ctx][128]."""
+    q = _f32(q)
+    assert k_cache.dtype == np.uint16 and v_cache.dtype == np.uint16
+    assert k_cache.flags.c_contiguous and v_cache.flags.c_contiguous
+    ctx = k_cache.shape[-2]
+    out = np.empty(q_heads * HEAD_DIM, dtype=np.float32)
+    _check(lib().orc_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), ctx, n, q_heads, kv_heads, _ptr(out),
+                               threads), "attention")
+    return out
+
+
+def argmax(x) -> int:
+    """Index of the first maximum."""
+    x = _f32(x)
+    return int(lib().orc_argmax(_ptr(x), x.size))
