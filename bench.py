@@ -17,6 +17,15 @@ host memory, quantised on the device, and the outputs copied back.
 oracle in oracle/, OpenMP over all host threads) on a bounded sample of the
 same workload.  Multi-GPU (torchrun): this matvec is a "stay on one GPU" op,
 so N ranks run N independent replicas (weak scaling, no collective).
+
+--workload decode: the 36-layer synthetic Qwen3-style decode (hidden 2560,
+32/8 heads of 128, SwiGLU 9728, vocab 151936; Q4_K layers, Q6_K output; fp16
+KV cache prefilled with N(0, 1) at context 4096).  One step = 128 greedy
+tokens from the prefilled context (the state reset on the device at the
+start of the step), replaying one captured CUDA graph per token.  Metric:
+tokens/s of the whole job; with N ranks the gate/up and vocabulary matvecs
+are row-sharded (NCCL all-gather / all-reduce) and every rank decodes the
+same token stream (strong scaling).
 """
 from __future__ import annotations
 
@@ -47,6 +56,9 @@ WORKLOADS = {
     "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,8,6>",
                       profile="q6k_vocab_n151936_k2560"),
 }
+
+
+DECODE = dict(kind="decode", profile="decode_36layer_ctx4096")
 
 
 def weight_bytes(kind: str, rows: int, k: int) -> int:
@@ -433,13 +445,216 @@ def run_ours(args, rank: int, world: int):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- decode workload
+
+DECODE_TOKENS = 128
+
+
+def decode_cpu_reference(target_s: float = 15.0):
+    """Time the oracle's decode step (oracle/decode.py over oracle/oracle.c, OpenMP over all
+    host threads) on the 36-layer stack: whole tokens from the prefilled context."""
+    import torch
+
+    from mojo_llm_lab_b200 import decode as D
+    from oracle import decode as OD
+
+    cfg = D.DecodeConfig()
+    # Data preparation only (torch's CPU generator takes ~30 s for 2.4 GB).
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    w = D.generate_weights(cfg, dev)
+    k, v = D.generate_kv_cache(cfg, dev)
+    host = OD.host_model(w)
+    kh, vh = k.cpu().numpy().view(np.uint16).copy(), v.cpu().numpy().view(np.uint16).copy()
+    del w, k, v
+    threads = os.cpu_count() or 1
+    token, pos, n, t0 = 17, cfg.context, 0, time.perf_counter()
+    while True:
+        _, token = OD.reference_step(host, kh, vh, token, pos, threads)
+        pos, n = pos + 1, n + 1
+        el = time.perf_counter() - t0
+        if el >= target_s or pos >= cfg.ctx_capacity:
+            break
+    del torch
+    return {"value": n / el, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "sample": f"{n} greedy tokens of the 36-layer stack from context 4096 in {el:.1f} s "
+                      f"(oracle/decode.py + oracle/oracle.c, OpenMP {threads} threads, float64)",
+            "seconds_per_token": el / n}
+
+
+def run_decode_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    ref = decode_cpu_reference(target_s=max(5.0, min(30.0, 2.0 * args.steps)))
+    line = {"metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(ref["value"], 4),
+            "unit": "tokens/s", "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ref["seconds_per_token"] * DECODE_TOKENS * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
+            "config": {"workload": "36-layer Qwen3-style decode, ctx 4096, 128 greedy tokens"},
+            "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(ref["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_decode(args, rank: int, world: int):
+    import torch
+    import torch.distributed as dist
+
+    from mojo_llm_lab_b200 import decode as D
+    from mojo_llm_lab_b200 import ops
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    cfg = D.DecodeConfig()
+    group = dist.group.WORLD if world > 1 else None
+    weights = D.generate_weights(cfg, device, world=world, rank=rank)
+    k_cache, v_cache = D.generate_kv_cache(cfg, device)
+    stream = torch.cuda.Stream(device)
+    stream.wait_stream(torch.cuda.current_stream(device))
+    torch.cuda.set_stream(stream)
+    dec = D.Decoder(weights, k_cache, v_cache, pdl=not args.no_pdl, fused=args.fused, group=group)
+    start_token = 17
+
+    # Correctness gate: the first token's full logits against the oracle
+    # (rank 0; the logit shards are gathered first).
+    dec.reset(start_token)
+    dec.step()
+    torch.cuda.synchronize()
+    if world > 1:
+        logits = torch.empty(weights.vocab_shard.per_rank * world, dtype=torch.float32, device=device)
+        dist.all_gather_into_tensor(logits, dec.b.logits)
+        logits = logits[:cfg.vocab]
+    else:
+        logits = dec.b.logits
+    agreement = None
+    if rank == 0 and not args.skip_check:
+        from oracle import decode as OD
+        full = weights if world == 1 else D.generate_weights(cfg, device)
+        host = OD.host_model(full)
+        del full
+        kh0, vh0 = D.generate_kv_cache(cfg, device)
+        kh = kh0.cpu().numpy().view(np.uint16).copy()
+        vh = vh0.cpu().numpy().view(np.uint16).copy()
+        del kh0, vh0
+        ref, ref_next = OD.reference_step(host, kh, vh, start_token, cfg.context)
+        agreement = OD.logit_agreement(ref, logits.cpu().numpy())
+        if agreement["violations"] or not agreement["top_match"]:
+            raise SystemExit(f"decode correctness gate failed: {agreement}")
+        if dec.read_state()["next_token"] != ref_next:
+            raise SystemExit("decode correctness gate failed: next token differs from the oracle")
+        del host, kh, vh
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+
+    # One graph per token; a step = reset (device-to-device copy of the seed
+    # state) + 128 replays.
+    dec.reset(start_token)
+    seed = dec.b.state.clone()
+    dec.capture()
+    if world > 1:
+        dist.barrier()
+
+    def step():
+        dec.b.state.copy_(seed, non_blocking=True)
+        for _ in range(DECODE_TOKENS):
+            dec.replay()
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            step()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = DECODE_TOKENS / (ms * 1e-3)
+
+    # e2e through the public API: Decoder.generate (H2D of the seed state,
+    # 128 graph replays, D2H of the generated tokens).
+    e_ms_all = []
+    tokens = None
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        tokens = dec.generate(start_token, DECODE_TOKENS)
+        if i >= args.warmup:
+            e_ms_all.append((time.perf_counter() - t0) * 1e3)
+    e_ms = statistics.median(e_ms_all)
+    if world > 1:
+        t = torch.tensor([e_ms], device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
+    derr = ops.device_error()
+    if derr:
+        raise SystemExit(f"device error word set: {derr:#x}")
+    if world > 1:
+        toks = torch.tensor(tokens, device=device)
+        allt = torch.empty(world, len(tokens), dtype=toks.dtype, device=device)
+        dist.all_gather_into_tensor(allt, toks)
+        if not bool((allt == allt[0]).all()):
+            raise SystemExit("ranks decoded different token streams")
+    launches = dec.launches_per_step()
+    dec.graph = None
+    if world > 1:
+        dist.barrier()
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        mean_keys = cfg.context + (DECODE_TOKENS + 1) / 2
+        rank_bytes = (cfg.q4k_bytes() - 2 * cfg.layers * (cfg.ffn - weights.ffn_shard.local_rows) * cfg.hidden
+                      // 256 * 144 + weights.vocab_shard.local_rows * cfg.hidden // 256 * 210
+                      + cfg.kv_bytes_read(int(mean_keys)))
+        us_per_token = ms * 1e3 / DECODE_TOKENS
+        achieved = rank_bytes / (us_per_token * 1e-6) / 1e9
+        cpu = None if args.no_cpu_baseline or world > 1 else decode_cpu_reference(target_s=10.0)
+        line = {
+            "metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "Q4_K/Q6_K x Q8_1 dp4a, f64 accumulate; fp16 KV, f64 attention",
+            "data": "synthetic (seeded random weights, N(0,1) KV prefill)",
+            "config": {"workload": "36-layer Qwen3-style decode (hidden 2560, 32/8 heads x 128, SwiGLU 9728, "
+                                   "vocab 151936), ctx 4096, 128 greedy tokens per step",
+                       "us_per_token": round(us_per_token, 3), "bytes_per_token_per_gpu": int(rank_bytes),
+                       "parallelism": (f"gate/up + vocab rows/{world} per rank, NCCL" if world > 1 else "single GPU"),
+                       "l2": "2.4 GB of weights per token > L2; no flush", "pdl": not args.no_pdl,
+                       "fused_activations": dec.fused,
+                       "logit_agreement": agreement},
+            "e2e": {"value": round(DECODE_TOKENS / (e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 32,
+                    "d2h_bytes_per_step": 32 + DECODE_TOKENS * 4, "ms_per_step": round(e_ms, 4),
+                    "path": "Decoder.generate (C-ABI launches captured in a CUDA graph), host seed state in, tokens out"},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+                         "kernel": "whole decode step (algorithmic bytes: weights + KV rows read, per GPU)",
+                         "us_per_launch": round(us_per_token / launches, 4)},
+            "cpu_baseline": None if cpu is None else {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * DECODE_TOKENS * launches,
+        }
+        print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="q4k_matvec")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode"], default="q4k_matvec")
+    ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
     ap.add_argument("--copies", type=int, default=0)
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
@@ -451,8 +666,12 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":
-        run_reference(args, rank, world)
+        if args.workload == "decode":
+            run_decode_reference(args, rank, world)
+        else:
+            run_reference(args, rank, world)
         return
+    runner = run_decode if args.workload == "decode" else run_ours
     if world > 1:
         import datetime
 
@@ -462,11 +681,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         try:
-            run_ours(args, rank, world)
+            runner(args, rank, world)
         finally:
             dist.destroy_process_group()
     else:
-        run_ours(args, rank, world)
+        runner(args, rank, world)
 
 
 if __name__ == "__main__":

@@ -183,6 +183,37 @@ typedef struct mllb_decode_state {
     int32_t reserved[3];
 } mllb_decode_state;
 
+/*
+ * An activation produced inside a streaming matvec from fp32, instead of a
+ * Q8_1 buffer written by a kernel before it:
+ *   h = x + delta (fp32; delta may be NULL), stored to x_out when not NULL
+ *   (x_out must not overlap x or delta);
+ *   y = gamma ? fp32(h / sqrt(mean(h^2) + eps) * gamma) : h;
+ *   activation = Q8_1(y) with s = d * sum(q) -- the bytes mllb_rmsnorm_q8_1
+ *   (or mllb_q8_1_quantize) would write, built by every CTA for itself.
+ * advance (may be NULL): the step's final norm -- reset next_token_key and
+ * advance pos and steps as mllb_decode_final_norm does.
+ */
+typedef struct mllb_act_f32 {
+    const float *x;
+    const float *delta;
+    const float *gamma;
+    float *x_out;
+    double eps;
+    mllb_decode_state *advance;
+} mllb_act_f32;
+
+/* The streaming matvecs with that activation (K/256 in {8, 10, 16, 38} for
+ * Q4_K, {8, 10, 16} for gate/up and Q6_K; Q6_K rows a multiple of 8;
+ * MLLB_EUNSUPPORTED otherwise).  One kernel instead of two per matvec.  The
+ * host struct is read during the call only. */
+int mllb_q4k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out, int64_t n, int64_t k,
+                        unsigned flags, void *stream);
+int mllb_q4k_gate_up_act(const void *up_weights, const void *gate_weights, const mllb_act_f32 *act, float *up,
+                         float *gate, float *prod, int64_t n, int64_t k, unsigned flags, void *stream);
+int mllb_q6k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out, int64_t n, int64_t k,
+                        unsigned flags, void *stream);
+
 /* Host helpers for the packed next-token key: high 32 bits order the fp32
  * value, low 32 bits are 0xffffffff - index (ties go to the lower index).
  * mllb_token_key(t) is a key that selects token t (to seed a decode loop);
@@ -203,9 +234,12 @@ int mllb_decode_embed(const void *q6k_weights, int64_t vocab, int64_t k, mllb_de
 
 /*
  * Residual + RMSNorm + gamma + Q8_1 in one kernel:
- *   h = x + delta (fp32; delta may be NULL), stored to x_out when not NULL
- *   (x_out may equal x);  y = fp32(h / sqrt(mean(h^2) + eps) * gamma);
+ *   h = x + delta (fp32; delta may be NULL), stored to x_out when not NULL;
+ *   y = fp32(h / sqrt(mean(h^2) + eps) * gamma);
  *   q8 = Q8_1(y) (s_mode as mllb_q8_1_quantize).  k: multiple of 32, <= 32768.
+ * x_out may be x itself (in place; then one CTA does all the work) but must
+ * not otherwise overlap x or delta.  A separate x_out spreads the blocks over
+ * k/256 CTAs.
  * GGML add -> rms_norm -> mul -> quantize_q8_1 (benchmark/q4_compare.c:328-330
  * is the quantise node this absorbs).
  */
@@ -249,6 +283,19 @@ int64_t mllb_decode_attention_scratch(int64_t q_heads, int64_t kv_heads, int64_t
 int mllb_decode_attention(const float *q, const void *k_cache, const void *v_cache, const mllb_decode_state *state,
                           double *scratch, int64_t scratch_doubles, float *out, void *q8, int64_t q_heads,
                           int64_t kv_heads, int64_t ctx, unsigned flags, void *stream);
+
+/*
+ * Fused form for the decode step: qkv is the raw fused QKV projection (as
+ * mllb_decode_qk_rope_append takes it).  The kernel does the q-head RMSNorm
+ * + q_gamma + IMROPE itself, appends the K row (RMSNorm + k_gamma + IMROPE,
+ * fp16) and the V row (fp16) at state->pos, and attends as
+ * mllb_decode_attention -- one launch fewer, the same numbers.  pos outside
+ * [0, ctx) sets device error bit 16 and appends nothing.
+ */
+int mllb_decode_attention_qkv(const float *qkv, const float *q_gamma, const float *k_gamma, double theta_scale,
+                              const mllb_decode_state *state, void *k_cache, void *v_cache, double *scratch,
+                              int64_t scratch_doubles, float *out, void *q8, int64_t q_heads, int64_t kv_heads,
+                              int64_t ctx, unsigned flags, void *stream);
 
 /*
  * *key = max(*key, max over i of key(x[i], index_offset + i)) with the packed

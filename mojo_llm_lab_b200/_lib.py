@@ -29,6 +29,15 @@ S_SUM_X = 1
 _P = C.c_void_p
 _I64 = C.c_int64
 
+
+class ActF32(C.Structure):
+    """mllb_act_f32 of include/mllb200.h (an activation built in the kernel)."""
+    _fields_ = [("x", C.c_void_p), ("delta", C.c_void_p), ("gamma", C.c_void_p), ("x_out", C.c_void_p),
+                ("eps", C.c_double), ("advance", C.c_void_p)]
+
+
+_ACT = C.POINTER(ActF32)
+
 SIGNATURES = {
     "mllb_abi_version": (C.c_int, []),
     "mllb_last_error": (C.c_char_p, []),
@@ -54,7 +63,12 @@ SIGNATURES = {
                                              _P]),
     "mllb_decode_attention_scratch": (_I64, [_I64, _I64, _I64]),
     "mllb_decode_attention": (C.c_int, [_P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, C.c_uint, _P]),
+    "mllb_decode_attention_qkv": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64,
+                                            C.c_uint, _P]),
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
+    "mllb_q4k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q6k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
 }
 
 _lock = threading.Lock()

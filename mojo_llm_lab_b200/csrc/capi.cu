@@ -176,8 +176,8 @@ int grid_cap(int dev, int grid, int per_sm) {
 }
 
 template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
-int launch_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2, int n,
-                cudaStream_t stream, bool pdl) {
+int launch_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1, float* o2,
+                int n, cudaStream_t stream, bool pdl) {
   using C = mllb::TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
   int dev, grid, per_sm, rc;
   if ((rc = current_device(&dev))) return rc;
@@ -185,7 +185,7 @@ int launch_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* 
   const int tiles = (n + C::kT - 1) / C::kT;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, tiles, &grid, &per_sm))) return rc;
   grid = grid_cap(dev, grid, per_sm);
-  return launched(launch(kernel, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, pdl, w0, w1, q8, o0, o1, o2,
+  return launched(launch(kernel, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, pdl, w0, w1, src, o0, o1, o2,
                          n, pdl ? 1 : 0),
                   "streaming matvec kernel");
 }
@@ -197,31 +197,82 @@ int check_rows(int64_t n, int64_t k, int64_t max_rows) {
   return MLLB_OK;
 }
 
-int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
-                 int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
+mllb::ActSource q8_source(const uint8_t* q8) {
+  mllb::ActSource src = {};
+  src.q8 = q8;
+  return src;
+}
+
+// Streaming Q4_K launch for the shapes with a team configuration; returns
+// MLLB_EUNSUPPORTED (and launches nothing) for the others.
+int q4k_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1, float* o2,
+             int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
   using F = mllb::Q4kFormat;
   const int nb = static_cast<int>(k / 256);
   const int rows = static_cast<int>(n);
   if (w1 == nullptr) {
     switch (nb) {
-      case 8: return launch_team<F, 8, 1, MLLB_CFG_Q4K_8>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-      case 10: return launch_team<F, 10, 1, MLLB_CFG_Q4K_10>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-      case 16: return launch_team<F, 16, 1, MLLB_CFG_Q4K_16>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-      case 38: return launch_team<F, 38, 1, MLLB_CFG_Q4K_38>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 8: return launch_team<F, 8, 1, MLLB_CFG_Q4K_8>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
+      case 10: return launch_team<F, 10, 1, MLLB_CFG_Q4K_10>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
+      case 16: return launch_team<F, 16, 1, MLLB_CFG_Q4K_16>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
+      case 38: return launch_team<F, 38, 1, MLLB_CFG_Q4K_38>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
       default: break;
     }
   } else {
     switch (nb) {
-      case 8: return launch_team<F, 8, 2, MLLB_CFG_Q4K_DUAL_8>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-      case 10: return launch_team<F, 10, 2, MLLB_CFG_Q4K_DUAL_10>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
-      case 16: return launch_team<F, 16, 2, MLLB_CFG_Q4K_DUAL_16>(w0, w1, q8, o0, o1, o2, rows, stream, pdl);
+      case 8: return launch_team<F, 8, 2, MLLB_CFG_Q4K_DUAL_8>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
+      case 10: return launch_team<F, 10, 2, MLLB_CFG_Q4K_DUAL_10>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
+      case 16: return launch_team<F, 16, 2, MLLB_CFG_Q4K_DUAL_16>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
       default: break;
     }
   }
+  return fail(MLLB_EUNSUPPORTED, "no streaming configuration for K=%lld%s", static_cast<long long>(k),
+              w1 ? " (gate/up)" : "");
+}
+
+int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
+                 int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
+  const int rc = q4k_team(w0, w1, q8_source(q8), o0, o1, o2, n, k, stream, pdl);
+  if (rc != MLLB_EUNSUPPORTED) return rc;
   // The row kernel reads its weights only after the preceding kernel is done,
   // so it never takes the PDL attribute.
-  mllb::q4k_rowblock_kernel<<<rows, 128, 0, stream>>>(w0, w1, q8, o0, o1, o2, nb);
+  mllb::q4k_rowblock_kernel<<<static_cast<int>(n), 128, 0, stream>>>(w0, w1, q8, o0, o1, o2,
+                                                                      static_cast<int>(k / 256));
   return check_launch("q4k row kernel");
+}
+
+// Q6_K streaming launch (rows a multiple of 8); MLLB_EUNSUPPORTED for other K.
+int q6k_team(const uint8_t* w, const mllb::ActSource& src, float* out, int64_t rows, int64_t k, cudaStream_t s,
+             bool pdl) {
+  using F = mllb::Q6kFormat;
+  const int mr = static_cast<int>(rows);
+  switch (k / 256) {
+    case 8: return launch_team<F, 8, 1, MLLB_CFG_Q6K_8>(w, nullptr, src, out, nullptr, nullptr, mr, s, pdl);
+    case 10: return launch_team<F, 10, 1, MLLB_CFG_Q6K_10>(w, nullptr, src, out, nullptr, nullptr, mr, s, pdl);
+    case 16: return launch_team<F, 16, 1, MLLB_CFG_Q6K_16>(w, nullptr, src, out, nullptr, nullptr, mr, s, pdl);
+    default: return fail(MLLB_EUNSUPPORTED, "no Q6_K streaming configuration for K=%lld", static_cast<long long>(k));
+  }
+}
+
+// Validate a host-side mllb_act_f32 and turn it into the kernel's ActSource.
+int act_source(const mllb_act_f32* a, int64_t k, mllb::ActSource* src) {
+  if (!a || !a->x) return fail(MLLB_EINVAL, "null pointer: activation source");
+  if (k > 65536) return fail(MLLB_EUNSUPPORTED, "K=%lld too large for an in-kernel activation", static_cast<long long>(k));
+  if (!aligned(a->x, 4) || !aligned(a->delta, 4) || !aligned(a->gamma, 4) || !aligned(a->x_out, 4) ||
+      !aligned(a->advance, 8))
+    return fail(MLLB_EALIGN, "activation pointers must be 4-byte (state 8-byte) aligned");
+  const auto overlaps = [](const float* p, const float* q, int64_t n) { return p && q && p < q + n && q < p + n; };
+  if (overlaps(a->x_out, a->x, k) || overlaps(a->x_out, a->delta, k))
+    return fail(MLLB_EINVAL, "x_out must not overlap x or delta");
+  if (a->gamma && !(a->eps >= 0.0)) return fail(MLLB_EINVAL, "eps must be >= 0");
+  *src = {};
+  src->x = a->x;
+  src->delta = a->delta;
+  src->gamma = a->gamma;
+  src->x_out = a->x_out;
+  src->eps = a->eps;
+  src->advance = reinterpret_cast<mllb::DecodeState*>(a->advance);
+  return MLLB_OK;
 }
 
 }  // namespace
@@ -332,15 +383,10 @@ int mllb_q6k_matvec_ex(const void* weights, const void* q8, float* out, int64_t 
   const int64_t main_rows = n - n % 8;
   const int64_t tail = n - main_rows;
   if (main_rows > 0) {
-    using F = mllb::Q6kFormat;
-    const int mr = static_cast<int>(main_rows);
-    switch (nb) {
-      case 8: rc = launch_team<F, 8, 1, MLLB_CFG_Q6K_8>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
-      case 10: rc = launch_team<F, 10, 1, MLLB_CFG_Q6K_10>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
-      case 16: rc = launch_team<F, 16, 1, MLLB_CFG_Q6K_16>(w, nullptr, a, out, nullptr, nullptr, mr, s, pdl); break;
-      default:
-        mllb::q6k_rowblock_kernel<<<static_cast<int>(main_rows), 128, 0, s>>>(w, a, out, nb);
-        rc = check_launch("q6k row kernel");
+    rc = q6k_team(w, q8_source(a), out, main_rows, k, s, pdl);
+    if (rc == MLLB_EUNSUPPORTED) {
+      mllb::q6k_rowblock_kernel<<<static_cast<int>(main_rows), 128, 0, s>>>(w, a, out, nb);
+      rc = check_launch("q6k row kernel");
     }
     if (rc) return rc;
   }
@@ -411,14 +457,21 @@ int mllb_stream_read(const void* data, int64_t bytes, void* out, int64_t blocks,
 
 namespace {
 
-constexpr int kAttnMaxChunk = 256;
+constexpr int64_t kAttnMaxSplits = 6144;  // combine weights: 48 KB of shared memory
 
-// Context chunks per KV head: enough CTAs for one per SM, and chunks of at
-// most kAttnMaxChunk keys.
-int64_t attention_splits(int dev, int64_t kv_heads, int64_t ctx) {
-  int64_t base = sm_count(dev) / kv_heads;
+// Context chunks per KV head: enough CTAs to give every SM its resident
+// share, and chunks of at most the kernel's chunk size.
+int64_t attention_splits(int dev, int64_t q_heads, int64_t kv_heads, int64_t ctx) {
+  int per_sm = 1, max_chunk = 128;
+  switch (q_heads / kv_heads) {
+    case 1: per_sm = mllb::AttnConfig<1>::kCtasPerSm; max_chunk = mllb::AttnConfig<1>::kMaxChunk; break;
+    case 2: per_sm = mllb::AttnConfig<2>::kCtasPerSm; max_chunk = mllb::AttnConfig<2>::kMaxChunk; break;
+    case 4: per_sm = mllb::AttnConfig<4>::kCtasPerSm; max_chunk = mllb::AttnConfig<4>::kMaxChunk; break;
+    default: per_sm = mllb::AttnConfig<8>::kCtasPerSm; max_chunk = mllb::AttnConfig<8>::kMaxChunk; break;
+  }
+  int64_t base = static_cast<int64_t>(sm_count(dev)) * per_sm / kv_heads;
   if (base < 1) base = 1;
-  const int64_t need = (ctx + kAttnMaxChunk - 1) / kAttnMaxChunk;
+  const int64_t need = (ctx + max_chunk - 1) / max_chunk;
   return base > need ? base : need;
 }
 
@@ -434,19 +487,72 @@ int check_attention_shape(int64_t q_heads, int64_t kv_heads, int64_t ctx) {
   return MLLB_OK;
 }
 
+struct AttentionArgs {
+  const float* q;        // rotated queries (unfused), or nullptr
+  const float* qkv;      // raw QKV projection (fused), or nullptr
+  const float* q_gamma;
+  const float* k_gamma;
+  double theta;
+  int64_t q_heads, kv_heads, ctx;
+  const mllb::DecodeState* state;
+  uint8_t* k_cache;
+  uint8_t* v_cache;
+  double* part_acc;
+  double* part_ml;
+  int64_t splits;
+};
+
 template <int G>
-int launch_attention(const float* q, const uint8_t* k_cache, const uint8_t* v_cache, const mllb::DecodeState* state,
-                     double* part_acc, double* part_ml, int64_t splits, int64_t kv_heads, int64_t ctx,
-                     cudaStream_t stream, bool pdl) {
+int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
   using C = mllb::AttnConfig<G>;
   int dev, rc, grid, per_sm;
   if ((rc = current_device(&dev))) return rc;
   auto kernel = mllb::attn_split_kernel<G>;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, 1, &grid, &per_sm))) return rc;
-  return launched(launch(kernel, dim3(static_cast<unsigned>(splits), static_cast<unsigned>(kv_heads)),
-                         dim3(C::kThreads), C::kSmemBytes, stream, pdl, q, k_cache, v_cache, state, part_acc, part_ml,
-                         static_cast<int>(ctx), static_cast<int>(splits), 1.0 / sqrt(128.0)),
+  return launched(launch(kernel, dim3(static_cast<unsigned>(a.splits), static_cast<unsigned>(a.kv_heads)),
+                         dim3(C::kThreads), C::kSmemBytes, stream, pdl, a.q, a.qkv, a.q_gamma, a.k_gamma, a.theta,
+                         static_cast<int>(a.q_heads), static_cast<int>(a.kv_heads), a.state, a.k_cache, a.v_cache,
+                         a.part_acc, a.part_ml, static_cast<int>(a.ctx), static_cast<int>(a.splits),
+                         1.0 / sqrt(128.0)),
                   "decode attention kernel");
+}
+
+// Split kernel + combine for both entry points.
+int attention_impl(AttentionArgs a, double* scratch, int64_t scratch_doubles, float* out, void* q8, unsigned flags,
+                   void* stream) {
+  if (!a.k_cache || !a.v_cache || !a.state || !scratch) return fail(MLLB_EINVAL, "null pointer");
+  if (!out && !q8) return fail(MLLB_EINVAL, "no output requested");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_attention_shape(a.q_heads, a.kv_heads, a.ctx);
+  if (rc) return rc;
+  if (!aligned(a.q, 16) || !aligned(a.qkv, 16) || !aligned(a.q_gamma, 4) || !aligned(a.k_gamma, 4) ||
+      !aligned(a.k_cache, 16) || !aligned(a.v_cache, 16) || !aligned(a.state, 8) || !aligned(scratch, 8) ||
+      !aligned(out, 4) || !aligned(q8, 4))
+    return fail(MLLB_EALIGN, "q/qkv and caches need 16-byte, state/scratch 8-byte, others 4-byte alignment");
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  a.splits = attention_splits(dev, a.q_heads, a.kv_heads, a.ctx);
+  const int64_t need = a.q_heads * a.splits * (128 + 2);
+  if (scratch_doubles < need)
+    return fail(MLLB_EINVAL, "scratch holds %lld doubles, %lld needed", static_cast<long long>(scratch_doubles),
+                static_cast<long long>(need));
+  if (a.splits > kAttnMaxSplits) return fail(MLLB_EUNSUPPORTED, "context too long");
+  a.part_acc = scratch;
+  a.part_ml = scratch + a.q_heads * a.splits * 128;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = flags & MLLB_LAUNCH_PDL;
+  switch (a.q_heads / a.kv_heads) {
+    case 1: rc = launch_attention<1>(a, s, pdl); break;
+    case 2: rc = launch_attention<2>(a, s, pdl); break;
+    case 4: rc = launch_attention<4>(a, s, pdl); break;
+    default: rc = launch_attention<8>(a, s, pdl); break;
+  }
+  if (rc) return rc;
+  return launched(launch(mllb::attn_combine_kernel, dim3(static_cast<unsigned>(a.q_heads)), dim3(128),
+                         static_cast<size_t>(a.splits) * sizeof(double), s, pdl,
+                         static_cast<const double*>(a.part_acc), static_cast<const double*>(a.part_ml),
+                         static_cast<int>(a.splits), out, static_cast<uint8_t*>(q8), MLLB_Q8_1_S_D_SUMQ),
+                  "attention combine kernel");
 }
 
 int rmsnorm_q8_1_launch(const float* x, const float* delta, float* x_out, const float* gamma, double eps, void* q8,
@@ -459,11 +565,14 @@ int rmsnorm_q8_1_launch(const float* x, const float* delta, float* x_out, const 
   if (!(eps >= 0.0)) return fail(MLLB_EINVAL, "eps must be >= 0");
   if (!aligned(x, 4) || !aligned(delta, 4) || !aligned(x_out, 4) || !aligned(gamma, 4) || !aligned(q8, 4))
     return fail(MLLB_EALIGN, "fp32 and Q8_1 pointers must be 4-byte aligned");
-  int dev, rc, grid, per_sm;
-  if ((rc = current_device(&dev))) return rc;
-  const int smem = static_cast<int>(k) * 4;
-  if ((rc = stream_grid(mllb::rmsnorm_q8_1_kernel, 32768 * 4, 1024, dev, 1, &grid, &per_sm))) return rc;
-  return launched(launch(mllb::rmsnorm_q8_1_kernel, dim3(1), dim3(1024), smem, static_cast<cudaStream_t>(stream),
+  const auto overlaps = [](const float* a, const float* b, int64_t n) { return a && b && a < b + n && b < a + n; };
+  if (overlaps(x_out, x, k) && x_out != x) return fail(MLLB_EINVAL, "x_out overlaps x without being x");
+  if (overlaps(x_out, delta, k)) return fail(MLLB_EINVAL, "x_out overlaps delta");
+  // In place (x_out == x) one CTA reads every x before any is written;
+  // otherwise one CTA per 8 Q8_1 blocks, each summing all k squares itself.
+  const int64_t blocks = k / 32;
+  const int grid = x_out == x ? 1 : static_cast<int>((blocks + 7) / 8);
+  return launched(launch(mllb::rmsnorm_q8_1_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
                          flags & MLLB_LAUNCH_PDL, x, delta, x_out, gamma, eps, static_cast<uint8_t*>(q8),
                          static_cast<int>(k), s_mode, advance),
                   "rmsnorm q8_1 kernel");
@@ -527,8 +636,8 @@ int mllb_decode_qk_rope_append(const float* qkv, const float* q_gamma, const flo
       !aligned(k_cache, 2) || !aligned(v_cache, 2))
     return fail(MLLB_EALIGN, "fp32 pointers need 4-byte, caches 2-byte, state 8-byte alignment");
   const int64_t warps = q_heads + 2 * kv_heads;
-  const int grid = static_cast<int>((warps + 7) / 8);
-  return launched(launch(mllb::qk_rope_append_kernel, dim3(grid), dim3(256), 0, static_cast<cudaStream_t>(stream),
+  const int grid = static_cast<int>((warps + 3) / 4);
+  return launched(launch(mllb::qk_rope_append_kernel, dim3(grid), dim3(128), 0, static_cast<cudaStream_t>(stream),
                          flags & MLLB_LAUNCH_PDL, qkv, q_gamma, k_gamma,
                          reinterpret_cast<const mllb::DecodeState*>(state), theta_scale, q_out,
                          static_cast<__half*>(k_cache), static_cast<__half*>(v_cache), static_cast<int>(q_heads),
@@ -541,46 +650,43 @@ int64_t mllb_decode_attention_scratch(int64_t q_heads, int64_t kv_heads, int64_t
   if (rc) return rc;
   int dev;
   if ((rc = current_device(&dev))) return rc;
-  return q_heads * attention_splits(dev, kv_heads, ctx) * (128 + 2);
+  return q_heads * attention_splits(dev, q_heads, kv_heads, ctx) * (128 + 2);
 }
 
 int mllb_decode_attention(const float* q, const void* k_cache, const void* v_cache, const mllb_decode_state* state,
                           double* scratch, int64_t scratch_doubles, float* out, void* q8, int64_t q_heads,
                           int64_t kv_heads, int64_t ctx, unsigned flags, void* stream) {
-  if (!q || !k_cache || !v_cache || !state || !scratch) return fail(MLLB_EINVAL, "null pointer");
-  if (!out && !q8) return fail(MLLB_EINVAL, "no output requested");
-  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
-  int rc = check_attention_shape(q_heads, kv_heads, ctx);
-  if (rc) return rc;
-  if (!aligned(q, 16) || !aligned(k_cache, 16) || !aligned(v_cache, 16) || !aligned(state, 8) ||
-      !aligned(scratch, 8) || !aligned(out, 4) || !aligned(q8, 4))
-    return fail(MLLB_EALIGN, "q and caches need 16-byte, state/scratch 8-byte, out/q8 4-byte alignment");
-  int dev;
-  if ((rc = current_device(&dev))) return rc;
-  const int64_t splits = attention_splits(dev, kv_heads, ctx);
-  const int64_t need = q_heads * splits * (128 + 2);
-  if (scratch_doubles < need)
-    return fail(MLLB_EINVAL, "scratch holds %lld doubles, %lld needed", static_cast<long long>(scratch_doubles),
-                static_cast<long long>(need));
-  if (splits > 65535) return fail(MLLB_EUNSUPPORTED, "context too long");
-  double* part_acc = scratch;
-  double* part_ml = scratch + q_heads * splits * 128;
-  const auto* st = reinterpret_cast<const mllb::DecodeState*>(state);
-  const auto* kc = static_cast<const uint8_t*>(k_cache);
-  const auto* vc = static_cast<const uint8_t*>(v_cache);
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool pdl = flags & MLLB_LAUNCH_PDL;
-  switch (q_heads / kv_heads) {
-    case 1: rc = launch_attention<1>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
-    case 2: rc = launch_attention<2>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
-    case 4: rc = launch_attention<4>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
-    default: rc = launch_attention<8>(q, kc, vc, st, part_acc, part_ml, splits, kv_heads, ctx, s, pdl); break;
-  }
-  if (rc) return rc;
-  return launched(launch(mllb::attn_combine_kernel, dim3(static_cast<unsigned>(q_heads)), dim3(128), 0, s, pdl,
-                         static_cast<const double*>(part_acc), static_cast<const double*>(part_ml),
-                         static_cast<int>(splits), out, static_cast<uint8_t*>(q8), MLLB_Q8_1_S_D_SUMQ),
-                  "attention combine kernel");
+  if (!q) return fail(MLLB_EINVAL, "null pointer: q");
+  AttentionArgs a = {};
+  a.q = q;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.ctx = ctx;
+  a.state = reinterpret_cast<const mllb::DecodeState*>(state);
+  // The unfused kernel only reads the caches.
+  a.k_cache = static_cast<uint8_t*>(const_cast<void*>(k_cache));
+  a.v_cache = static_cast<uint8_t*>(const_cast<void*>(v_cache));
+  return attention_impl(a, scratch, scratch_doubles, out, q8, flags, stream);
+}
+
+int mllb_decode_attention_qkv(const float* qkv, const float* q_gamma, const float* k_gamma, double theta_scale,
+                              const mllb_decode_state* state, void* k_cache, void* v_cache, double* scratch,
+                              int64_t scratch_doubles, float* out, void* q8, int64_t q_heads, int64_t kv_heads,
+                              int64_t ctx, unsigned flags, void* stream) {
+  if (!qkv || !q_gamma || !k_gamma) return fail(MLLB_EINVAL, "null pointer");
+  if (!(theta_scale > 0.0)) return fail(MLLB_EINVAL, "theta_scale must be positive");
+  AttentionArgs a = {};
+  a.qkv = qkv;
+  a.q_gamma = q_gamma;
+  a.k_gamma = k_gamma;
+  a.theta = theta_scale;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.ctx = ctx;
+  a.state = reinterpret_cast<const mllb::DecodeState*>(state);
+  a.k_cache = static_cast<uint8_t*>(k_cache);
+  a.v_cache = static_cast<uint8_t*>(v_cache);
+  return attention_impl(a, scratch, scratch_doubles, out, q8, flags, stream);
 }
 
 int mllb_argmax_f32(const float* x, int64_t n, int64_t index_offset, int64_t* key, unsigned flags, void* stream) {
@@ -598,6 +704,53 @@ int mllb_argmax_f32(const float* x, int64_t n, int64_t index_offset, int64_t* ke
                          static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, n, index_offset,
                          reinterpret_cast<long long*>(key)),
                   "argmax kernel");
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int mllb_q4k_matvec_act(const void* weights, const mllb_act_f32* act, float* out, int64_t n, int64_t k,
+                        unsigned flags, void* stream) {
+  if (!weights || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  mllb::ActSource src;
+  if ((rc = act_source(act, k, &src))) return rc;
+  if (!aligned(weights, 16) || !aligned(out, 4)) return fail(MLLB_EALIGN, "weights need 16-byte, out 4-byte alignment");
+  return q4k_team(static_cast<const uint8_t*>(weights), nullptr, src, out, nullptr, nullptr, n, k,
+                  static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL);
+}
+
+int mllb_q4k_gate_up_act(const void* up_weights, const void* gate_weights, const mllb_act_f32* act, float* up,
+                         float* gate, float* prod, int64_t n, int64_t k, unsigned flags, void* stream) {
+  if (!up_weights || !gate_weights) return fail(MLLB_EINVAL, "null pointer");
+  if (!up && !gate && !prod) return fail(MLLB_EINVAL, "no output requested");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  mllb::ActSource src;
+  if ((rc = act_source(act, k, &src))) return rc;
+  if (!aligned(up_weights, 16) || !aligned(gate_weights, 16) || !aligned(up, 4) || !aligned(gate, 4) ||
+      !aligned(prod, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, outputs 4-byte alignment");
+  return q4k_team(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights), src, up,
+                  gate, prod, n, k, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL);
+}
+
+int mllb_q6k_matvec_act(const void* weights, const mllb_act_f32* act, float* out, int64_t n, int64_t k,
+                        unsigned flags, void* stream) {
+  if (!weights || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (n % 8) return fail(MLLB_EUNSUPPORTED, "in-kernel activation needs a multiple of 8 rows");
+  mllb::ActSource src;
+  if ((rc = act_source(act, k, &src))) return rc;
+  if (!aligned(weights, 16) || !aligned(out, 4)) return fail(MLLB_EALIGN, "weights need 16-byte, out 4-byte alignment");
+  return q6k_team(static_cast<const uint8_t*>(weights), src, out, n, k, static_cast<cudaStream_t>(stream),
+                  flags & MLLB_LAUNCH_PDL);
 }
 
 }  // extern "C"

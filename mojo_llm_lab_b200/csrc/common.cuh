@@ -9,6 +9,7 @@
 // * exact conversions and warp reductions used by the fp64 row accumulation.
 #pragma once
 
+#include <climits>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
@@ -24,6 +25,19 @@ enum : uint32_t {
   kErrKvOverflow = 1u << 4,        // decode: position at or past the KV capacity (nothing written)
   kErrKvWaitTimeout = 1u << 5,     // decode attention gave up waiting for its K/V copies
 };
+
+// Device-resident state of a decode loop; mirrors mllb_decode_state of the
+// public header (32 bytes).
+struct DecodeState {
+  long long next_token_key;  // packed (value, index) of the greedy next token
+  int pos;                   // position / KV row of the token being decoded
+  int token;                 // token being decoded (written by the embedding)
+  int steps;                 // completed decode steps
+  int reserved[3];
+};
+static_assert(sizeof(DecodeState) == 32, "decode state layout");
+
+constexpr long long kNoToken = LLONG_MIN;
 
 // 1 s of wall time, and a hard iteration cap behind it.
 constexpr uint64_t kWaitLimitNs = 1000000000ull;
@@ -203,8 +217,15 @@ __device__ unsigned long long g_mllb_trace[4096][8];
   do {                                                                                       \
     if (threadIdx.x == 0 && blockIdx.x < 4096) g_mllb_trace[blockIdx.x][p] = mllb::global_timer_ns(); \
   } while (0)
+#define MLLB_TRACE_CTA(cta, p)                                                                    \
+  do {                                                                                            \
+    if (threadIdx.x == 0 && (cta) < 4096) g_mllb_trace[(cta)][p] = mllb::global_timer_ns();       \
+  } while (0)
 #else
 #define MLLB_TRACE_POINT(p) \
   do {                      \
+  } while (0)
+#define MLLB_TRACE_CTA(cta, p) \
+  do {                         \
   } while (0)
 #endif

@@ -29,25 +29,12 @@
 // and softmax weights carry the compensating 2^1008.
 #pragma once
 
-#include <climits>
-
 #include "common.cuh"
 #include "imrope.cuh"
 #include "q8_1.cuh"
 
 namespace mllb {
 
-// Mirrors mllb_decode_state of the public header (32 bytes).
-struct DecodeState {
-  long long next_token_key;  // packed (value, index) of the greedy next token
-  int pos;                   // position / KV row of the token being decoded
-  int token;                 // token being decoded (written by the embedding)
-  int steps;                 // completed decode steps
-  int reserved[3];
-};
-static_assert(sizeof(DecodeState) == 32, "decode state layout");
-
-constexpr long long kNoToken = LLONG_MIN;
 constexpr int kQ6kBytes = 210;
 
 // Order-preserving key: larger value first, then the lower index.  The high
@@ -76,16 +63,6 @@ __device__ __forceinline__ double warp_max_double(double v) {
 #pragma unroll
   for (int offset = 16; offset >= 1; offset >>= 1) v = fmax(v, __shfl_xor_sync(0xffffffffu, v, offset));
   return v;
-}
-
-// Store one Q8_1 block whose 32 values were quantised one per lane.
-__device__ __forceinline__ void q8_1_store_block(uint8_t* blk, int q, uint32_t d16, uint32_t s16, int lane) {
-  const uint32_t b = static_cast<uint32_t>(q) & 0xffu;
-  const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
-  const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
-  const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
-  if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + 4 + lane) = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
-  if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = d16 | (s16 << 16);
 }
 
 // ------------------------------------------------------------ embedding
@@ -124,26 +101,37 @@ __global__ void __launch_bounds__(256) embed_q6k_kernel(const uint8_t* __restric
 
 // ------------------------------------------------ residual + RMSNorm -> Q8_1
 
-// One CTA: h = x (+ delta) in fp32, written to x_out when given (x_out may
-// alias x); r = 1 / sqrt(sum(h^2) / k + eps) in fp64; y = fp32(h * r * gamma);
-// Q8_1 of y.  With `advance` (the step's final norm) thread 0 also resets the
-// next-token key and moves the state to the next position.
-__global__ void __launch_bounds__(1024) rmsnorm_q8_1_kernel(const float* x, const float* __restrict__ delta,
-                                                            float* x_out, const float* __restrict__ gamma,
-                                                            double eps, uint8_t* __restrict__ q8, int k, int s_mode,
-                                                            DecodeState* advance) {
-  extern __shared__ float hs[];
-  __shared__ double partial[32];
+// h = x (+ delta) in fp32, written to x_out when given; r = 1 / sqrt(sum(h^2)
+// / k + eps) in fp64; y = fp32(h * r * gamma); Q8_1 of y.  Every CTA sums
+// the squares of all k values itself (the same order in each, so the same r)
+// and quantises the Q8_1 blocks b = blockIdx.x + i * gridDim.x..., one per
+// warp, storing their h to x_out.  x_out may alias x only with one CTA.
+// With `advance` (the step's final norm) CTA 0 also resets the next-token
+// key and moves the state to the next position.
+__global__ void __launch_bounds__(256) rmsnorm_q8_1_kernel(const float* x, const float* __restrict__ delta,
+                                                           float* x_out, const float* __restrict__ gamma,
+                                                           double eps, uint8_t* __restrict__ q8, int k, int s_mode,
+                                                           DecodeState* advance) {
+  __shared__ double partial[8];
   pdl_wait_prerequisite();
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  // Loads in batches of 8 per thread, all issued before their first use.
+  constexpr int kBatch = 8;
   double ss = 0.0;
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    float h = x[i];
-    if (delta) h += delta[i];
-    hs[i] = h;
-    if (x_out) x_out[i] = h;
-    ss = fma(static_cast<double>(h), static_cast<double>(h), ss);
+  for (int base = threadIdx.x; base < k; base += kBatch * blockDim.x) {
+    float xv[kBatch], dv[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const int i = base + u * blockDim.x;
+      xv[u] = i < k ? x[i] : 0.0f;
+      dv[u] = (delta && i < k) ? delta[i] : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) {
+      const float h = delta ? xv[u] + dv[u] : xv[u];
+      ss = fma(static_cast<double>(h), static_cast<double>(h), ss);
+    }
   }
   ss = warp_sum_double(ss);
   if (lane == 0) partial[warp] = ss;
@@ -151,14 +139,20 @@ __global__ void __launch_bounds__(1024) rmsnorm_q8_1_kernel(const float* x, cons
   double total = lane < warps ? partial[lane] : 0.0;
   total = warp_sum_double(total);
   const double r = 1.0 / sqrt(total / static_cast<double>(k) + eps);
-  for (int b = warp; b < k / 32; b += warps) {
+  // Every thread has read all of x above; only then may an aliasing x_out
+  // (single CTA) be written.
+  __syncthreads();
+  for (int b = blockIdx.x * warps + warp; b < k / 32; b += gridDim.x * warps) {
     const int i = b * 32 + lane;
-    const float y = static_cast<float>(static_cast<double>(hs[i]) * r * static_cast<double>(gamma[i]));
+    float h = x[i];
+    if (delta) h += delta[i];
+    if (x_out) x_out[i] = h;
+    const float y = static_cast<float>(static_cast<double>(h) * r * static_cast<double>(gamma[i]));
     uint32_t d16, s16;
     const int q = q8_1_quantize_lane(y, s_mode, &d16, &s16);
     q8_1_store_block(q8 + static_cast<size_t>(b) * 36, q, d16, s16, lane);
   }
-  if (advance && threadIdx.x == 0) {
+  if (advance && blockIdx.x == 0 && threadIdx.x == 0) {
     advance->next_token_key = kNoToken;
     advance->pos += 1;
     advance->steps += 1;
@@ -172,23 +166,28 @@ __global__ void __launch_bounds__(1024) rmsnorm_q8_1_kernel(const float* x, cons
 // IMROPE -> q_out (fp32).  K heads: RMSNorm + k_gamma + IMROPE, rounded to
 // fp32 and then to fp16 at row `pos` of the cache.  V heads: fp16 of the
 // projection at row `pos`.  The four IMROPE axis positions of a text token
-// are (pos, pos, pos, 0).  pos outside [0, ctx) raises kErrKvOverflow and
-// appends nothing.  Cache layout: [kv_head][ctx][128] fp16.
-__global__ void __launch_bounds__(256) qk_rope_append_kernel(const float* __restrict__ qkv,
+// are (pos, pos, pos, 0), the same for every head, so each CTA first builds
+// the 64 (cos, sin) pairs once (one fp64 pow + sincos per thread).  pos
+// outside [0, ctx) raises kErrKvOverflow and appends nothing.  Cache layout:
+// [kv_head][ctx][128] fp16.
+__global__ void __launch_bounds__(128) qk_rope_append_kernel(const float* __restrict__ qkv,
                                                              const float* __restrict__ q_gamma,
                                                              const float* __restrict__ k_gamma,
                                                              const DecodeState* __restrict__ state, double theta,
                                                              float* __restrict__ q_out, __half* __restrict__ k_cache,
                                                              __half* __restrict__ v_cache, int hq, int hkv, int ctx) {
+  __shared__ double2 rot[kHeadDim / 2];
   pdl_wait_prerequisite();
   pdl_launch_dependents();
   const int lane = threadIdx.x & 31;
   const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (w >= hq + 2 * hkv) return;
   const int pos = state->pos;
+  if (threadIdx.x < kHeadDim / 2) rot[threadIdx.x] = imrope_rotation(threadIdx.x, pos, pos, pos, 0, theta);
+  __syncthreads();
+  if (w >= hq + 2 * hkv) return;
   double o[4];
   if (w < hq) {
-    imrope_head_values(qkv + static_cast<size_t>(w) * kHeadDim, q_gamma, pos, pos, pos, 0, theta, lane, o);
+    imrope_head_table(qkv + static_cast<size_t>(w) * kHeadDim, q_gamma, rot, lane, o);
     float* dst = q_out + static_cast<size_t>(w) * kHeadDim;
     dst[lane] = static_cast<float>(o[0]);
     dst[lane + 64] = static_cast<float>(o[1]);
@@ -203,7 +202,7 @@ __global__ void __launch_bounds__(256) qk_rope_append_kernel(const float* __rest
   const int j = w < hq + hkv ? w - hq : w - hq - hkv;
   const size_t row = (static_cast<size_t>(j) * ctx + pos) * kHeadDim;
   if (w < hq + hkv) {
-    imrope_head_values(qkv + static_cast<size_t>(w) * kHeadDim, k_gamma, pos, pos, pos, 0, theta, lane, o);
+    imrope_head_table(qkv + static_cast<size_t>(w) * kHeadDim, k_gamma, rot, lane, o);
     k_cache[row + lane] = __float2half_rn(static_cast<float>(o[0]));
     k_cache[row + lane + 64] = __float2half_rn(static_cast<float>(o[1]));
     k_cache[row + lane + 32] = __float2half_rn(static_cast<float>(o[2]));
@@ -228,12 +227,21 @@ __device__ __forceinline__ double half_bits_scaled(uint32_t h16) {
 
 constexpr double kTwo1008 = 0x1p1008;
 
-// Sum a value index i (0..31) over the 32 lanes of a warp for all 32
-// indices at once: after five exchange steps lane l holds the total of
-// index l.  31 shuffles for 32 sums.
+// Sum, over the 32 lanes of a warp, each of 32 values v[slot] at once:
+// afterwards lane l holds the total of logical index l = key * G + head.
+// Lane l keeps logical index i in slot i ^ (l & ~(G - 1)) (key bits XORed
+// with its own), so on every key-bit step the value to send is the upper
+// half of the live slots and the one to keep the lower half: no selects.
+// The head bits (unpermuted) take the select form.  31 shuffles.
+template <int G>
 __device__ __forceinline__ double transpose_reduce32(double (&v)[32], int lane) {
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
+  for (int off = 16; off >= G; off >>= 1) {
+#pragma unroll
+    for (int p = 0; p < off; ++p) v[p] += __shfl_xor_sync(0xffffffffu, v[p + off], off);
+  }
+#pragma unroll
+  for (int off = G / 2; off >= 1; off >>= 1) {
     const bool upper = (lane & off) != 0;
 #pragma unroll
     for (int i = 0; i < off; ++i) {
@@ -246,20 +254,30 @@ __device__ __forceinline__ double transpose_reduce32(double (&v)[32], int lane) 
 }
 
 // One CTA per (context chunk, KV head); G query heads share the KV head.
+// 16 warps where 128 registers a thread suffice (G = 4, the decode shape,
+// and G = 1), otherwise 8.
 template <int G>
 struct AttnConfig {
-  static constexpr int kWarps = 8;
+  static constexpr int kWarps = (G == 4 || G == 1) ? 16 : 8;
   static constexpr int kThreads = kWarps * 32;
+  static constexpr int kCtasPerSm = 1;
   static constexpr int kMaxChunk = 256;                   // keys per CTA
+  static constexpr int kSub = 64;                         // keys per staged sub-chunk
+  static constexpr int kNumSub = kMaxChunk / kSub;
   static constexpr int kRowBytes = kHeadDim * 2;          // one fp16 K or V row
   static constexpr int kKeysPerPass = 32 / G;             // keys per warp per score pass
+  static constexpr int kWarpsPerHead = kWarps / G;
   static constexpr int kKOffset = 0;
   static constexpr int kVOffset = kMaxChunk * kRowBytes;
-  static constexpr int kScoreOffset = 2 * kMaxChunk * kRowBytes;  // fp64 [G][kMaxChunk]
-  static constexpr int kBarOffset = kScoreOffset + G * kMaxChunk * 8;
-  static constexpr int kSmemBytes = kBarOffset + 16;
-  static_assert(32 % G == 0 && G <= kWarps, "query heads per KV head");
-  static_assert(kWarps * G * kHeadDim * 8 <= kVOffset, "P.V reduction buffer fits in the K buffer");
+  static constexpr int kScoreOffset = 2 * kMaxChunk * kRowBytes;            // fp64 [G][kMaxChunk]
+  static constexpr int kQOffset = kScoreOffset + G * kMaxChunk * 8;         // fp32 [G][128]
+  static constexpr int kRotOffset = kQOffset + G * kHeadDim * 4;            // double2 [64]
+  static constexpr int kRedOffset = kRotOffset + kHeadDim / 2 * 16;         // fp64 [2][kWarps]
+  static constexpr int kBarOffset = kRedOffset + 2 * kWarps * 8;            // 2 x kNumSub mbarriers
+  static constexpr int kSmemBytes = kBarOffset + 2 * kNumSub * 8;
+  static_assert(32 % G == 0 && G <= kWarps && kWarps % G == 0, "query heads per KV head");
+  static_assert(kSub % kKeysPerPass == 0, "score passes stay inside one sub-chunk");
+  static_assert(kWarps * G * kHeadDim * 8 <= kScoreOffset, "P.V reduction buffer fits in the K and V buffers");
 };
 
 // Chunk c of the n = pos + 1 keys: per = roundup16(ceil(n / splits)) keys
@@ -267,23 +285,40 @@ struct AttnConfig {
 //   part_ml[(hh * splits + c) * 2 + {0, 1}] = m (max score), l = sum exp(s - m)
 //   part_acc[(hh * splits + c) * 128 + d]   = sum exp(s - m) * v[d]
 // with s = (q . k) * scale, all fp64.  An empty chunk writes m = -inf, l = 0.
-// K/V rows below pos are final (written by earlier steps) and are copied in
-// before waiting on the preceding kernel; row pos, appended by that kernel,
-// is read after the wait.
+//
+// K/V rows below pos are final (written by earlier steps): they are copied
+// in 64-row sub-chunks (one mbarrier each, so scoring starts on the first)
+// before waiting on the preceding kernel.  Row pos, the token's own:
+//  - qkv == nullptr: the preceding kernel appended it; it is read after the
+//    wait, and q is the already normalised and rotated query;
+//  - qkv != nullptr (fused): this kernel does the per-head RMSNorm + gamma +
+//    IMROPE of the G query heads from the raw QKV projection, and the CTA
+//    whose chunk holds pos also forms the K row (RMSNorm + k_gamma + IMROPE
+//    -> fp32 -> fp16) and the V row (fp16), appends both to the caches and
+//    uses them directly.  The 64 rotations are built before the wait.
 template <int G>
-__global__ void __launch_bounds__(AttnConfig<G>::kThreads, 1)
-    attn_split_kernel(const float* __restrict__ q, const uint8_t* __restrict__ k_cache,
-                      const uint8_t* __restrict__ v_cache, const DecodeState* __restrict__ state,
-                      double* __restrict__ part_acc, double* __restrict__ part_ml, int ctx, int splits,
-                      double scale) {
+__global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasPerSm)
+    attn_split_kernel(const float* __restrict__ q, const float* __restrict__ qkv, const float* __restrict__ q_gamma,
+                      const float* __restrict__ k_gamma, double theta, int hq, int hkv,
+                      const DecodeState* __restrict__ state, uint8_t* __restrict__ k_cache,
+                      uint8_t* __restrict__ v_cache, double* __restrict__ part_acc, double* __restrict__ part_ml,
+                      int ctx, int splits, double scale) {
   using C = AttnConfig<G>;
+  constexpr int W = C::kWarps, KB = C::kKeysPerPass, WG = C::kWarpsPerHead;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ks = smem + C::kKOffset;
   uint8_t* vs = smem + C::kVOffset;
   double* sc = reinterpret_cast<double*>(smem + C::kScoreOffset);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  float* qs = reinterpret_cast<float*>(smem + C::kQOffset);
+  double2* rot = reinterpret_cast<double2*>(smem + C::kRotOffset);
+  double* red_m = reinterpret_cast<double*>(smem + C::kRedOffset);
+  double* red_l = red_m + W;
+  uint64_t* bar_k = reinterpret_cast<uint64_t*>(smem + C::kBarOffset);
+  uint64_t* bar_v = bar_k + C::kNumSub;
   const int split = blockIdx.x, j = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const bool fused = qkv != nullptr;
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 0);
 
   const int pos = state->pos;
   const int n = pos < 0 ? 0 : (pos < ctx ? pos + 1 : ctx);
@@ -291,116 +326,194 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, 1)
   const int t0 = min(split * per, n), t1 = min(t0 + per, n);
   const int cnt = t1 - t0;
   const int old_cnt = max(min(t1, pos) - t0, 0);
+  const bool has_new = cnt > old_cnt;  // this chunk holds row pos
+  const int sub_new = old_cnt / C::kSub;
   const size_t row0 = (static_cast<size_t>(j) * ctx + t0) * C::kRowBytes;
 
   if (tid == 0) {
-    mbar_init(&bar[0], 1);
-    mbar_init(&bar[1], 1);
+    for (int s = 0; s < C::kNumSub; ++s) {
+      const uint32_t count = (has_new && s == sub_new) ? 2u : 1u;
+      mbar_init(&bar_k[s], count);
+      mbar_init(&bar_v[s], count);
+    }
     fence_mbar_init();
   }
   __syncthreads();
   if (tid == 0) {
-    if (old_cnt > 0) {
-      const uint64_t policy = l2_evict_first_policy();
-      const uint32_t bytes = static_cast<uint32_t>(old_cnt) * C::kRowBytes;
-      mbar_arrive_expect_tx(&bar[0], bytes);
-      bulk_copy_g2s(ks, k_cache + row0, bytes, &bar[0], policy);
-      mbar_arrive_expect_tx(&bar[1], bytes);
-      bulk_copy_g2s(vs, v_cache + row0, bytes, &bar[1], policy);
-    } else {
-      mbar_arrive(&bar[0]);
-      mbar_arrive(&bar[1]);
+    const uint64_t policy = l2_evict_first_policy();
+    for (int s = 0; s < C::kNumSub; ++s) {
+      const int rows = min(max(old_cnt - s * C::kSub, 0), C::kSub);
+      if (rows > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(rows) * C::kRowBytes;
+        const size_t off = static_cast<size_t>(s) * C::kSub * C::kRowBytes;
+        mbar_arrive_expect_tx(&bar_k[s], bytes);
+        bulk_copy_g2s(ks + off, k_cache + row0 + off, bytes, &bar_k[s], policy);
+      } else {
+        mbar_arrive(&bar_k[s]);
+      }
+    }
+    for (int s = 0; s < C::kNumSub; ++s) {
+      const int rows = min(max(old_cnt - s * C::kSub, 0), C::kSub);
+      if (rows > 0) {
+        const uint32_t bytes = static_cast<uint32_t>(rows) * C::kRowBytes;
+        const size_t off = static_cast<size_t>(s) * C::kSub * C::kRowBytes;
+        mbar_arrive_expect_tx(&bar_v[s], bytes);
+        bulk_copy_g2s(vs + off, v_cache + row0 + off, bytes, &bar_v[s], policy);
+      } else {
+        mbar_arrive(&bar_v[s]);
+      }
     }
   }
+  if (fused && tid < kHeadDim / 2) rot[tid] = imrope_rotation(tid, pos, pos, pos, 0, theta);
+  __syncthreads();
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 1);
   pdl_wait_prerequisite();
   pdl_launch_dependents();
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 2);
 
-  // The row appended by the preceding kernel (at most one per chunk).
-  if (cnt > old_cnt && tid < 32) {
-    const size_t off = row0 + static_cast<size_t>(old_cnt) * C::kRowBytes;
-    const uint8_t* src = (tid < 16 ? k_cache : v_cache) + off;
-    uint8_t* dst = (tid < 16 ? ks : vs) + old_cnt * C::kRowBytes;
-    reinterpret_cast<uint4*>(dst)[tid & 15] = reinterpret_cast<const uint4*>(src)[tid & 15];
+  // The query heads (and, in the chunk holding pos, the new K/V row).
+  if (fused) {
+    const int tasks = G + (has_new ? 2 : 0);
+    for (int task = warp; task < tasks; task += W) {
+      double o[4];
+      if (task < G) {
+        imrope_head_table(qkv + static_cast<size_t>(j * G + task) * kHeadDim, q_gamma, rot, lane, o);
+        float* dst = qs + task * kHeadDim;
+        dst[lane] = static_cast<float>(o[0]);
+        dst[lane + 64] = static_cast<float>(o[1]);
+        dst[lane + 32] = static_cast<float>(o[2]);
+        dst[lane + 96] = static_cast<float>(o[3]);
+      } else {
+        const bool is_k = task == G;
+        __half hv[4];
+        if (is_k) {
+          imrope_head_table(qkv + static_cast<size_t>(hq + j) * kHeadDim, k_gamma, rot, lane, o);
+          hv[0] = __float2half_rn(static_cast<float>(o[0]));  // dim lane
+          hv[1] = __float2half_rn(static_cast<float>(o[2]));  // dim lane + 32
+          hv[2] = __float2half_rn(static_cast<float>(o[1]));  // dim lane + 64
+          hv[3] = __float2half_rn(static_cast<float>(o[3]));  // dim lane + 96
+        } else {
+          const float* src = qkv + static_cast<size_t>(hq + hkv + j) * kHeadDim;
+#pragma unroll
+          for (int i = 0; i < 4; ++i) hv[i] = __float2half_rn(src[lane + 32 * i]);
+        }
+        __half* srow = reinterpret_cast<__half*>((is_k ? ks : vs) + old_cnt * C::kRowBytes);
+        __half* grow = reinterpret_cast<__half*>((is_k ? k_cache : v_cache) + row0 + old_cnt * C::kRowBytes);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          srow[lane + 32 * i] = hv[i];
+          grow[lane + 32 * i] = hv[i];
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(is_k ? &bar_k[sub_new] : &bar_v[sub_new]);
+      }
+    }
+    if (pos >= ctx && split == 0 && j == 0 && tid == 0) record_error(kErrKvOverflow);
+    __syncthreads();
+  } else if (has_new && (tid == 0 || tid == 32)) {
+    const bool is_k = tid == 0;
+    const uint4* src = reinterpret_cast<const uint4*>((is_k ? k_cache : v_cache) + row0 + old_cnt * C::kRowBytes);
+    uint4* dst = reinterpret_cast<uint4*>((is_k ? ks : vs) + old_cnt * C::kRowBytes);
+    uint4 row[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) row[i] = src[i];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[i] = row[i];
+    mbar_arrive(is_k ? &bar_k[sub_new] : &bar_v[sub_new]);
   }
   // Lane l owns dims 4l..4l+3 of the G query heads, scaled by 2^1008.
   double qd[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) {
-    const float4 v = reinterpret_cast<const float4*>(q + static_cast<size_t>(j * G + g) * kHeadDim)[lane];
+    const float4 v = fused ? reinterpret_cast<const float4*>(qs + g * kHeadDim)[lane]
+                           : reinterpret_cast<const float4*>(q + static_cast<size_t>(j * G + g) * kHeadDim)[lane];
     qd[g][0] = static_cast<double>(v.x) * kTwo1008;
     qd[g][1] = static_cast<double>(v.y) * kTwo1008;
     qd[g][2] = static_cast<double>(v.z) * kTwo1008;
     qd[g][3] = static_cast<double>(v.w) * kTwo1008;
   }
-  bool ok = mbar_wait_bounded(&bar[0], 0);
-  __syncthreads();
 
-  // Scores: each warp pass covers kKeysPerPass keys x G heads = 32 dot products.
-  constexpr int KB = C::kKeysPerPass;
-  if (ok) {
-    for (int base = warp * KB; base < cnt; base += C::kWarps * KB) {
-      double v[32];
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 3);
+  // Scores: a warp pass covers KB keys x G heads = 32 dot products; lane l
+  // reads key (slot ^ l / G) of the pass, the layout transpose_reduce32 wants.
+  bool ok = true;
+  const int lane_key = lane / G;
+  for (int pass = warp; pass * KB < cnt; pass += W) {
+    const int base = pass * KB;
+    ok = mbar_wait_bounded(&bar_k[base / C::kSub], 0) && ok;
+    double v[32];
 #pragma unroll
-      for (int kk = 0; kk < KB; ++kk) {
-        const int t = base + kk;
-        uint2 w = make_uint2(0u, 0u);
-        if (t < cnt) w = *reinterpret_cast<const uint2*>(ks + t * C::kRowBytes + lane * 8);
-        const double k0 = half_bits_scaled(w.x & 0xffffu), k1 = half_bits_scaled(w.x >> 16);
-        const double k2 = half_bits_scaled(w.y & 0xffffu), k3 = half_bits_scaled(w.y >> 16);
+    for (int kp = 0; kp < KB; ++kp) {
+      const int t = base + (kp ^ lane_key);
+      uint2 w = make_uint2(0u, 0u);
+      if (t < cnt) w = *reinterpret_cast<const uint2*>(ks + t * C::kRowBytes + lane * 8);
+      const double k0 = half_bits_scaled(w.x & 0xffffu), k1 = half_bits_scaled(w.x >> 16);
+      const double k2 = half_bits_scaled(w.y & 0xffffu), k3 = half_bits_scaled(w.y >> 16);
 #pragma unroll
-        for (int g = 0; g < G; ++g)
-          v[kk * G + g] = fma(qd[g][3], k3, fma(qd[g][2], k2, fma(qd[g][1], k1, qd[g][0] * k0)));
-      }
-      const double total = transpose_reduce32(v, lane);
-      const int t = base + lane / G;
-      if (t < cnt) sc[(lane % G) * C::kMaxChunk + t] = total * scale;
+      for (int g = 0; g < G; ++g)
+        v[kp * G + g] = fma(qd[g][3], k3, fma(qd[g][2], k2, fma(qd[g][1], k1, qd[g][0] * k0)));
     }
+    const double total = transpose_reduce32<G>(v, lane);
+    const int t = base + lane_key;
+    if (t < cnt) sc[(lane % G) * C::kMaxChunk + t] = total * scale;
   }
   __syncthreads();
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 4);
 
-  // Chunk softmax, one warp per query head; the weights are stored x 2^1008.
-  if (warp < G) {
-    double* s = sc + warp * C::kMaxChunk;
+  // Chunk softmax: WG warps per query head; weights stored x 2^1008.
+  {
+    const int g = warp / WG, r = warp % WG;
+    double* s = sc + g * C::kMaxChunk;
     double m = -INFINITY;
-    for (int t = lane; t < cnt; t += 32) m = fmax(m, s[t]);
+    for (int t = r * 32 + lane; t < cnt; t += WG * 32) m = fmax(m, s[t]);
     m = warp_max_double(m);
+    if (lane == 0) red_m[warp] = m;
+    __syncthreads();
+    m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < WG; ++i) m = fmax(m, red_m[g * WG + i]);
     double l = 0.0;
-    for (int t = lane; t < cnt; t += 32) {
+    for (int t = r * 32 + lane; t < cnt; t += WG * 32) {
       const double p = exp(s[t] - m);
       s[t] = p * kTwo1008;
       l += p;
     }
     l = warp_sum_double(l);
-    if (lane == 0) {
-      double* ml = part_ml + (static_cast<size_t>(j * G + warp) * splits + split) * 2;
-      ml[0] = (ok && cnt > 0) ? m : -INFINITY;
-      ml[1] = (ok && cnt > 0) ? l : 0.0;
+    if (lane == 0) red_l[warp] = l;
+    __syncthreads();
+    if (r == 0 && lane == 0) {
+      double total = 0.0;
+#pragma unroll
+      for (int i = 0; i < WG; ++i) total += red_l[g * WG + i];
+      double* ml = part_ml + (static_cast<size_t>(j * G + g) * splits + split) * 2;
+      ml[0] = cnt > 0 ? m : -INFINITY;
+      ml[1] = cnt > 0 ? total : 0.0;
     }
   }
-  ok = mbar_wait_bounded(&bar[1], 0) && ok;
-  if (!ok && tid == 0) record_error(kErrKvWaitTimeout);
-  __syncthreads();
 
-  // P.V: warp w takes keys w, w + 8, ...; lane l owns dims 4l..4l+3.
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 5);
+  // P.V: warp w takes keys w, w + W, ...; lane l owns dims 4l..4l+3.
+  for (int s = 0; s < C::kNumSub; ++s) ok = mbar_wait_bounded(&bar_v[s], 0) && ok;
   double acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0;
-  if (ok) {
-    for (int t = warp; t < cnt; t += C::kWarps) {
-      const uint2 w = *reinterpret_cast<const uint2*>(vs + t * C::kRowBytes + lane * 8);
-      const double v0 = half_bits_scaled(w.x & 0xffffu), v1 = half_bits_scaled(w.x >> 16);
-      const double v2 = half_bits_scaled(w.y & 0xffffu), v3 = half_bits_scaled(w.y >> 16);
+  for (int t = warp; t < cnt; t += W) {
+    const uint2 w = *reinterpret_cast<const uint2*>(vs + t * C::kRowBytes + lane * 8);
+    const double v0 = half_bits_scaled(w.x & 0xffffu), v1 = half_bits_scaled(w.x >> 16);
+    const double v2 = half_bits_scaled(w.y & 0xffffu), v3 = half_bits_scaled(w.y >> 16);
 #pragma unroll
-      for (int g = 0; g < G; ++g) {
-        const double p = sc[g * C::kMaxChunk + t];
-        acc[g][0] = fma(p, v0, acc[g][0]);
-        acc[g][1] = fma(p, v1, acc[g][1]);
-        acc[g][2] = fma(p, v2, acc[g][2]);
-        acc[g][3] = fma(p, v3, acc[g][3]);
-      }
+    for (int g = 0; g < G; ++g) {
+      const double p = sc[g * C::kMaxChunk + t];
+      acc[g][0] = fma(p, v0, acc[g][0]);
+      acc[g][1] = fma(p, v1, acc[g][1]);
+      acc[g][2] = fma(p, v2, acc[g][2]);
+      acc[g][3] = fma(p, v3, acc[g][3]);
     }
   }
-  // Cross-warp sum in warp order through the K buffer (no longer read).
+  if (!ok && tid == 0) record_error(kErrKvWaitTimeout);
+  __syncthreads();
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 6);
+  // Cross-warp sum in warp order through the K and V buffers (no longer read).
   double* red = reinterpret_cast<double*>(ks);
 #pragma unroll
   for (int g = 0; g < G; ++g) {
@@ -414,37 +527,65 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, 1)
   for (int idx = tid; idx < G * kHeadDim; idx += C::kThreads) {
     double s = 0.0;
 #pragma unroll
-    for (int w = 0; w < C::kWarps; ++w) s += red[w * G * kHeadDim + idx];
+    for (int w = 0; w < W; ++w) s += red[w * G * kHeadDim + idx];
     const int g = idx / kHeadDim, d = idx % kHeadDim;
     part_acc[(static_cast<size_t>(j * G + g) * splits + split) * kHeadDim + d] = s;
   }
-  // After a timed-out wait, give the copy another bounded wait before the
+  MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 7);
+  // After a timed-out wait, give the copies another bounded wait before the
   // shared memory is released.
-  if (!ok && tid == 0) mbar_wait_bounded(&bar[0], 0);
+  if (!ok && tid == 0) {
+    for (int s = 0; s < C::kNumSub; ++s) {
+      mbar_wait_bounded(&bar_k[s], 0);
+      mbar_wait_bounded(&bar_v[s], 0);
+    }
+  }
 }
 
 // One CTA of 128 threads per query head: merge the chunk partials,
 //   M = max m_c,  L = sum l_c e^(m_c - M),  out[d] = fp32(sum acc_c[d] e^(m_c - M) / L),
 // then quantise the head's 128 values to 4 Q8_1 blocks (one per warp).
+// Warp 0 turns the chunk maxima into weights e^(m_c - M) in shared memory
+// (dynamic, `splits` doubles); every thread then sums its dimension over the
+// chunks with independent loads.
 __global__ void __launch_bounds__(128) attn_combine_kernel(const double* __restrict__ part_acc,
                                                            const double* __restrict__ part_ml, int splits,
                                                            float* __restrict__ out, uint8_t* __restrict__ q8,
                                                            int s_mode) {
+  extern __shared__ double weight[];
+  __shared__ double total_l;
   pdl_wait_prerequisite();
   pdl_launch_dependents();
   const int h = blockIdx.x, d = threadIdx.x, lane = d & 31;
   const double* ml = part_ml + static_cast<size_t>(h) * splits * 2;
   const double* acc = part_acc + static_cast<size_t>(h) * splits * kHeadDim + d;
-  double m_max = -INFINITY;
-  for (int c = 0; c < splits; ++c) m_max = fmax(m_max, ml[2 * c]);
-  double l = 0.0, o = 0.0;
-  for (int c = 0; c < splits; ++c) {
-    const double m = ml[2 * c];
-    if (m == -INFINITY) continue;
-    const double w = exp(m - m_max);
-    l += ml[2 * c + 1] * w;
-    o += acc[static_cast<size_t>(c) * kHeadDim] * w;
+  if (d < 32) {
+    double m_max = -INFINITY;
+    for (int c = lane; c < splits; c += 32) m_max = fmax(m_max, ml[2 * c]);
+    m_max = warp_max_double(m_max);
+    double l = 0.0;
+    for (int c = lane; c < splits; c += 32) {
+      const double m = ml[2 * c];
+      const double w = m == -INFINITY ? 0.0 : exp(m - m_max);
+      weight[c] = w;
+      l += ml[2 * c + 1] * w;
+    }
+    l = warp_sum_double(l);
+    if (lane == 0) total_l = l;
   }
+  __syncthreads();
+  // All loads of a batch of 32 chunks are issued before the sums use them.
+  constexpr int kBatch = 32;
+  double o = 0.0;
+  for (int c0 = 0; c0 < splits; c0 += kBatch) {
+    double a[kBatch];
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u) a[u] = c0 + u < splits ? acc[static_cast<size_t>(c0 + u) * kHeadDim] : 0.0;
+#pragma unroll
+    for (int u = 0; u < kBatch; ++u)
+      if (c0 + u < splits) o = fma(a[u], weight[c0 + u], o);
+  }
+  const double l = total_l;
   const float y = l > 0.0 ? static_cast<float>(o / l) : 0.0f;
   if (out) out[static_cast<size_t>(h) * kHeadDim + d] = y;
   if (q8) {

@@ -56,6 +56,38 @@ __device__ __forceinline__ void imrope_head_values(const float* __restrict__ x, 
   }
 }
 
+// (cos, sin) of pair p's angle pos[axis(p)] * theta_scale^p, fp64.
+__device__ __forceinline__ double2 imrope_rotation(int p, int32_t p0, int32_t p1, int32_t p2, int32_t p3,
+                                                   double theta_scale) {
+  const int axis = imrope_axis(p);
+  const int32_t position = axis == 0 ? p0 : axis == 1 ? p1 : axis == 2 ? p2 : p3;
+  const double angle = static_cast<double>(position) * pow(theta_scale, static_cast<double>(p));
+  double s, c;
+  sincos(angle, &s, &c);
+  return make_double2(c, s);
+}
+
+// imrope_head_values with the 64 rotations precomputed (rot[p] = (cos, sin)).
+__device__ __forceinline__ void imrope_head_table(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                  const double2* rot, int lane, double (&o)[4]) {
+  const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+  double ss = static_cast<double>(x0) * x0;
+  ss = fma(static_cast<double>(x1), static_cast<double>(x1), ss);
+  ss = fma(static_cast<double>(x2), static_cast<double>(x2), ss);
+  ss = fma(static_cast<double>(x3), static_cast<double>(x3), ss);
+  ss = warp_sum_double(ss);
+  const double r = 1.0 / sqrt(ss / kHeadDim + 1e-6);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const int p = lane + 32 * half;
+    const double2 cs = rot[p];
+    const double ya = static_cast<double>(half ? x1 : x0) * r * static_cast<double>(gamma[p]);
+    const double yb = static_cast<double>(half ? x3 : x2) * r * static_cast<double>(gamma[p + 64]);
+    o[2 * half] = ya * cs.x - yb * cs.y;
+    o[2 * half + 1] = ya * cs.y + yb * cs.x;
+  }
+}
+
 // One head, computed by the 32 lanes of the calling warp, stored as fp32.
 __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, const float* __restrict__ gamma,
                                                  const int32_t* __restrict__ pos, double theta_scale,

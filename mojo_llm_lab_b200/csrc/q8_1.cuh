@@ -38,6 +38,16 @@ __device__ __forceinline__ int q8_1_quantize_lane(float x, int s_mode, uint32_t*
   return q;
 }
 
+// Store one Q8_1 block (36 bytes) whose 32 values were quantised one per lane.
+__device__ __forceinline__ void q8_1_store_block(uint8_t* blk, int q, uint32_t d16, uint32_t s16, int lane) {
+  const uint32_t b = static_cast<uint32_t>(q) & 0xffu;
+  const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
+  const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
+  const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
+  if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(blk + 4 + lane) = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
+  if (lane == 0) *reinterpret_cast<uint32_t*>(blk) = d16 | (s16 << 16);
+}
+
 // grid-stride over Q8_1 blocks, one warp each.
 __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restrict__ x, uint8_t* __restrict__ out,
                                                             int64_t blocks, int s_mode) {

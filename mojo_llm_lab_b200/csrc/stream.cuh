@@ -36,8 +36,26 @@
 #include "common.cuh"
 #include "q4k.cuh"
 #include "q6k.cuh"
+#include "q8_1.cuh"
 
 namespace mllb {
+
+// Where a streaming kernel's activation comes from: Q8_1 bytes (q8), or
+// produced in the kernel from fp32 (x != nullptr): h = x + delta (fp32),
+// y = gamma ? fp32(h / sqrt(mean(h^2) + eps) * gamma) : h (fp64 inside), then
+// Q8_1 of y (s = d * sum q) -- what rmsnorm_q8_1 / q8_1_quantize would have
+// written, built by every CTA in its own shared memory.  CTA 0 stores h to
+// x_out (which must not overlap x) and, with `advance`, moves a decode state
+// to its next position (the step's final norm).
+struct ActSource {
+  const uint8_t* q8;
+  const float* x;
+  const float* delta;
+  const float* gamma;
+  float* x_out;
+  double eps;
+  DecodeState* advance;
+};
 
 // ============================================================== formats
 
@@ -63,6 +81,22 @@ struct Q4kFormat {
   template <int NB>
   __device__ static void stage_activation(const uint8_t* q8, uint8_t* act, int tid, int nthreads) {
     stage_q8_1<NB * 8>(q8, act, tid, nthreads);
+  }
+
+  // Write Q8_1 group g (quantised one value per lane) in this layout.
+  template <int NB>
+  __device__ static void store_group(uint8_t* act, int g, int lane, int q, uint32_t d16, uint32_t) {
+    constexpr int G = NB * 8;
+    const uint32_t b = static_cast<uint32_t>(q) & 0xffu;
+    const uint32_t b1 = __shfl_down_sync(0xffffffffu, b, 1);
+    const uint32_t b2 = __shfl_down_sync(0xffffffffu, b, 2);
+    const uint32_t b3 = __shfl_down_sync(0xffffffffu, b, 3);
+    const int sum = warp_sum_int(q);
+    if ((lane & 3) == 0) *reinterpret_cast<uint32_t*>(act + g * 32 + lane) = b | (b1 << 8) | (b2 << 16) | (b3 << 24);
+    if (lane == 0) {
+      reinterpret_cast<double*>(act + G * 32)[g] = half_bits_to_double(d16);
+      reinterpret_cast<int*>(act + G * 40)[g] = sum;
+    }
   }
 
   template <int NB>
@@ -130,6 +164,11 @@ struct Q6kFormat {
   }
 
   template <int NB>
+  __device__ static void store_group(uint8_t* act, int g, int lane, int q, uint32_t d16, uint32_t s16) {
+    q8_1_store_block(act + g * kQ8BlockBytes, q, d16, s16, lane);
+  }
+
+  template <int NB>
   __device__ static Slot load_slot(const uint8_t* act, int p) {
     Slot sl;
     const int b = p >> 3, u8 = p & 7;
@@ -165,6 +204,76 @@ struct Q6kFormat {
   }
 };
 
+// ============================================================== producer
+
+// Build the activation of an ActSource with x != nullptr in shared memory,
+// by the `nthreads` consumer threads (warp-aligned; named barrier 1).
+// `red` holds one double per consumer warp.  Loads are issued in batches
+// before their first use: each is an L2 round trip.
+template <class Fmt, int NB, int NTHREADS>
+__device__ __forceinline__ void produce_activation(const ActSource& src, uint8_t* act, double* red, int tid) {
+  constexpr int K = NB * 256, G = NB * 8, NW = NTHREADS / 32;
+  constexpr int kPer = (G + NW - 1) / NW;   // Q8_1 groups per warp
+  constexpr int kBatch = 8;
+  const int lane = tid & 31, warp = tid >> 5;
+  double r = 1.0;
+  if (src.gamma) {
+    double ss = 0.0;
+    for (int base = tid; base < K; base += kBatch * NTHREADS) {
+      float xv[kBatch], dv[kBatch];
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const int i = base + u * NTHREADS;
+        xv[u] = i < K ? src.x[i] : 0.0f;
+        dv[u] = (src.delta && i < K) ? src.delta[i] : 0.0f;
+      }
+#pragma unroll
+      for (int u = 0; u < kBatch; ++u) {
+        const float h = src.delta ? xv[u] + dv[u] : xv[u];
+        ss = fma(static_cast<double>(h), static_cast<double>(h), ss);
+      }
+    }
+    ss = warp_sum_double(ss);
+    if (lane == 0) red[warp] = ss;
+    named_barrier(1, NTHREADS);
+    double total = 0.0;
+#pragma unroll 4
+    for (int w = 0; w < NW; ++w) total += red[w];
+    r = 1.0 / sqrt(total / static_cast<double>(K) + src.eps);
+  }
+  float hv[kPer], gv[kPer];
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int g = warp + u * NW;
+    const int i = g * 32 + lane;
+    float h = 0.0f, gm = 1.0f;
+    if (g < G) {
+      h = src.x[i];
+      if (src.delta) h += src.delta[i];
+      if (src.gamma) gm = src.gamma[i];
+    }
+    hv[u] = h;
+    gv[u] = gm;
+  }
+#pragma unroll
+  for (int u = 0; u < kPer; ++u) {
+    const int g = warp + u * NW;
+    if (g < G) {
+      if (src.x_out && blockIdx.x == 0) src.x_out[g * 32 + lane] = hv[u];
+      const float y = src.gamma ? static_cast<float>(static_cast<double>(hv[u]) * r * static_cast<double>(gv[u]))
+                                : hv[u];
+      uint32_t d16, s16;
+      const int q = q8_1_quantize_lane(y, kQ8SumDTimesSumQ, &d16, &s16);
+      Fmt::template store_group<NB>(act, g, lane, q, d16, s16);
+    }
+  }
+  if (src.advance && blockIdx.x == 0 && tid == 0) {
+    src.advance->next_token_key = kNoToken;
+    src.advance->pos += 1;
+    src.advance->steps += 1;
+  }
+}
+
 // ============================================================== geometry
 
 template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
@@ -186,7 +295,8 @@ struct TeamConfig {
   static constexpr int kPartOffset = kActOffset + Fmt::template ActLayout<NB>::kBytes;
   static constexpr int kBarOffset = kPartOffset + TEAMS * kTeamPartials * 8;
   static constexpr int kAbortOffset = kBarOffset + (3 * S + 1) * 8;
-  static constexpr int kSmemBytes = kAbortOffset + 16;
+  static constexpr int kRedOffset = kAbortOffset + 16;               // producer: one double per consumer warp
+  static constexpr int kSmemBytes = kRedOffset + (kConsumers / 32) * 8;
   // Two resident CTAs (this kernel + the next of a stream) when the ring is
   // small enough; deep rings take the whole SM.
   static constexpr int kMinBlocks = kSmemBytes <= 112 * 1024 ? 2 : 1;
@@ -212,9 +322,9 @@ struct TeamConfig {
 template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
 __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThreads,
                                   TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kMinBlocks)
-    team_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1,
-                       const uint8_t* __restrict__ q8, float* __restrict__ out0, float* __restrict__ out1,
-                       float* __restrict__ out2, int n_rows, int pdl) {
+    team_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1, const ActSource src,
+                       float* __restrict__ out0, float* __restrict__ out1, float* __restrict__ out2, int n_rows,
+                       int pdl) {
   using C = TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
   constexpr int W = C::kW, RG = C::kRG, T = C::kT, P = C::kP, ROWB = C::kRowBytes;
   constexpr int DECB = Fmt::kDecBytes;
@@ -316,7 +426,11 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
   const int twarp = warp % W;  // warp index inside the team
   pdl_wait_prerequisite();     // the activation may come from the preceding kernel
   MLLB_TRACE_POINT(1);
-  Fmt::template stage_activation<NB>(q8, act, threadIdx.x, C::kConsumers);
+  if (src.x)
+    produce_activation<Fmt, NB, C::kConsumers>(src, act, reinterpret_cast<double*>(smem + C::kRedOffset),
+                                               threadIdx.x);
+  else
+    Fmt::template stage_activation<NB>(src.q8, act, threadIdx.x, C::kConsumers);
   named_barrier(1, C::kConsumers);
   if (threadIdx.x == 0) mbar_arrive(act_ready);
   pdl_launch_dependents();  // with the loader's: the CTA triggers once staged

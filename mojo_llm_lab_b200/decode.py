@@ -38,7 +38,7 @@ import numpy as np
 import torch
 
 from . import formats as F
-from ._lib import LAUNCH_PDL, check, lib
+from ._lib import LAUNCH_PDL, ActF32, check, lib
 from .shard import RowShard
 
 HEAD_DIM = 128
@@ -260,10 +260,9 @@ def parse_state(raw: bytes) -> dict:
 
 @dataclass
 class _Buffers:
-    hidden: torch.Tensor
+    hidden: torch.Tensor      # residual stream, two buffers (norms write the other one)
     q8_hidden: torch.Tensor
     qkv: torch.Tensor
-    q_rot: torch.Tensor
     attn: torch.Tensor
     q8_attn: torch.Tensor
     o_out: torch.Tensor
@@ -287,7 +286,7 @@ class Decoder:
     """
 
     def __init__(self, weights: DecodeWeights, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pdl: bool = True,
-                 group=None):
+                 fused: bool = False, group=None):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
@@ -313,12 +312,19 @@ class Decoder:
             raise ValueError(f"attention shape rejected: {lib().mllb_last_error().decode()}")
         ffn_local = weights.ffn_shard.local_rows
         self.b = _Buffers(
-            hidden=f32(cfg.hidden), q8_hidden=u8(cfg.hidden // 32 * 36), qkv=f32(cfg.qkv_rows),
-            q_rot=f32(cfg.attn_width), attn=f32(cfg.attn_width), q8_attn=u8(cfg.attn_width // 32 * 36),
+            hidden=torch.zeros((2, cfg.hidden), dtype=torch.float32, device=dev), q8_hidden=u8(cfg.hidden // 32 * 36), qkv=f32(cfg.qkv_rows),
+            attn=f32(cfg.attn_width), q8_attn=u8(cfg.attn_width // 32 * 36),
             o_out=f32(cfg.hidden), prod=f32(ffn_local), q8_prod=u8(cfg.ffn // 32 * 36), down_out=f32(cfg.hidden),
             logits=f32(weights.vocab_shard.local_rows),
             state=u8(STATE_BYTES), tokens=torch.zeros(cfg.new_tokens, dtype=torch.int32, device=dev),
             scratch=torch.zeros(scratch_n, dtype=torch.float64, device=dev))
+        if self.world > 1 and fused:
+            self.b.extra["prod_full"] = torch.zeros(cfg.ffn, dtype=torch.float32, device=dev)
+        nb_h, nb_f = cfg.hidden // 256, cfg.ffn // 256
+        # The in-kernel activations need streaming configurations for every
+        # matvec they feed (otherwise the separate norm / quantise kernels run).
+        self.fused = (fused and nb_h in (8, 10, 16) and nb_f in (8, 10, 16, 38)
+                      and weights.vocab_shard.local_rows % 8 == 0)
         self.graph = None
 
     # -- state ------------------------------------------------------------
@@ -337,28 +343,86 @@ class Decoder:
 
     def step(self) -> None:
         """Launch one decode step on the current stream."""
+        if self.fused:
+            self._step_fused()
+        else:
+            self._step_unfused()
+
+    def _step_fused(self) -> None:
+        # Per layer: QKV (norm built in), attention (rope + append built in)
+        # and its combine, O, gate/up (residual + norm built in), down (Q8_1
+        # of the product built in): 6 launches.
         cfg, w, b, L = self.cfg, self.w, self.b, lib()
         s, fl = self._stream(), self.flags
         P = lambda t: t.data_ptr()  # noqa: E731
         state = P(b.state)
+        h = [P(b.hidden[0]), P(b.hidden[1])]
+        cur = 0
         check(L.mllb_decode_embed(P(w.embedding), cfg.vocab, cfg.hidden, state, P(b.tokens), cfg.new_tokens,
-                                  P(b.hidden), fl, s), "decode_embed")
+                                  h[cur], fl, s), "decode_embed")
         ffn_local = w.ffn_shard.local_rows
         for layer, lw in enumerate(w.layers):
             delta = None if layer == 0 else P(b.down_out)
-            check(L.mllb_rmsnorm_q8_1(P(b.hidden), delta, P(b.hidden), P(lw.attn_norm), cfg.eps, P(b.q8_hidden),
-                                      cfg.hidden, 0, fl, s), "attn_norm")
+            out = None if delta is None else h[1 - cur]
+            act = ActF32(h[cur], delta, P(lw.attn_norm), out, cfg.eps, None)
+            check(L.mllb_q4k_matvec_act(P(lw.qkv), act, P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s), "qkv")
+            if out is not None:
+                cur = 1 - cur
+            check(L.mllb_decode_attention_qkv(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
+                                              P(self.k_cache[layer]), P(self.v_cache[layer]), P(b.scratch),
+                                              b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads, cfg.kv_heads,
+                                              cfg.ctx_capacity, fl, s), "attention")
+            check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
+            act = ActF32(h[cur], P(b.o_out), P(lw.ffn_norm), h[1 - cur], cfg.eps, None)
+            check(L.mllb_q4k_gate_up_act(P(lw.up), P(lw.gate), act, None, None, P(b.prod), ffn_local, cfg.hidden,
+                                         fl, s), "gate_up")
+            cur = 1 - cur
+            if self.world > 1:
+                import torch.distributed as dist
+                dist.all_gather_into_tensor(b.extra["prod_full"], b.prod, group=self.group)
+                prod = P(b.extra["prod_full"])
+            else:
+                prod = P(b.prod)
+            check(L.mllb_q4k_matvec_act(P(lw.down), ActF32(prod, None, None, None, 0.0, None), P(b.down_out),
+                                        cfg.hidden, cfg.ffn, fl, s), "down")
+        act = ActF32(h[cur], P(b.down_out), P(w.out_norm), h[1 - cur], cfg.eps, state)
+        check(L.mllb_q6k_matvec_act(P(w.output), act, P(b.logits), w.vocab_shard.local_rows, cfg.hidden, fl, s),
+              "logits")
+        if self.world == 1:
+            check(L.mllb_argmax_f32(P(b.logits), cfg.vocab, 0, state, fl, s), "argmax")
+        else:
+            self._reduce_argmax(s, fl)
+
+    def _step_unfused(self) -> None:
+        cfg, w, b, L = self.cfg, self.w, self.b, lib()
+        s, fl = self._stream(), self.flags
+        P = lambda t: t.data_ptr()  # noqa: E731
+        state = P(b.state)
+        h = [P(b.hidden[0]), P(b.hidden[1])]
+        cur = 0
+        check(L.mllb_decode_embed(P(w.embedding), cfg.vocab, cfg.hidden, state, P(b.tokens), cfg.new_tokens,
+                                  h[cur], fl, s), "decode_embed")
+
+        def norm(delta, gamma, what):
+            # h[cur] + delta -> h[1 - cur]; the Q8_1 of its norm -> q8_hidden.
+            nonlocal cur
+            out = None if delta is None else h[1 - cur]
+            check(L.mllb_rmsnorm_q8_1(h[cur], delta, out, P(gamma), cfg.eps, P(b.q8_hidden), cfg.hidden, 0, fl, s),
+                  what)
+            if out is not None:
+                cur = 1 - cur
+
+        ffn_local = w.ffn_shard.local_rows
+        for layer, lw in enumerate(w.layers):
+            norm(None if layer == 0 else P(b.down_out), lw.attn_norm, "attn_norm")
             check(L.mllb_q4k_matvec_ex(P(lw.qkv), P(b.q8_hidden), P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s),
                   "qkv")
-            check(L.mllb_decode_qk_rope_append(P(b.qkv), P(lw.q_norm), P(lw.k_norm), state, cfg.theta_scale,
-                                               P(b.q_rot), P(self.k_cache[layer]), P(self.v_cache[layer]),
-                                               cfg.q_heads, cfg.kv_heads, cfg.ctx_capacity, fl, s), "qk_rope")
-            check(L.mllb_decode_attention(P(b.q_rot), P(self.k_cache[layer]), P(self.v_cache[layer]), state,
-                                          P(b.scratch), b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads,
-                                          cfg.kv_heads, cfg.ctx_capacity, fl, s), "attention")
+            check(L.mllb_decode_attention_qkv(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
+                                              P(self.k_cache[layer]), P(self.v_cache[layer]), P(b.scratch),
+                                              b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads, cfg.kv_heads,
+                                              cfg.ctx_capacity, fl, s), "attention")
             check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
-            check(L.mllb_rmsnorm_q8_1(P(b.hidden), P(b.o_out), P(b.hidden), P(lw.ffn_norm), cfg.eps,
-                                      P(b.q8_hidden), cfg.hidden, 0, fl, s), "ffn_norm")
+            norm(P(b.o_out), lw.ffn_norm, "ffn_norm")
             check(L.mllb_q4k_gate_up_ex(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod), ffn_local,
                                         cfg.hidden, fl, s), "gate_up")
             if self.world == 1:
@@ -367,7 +431,7 @@ class Decoder:
                 self._gather_prod(s, fl)
             check(L.mllb_q4k_matvec_ex(P(lw.down), P(b.q8_prod), P(b.down_out), cfg.hidden, cfg.ffn, fl, s),
                   "down")
-        check(L.mllb_decode_final_norm(P(b.hidden), P(b.down_out), P(b.hidden), P(w.out_norm), cfg.eps,
+        check(L.mllb_decode_final_norm(h[cur], P(b.down_out), h[1 - cur], P(w.out_norm), cfg.eps,
                                        P(b.q8_hidden), cfg.hidden, state, fl, s), "final_norm")
         check(L.mllb_q6k_matvec_ex(P(w.output), P(b.q8_hidden), P(b.logits), w.vocab_shard.local_rows, cfg.hidden,
                                    fl, s), "logits")
@@ -375,6 +439,15 @@ class Decoder:
             check(L.mllb_argmax_f32(P(b.logits), cfg.vocab, 0, state, fl, s), "argmax")
         else:
             self._reduce_argmax(s, fl)
+
+    def launches_per_step(self) -> int:
+        """Kernels of this library one step launches (collectives not counted)."""
+        # embedding; per layer (fused) QKV, attention split + combine, O,
+        # gate/up, down or (unfused) those plus two norms and the quantiser;
+        # final norm (unfused) and logits; argmax.
+        if self.fused:
+            return 1 + self.cfg.layers * 6 + 1 + 1
+        return 1 + self.cfg.layers * 9 + 2 + 1
 
     # -- sharded pieces -----------------------------------------------------
     def _gather_prod(self, s: int, fl: int) -> None:

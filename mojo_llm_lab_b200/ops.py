@@ -23,12 +23,13 @@ from __future__ import annotations
 import torch
 
 from . import formats as F
-from ._lib import LAUNCH_PDL, S_D_SUMQ, S_SUM_X, check, device_error, lib  # noqa: F401
+from ._lib import LAUNCH_PDL, S_D_SUMQ, S_SUM_X, ActF32, check, device_error, lib  # noqa: F401
 
 __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
     "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
     "rmsnorm_q8_1", "decode_embed", "decode_final_norm", "decode_qk_rope_append", "decode_attention",
+    "decode_attention_qkv", "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32",
     "argmax_key", "token_key", "key_token", "S_D_SUMQ", "S_SUM_X",
 ]
 
@@ -379,6 +380,43 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
     return out, q8
 
 
+def decode_attention_qkv(qkv: torch.Tensor, q_gamma: torch.Tensor, k_gamma: torch.Tensor, state: torch.Tensor,
+                         k_cache: torch.Tensor, v_cache: torch.Tensor, q_heads: int,
+                         theta_scale: float | None = None, out: torch.Tensor | None = None,
+                         q8: torch.Tensor | None = None, scratch: torch.Tensor | None = None, pdl: bool = False):
+    """Fused q/k RMSNorm + IMROPE, KV append at state.pos and attention -> (out fp32, Q8_1 of out)."""
+    _need(qkv, "qkv", torch.float32)
+    _need(q_gamma, "q_gamma", torch.float32)
+    _need(k_gamma, "k_gamma", torch.float32)
+    _need(k_cache, "k_cache", torch.float16)
+    _need(v_cache, "v_cache", torch.float16)
+    _need_state(state)
+    kv_heads, ctx = k_cache.shape[0], k_cache.shape[1]
+    if qkv.numel() != (q_heads + 2 * kv_heads) * F.HEAD_DIM:
+        raise ValueError("qkv must hold (q_heads + 2 kv_heads) x 128 values")
+    if v_cache.shape != k_cache.shape or k_cache.dim() != 3 or k_cache.shape[2] != F.HEAD_DIM:
+        raise ValueError("caches must both be [kv_heads, ctx, 128]")
+    with torch.cuda.device(qkv.device):
+        need = int(lib().mllb_decode_attention_scratch(q_heads, kv_heads, ctx))
+    if need < 0:
+        check(int(need), "decode_attention_scratch")
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.float64, device=qkv.device)
+    _need(scratch, "scratch", torch.float64)
+    width = q_heads * F.HEAD_DIM
+    if out is None:
+        out = torch.empty(width, dtype=torch.float32, device=qkv.device)
+    if q8 is None:
+        q8 = torch.empty(F.q8_1_bytes(width), dtype=torch.uint8, device=qkv.device)
+    theta = F.theta_scale_f32() if theta_scale is None else float(theta_scale)
+    _same_device(qkv, q_gamma, k_gamma, state, k_cache, v_cache, out, q8, scratch)
+    check(lib().mllb_decode_attention_qkv(qkv.data_ptr(), q_gamma.data_ptr(), k_gamma.data_ptr(), theta,
+                                          state.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), scratch.data_ptr(),
+                                          scratch.numel(), out.data_ptr(), q8.data_ptr(), q_heads, kv_heads, ctx,
+                                          _flags(pdl), _stream(qkv)), "decode_attention_qkv")
+    return out, q8
+
+
 def argmax_key(x: torch.Tensor, key: torch.Tensor, index_offset: int = 0, pdl: bool = False) -> torch.Tensor:
     """key[0] = max(key[0], packed (x[i], index_offset + i) over i); key: int64[1]."""
     _need(x, "x", torch.float32)
@@ -387,3 +425,49 @@ def argmax_key(x: torch.Tensor, key: torch.Tensor, index_offset: int = 0, pdl: b
     check(lib().mllb_argmax_f32(x.data_ptr(), x.numel(), index_offset, key.data_ptr(), _flags(pdl), _stream(x)),
           "argmax")
     return key
+
+
+# --------------------------------------------- matvecs with an fp32 activation
+
+def act_f32(x: torch.Tensor, delta: torch.Tensor | None = None, gamma: torch.Tensor | None = None,
+            x_out: torch.Tensor | None = None, eps: float = 1e-6, advance: torch.Tensor | None = None) -> ActF32:
+    """Describe an activation built inside the matvec: Q8_1(rmsnorm(x + delta) * gamma), or
+    Q8_1(x + delta) without gamma; x + delta is stored to x_out; advance is a decode state."""
+    for name, t in (("x", x), ("delta", delta), ("gamma", gamma), ("x_out", x_out)):
+        if t is not None:
+            _need(t, name, torch.float32)
+            if t.numel() != x.numel():
+                raise ValueError(f"{name} must have {x.numel()} values")
+    if advance is not None:
+        _need_state(advance)
+    _same_device(x, delta, gamma, x_out, advance)
+    return ActF32(x.data_ptr(), _ptr(delta), _ptr(gamma), _ptr(x_out), eps, _ptr(advance))
+
+
+def q4k_matvec_act(weights: torch.Tensor, act: ActF32, k: int, output: torch.Tensor, pdl: bool = False):
+    _need(weights, "weights", torch.uint8)
+    _need(output, "output", torch.float32)
+    rows = _rows(weights, F.q4k_row_bytes(k), "Q4_K")
+    check(lib().mllb_q4k_matvec_act(weights.data_ptr(), act, output.data_ptr(), rows, k, _flags(pdl),
+                                    _stream(weights)), "q4k_matvec_act")
+    return output
+
+
+def q4k_gate_up_act(up_weights: torch.Tensor, gate_weights: torch.Tensor, act: ActF32, k: int,
+                    up: torch.Tensor | None = None, gate: torch.Tensor | None = None,
+                    prod: torch.Tensor | None = None, pdl: bool = False):
+    _need(up_weights, "up_weights", torch.uint8)
+    _need(gate_weights, "gate_weights", torch.uint8)
+    rows = _rows(up_weights, F.q4k_row_bytes(k), "Q4_K")
+    check(lib().mllb_q4k_gate_up_act(up_weights.data_ptr(), gate_weights.data_ptr(), act, _ptr(up), _ptr(gate),
+                                     _ptr(prod), rows, k, _flags(pdl), _stream(up_weights)), "q4k_gate_up_act")
+    return up, gate, prod
+
+
+def q6k_matvec_act(weights: torch.Tensor, act: ActF32, k: int, output: torch.Tensor, pdl: bool = False):
+    _need(weights, "weights", torch.uint8)
+    _need(output, "output", torch.float32)
+    rows = _rows(weights, F.q6k_row_bytes(k), "Q6_K")
+    check(lib().mllb_q6k_matvec_act(weights.data_ptr(), act, output.data_ptr(), rows, k, _flags(pdl),
+                                    _stream(weights)), "q6k_matvec_act")
+    return output

@@ -67,16 +67,27 @@ def test_embed_bad_key_reports_and_uses_row_zero(orc):
 
 @pytest.mark.parametrize("k,with_delta,scale", [(2560, True, 1.0), (2560, False, 1.0), (4096, True, 1e4),
                                                 (32, True, 1e-3), (9728, False, 30.0), (32768, True, 1.0)])
-def test_rmsnorm_q8_1_bit_exact(orc, k, with_delta, scale):
+@pytest.mark.parametrize("in_place", [True, False])
+def test_rmsnorm_q8_1_bit_exact(orc, k, with_delta, scale, in_place):
     rng = np.random.default_rng(k)
     x = (rng.standard_normal(k) * scale).astype(np.float32)
     delta = (rng.standard_normal(k) * scale).astype(np.float32) if with_delta else None
     gamma = rng.uniform(0.5, 1.5, k).astype(np.float32)
     xd = dev(x)
-    q8 = ops.rmsnorm_q8_1(xd, dev(gamma), None if delta is None else dev(delta), x_out=xd)
+    out = xd if in_place else torch.full((k,), 9.0, device="cuda")
+    q8 = ops.rmsnorm_q8_1(xd, dev(gamma), None if delta is None else dev(delta), x_out=out)
     h_ref, q8_ref = orc.rmsnorm_q8_1(x, delta, gamma)
-    assert np.array_equal(xd.cpu().numpy(), h_ref)
+    assert np.array_equal(out.cpu().numpy(), h_ref)
     assert np.array_equal(q8.cpu().numpy(), q8_ref)
+    if not in_place:
+        assert np.array_equal(xd.cpu().numpy(), x)
+
+
+def test_rmsnorm_rejects_partial_overlap():
+    buf = torch.zeros(4096 + 32, device="cuda")
+    g = torch.ones(4096, device="cuda")
+    with pytest.raises(Exception):
+        ops.rmsnorm_q8_1(buf[:4096], g, x_out=buf[32:])
 
 
 def test_rmsnorm_zero_input_and_rejects_bad_k():
@@ -165,6 +176,49 @@ def test_attention_against_oracle(orc, hq, hkv, ctx, pos):
     assert exact > 0.999, exact
     assert np.array_equal(q8.cpu().numpy(), np.frombuffer(orc.quantize_q8_1(got), dtype=np.uint8))
     assert ops.device_error() == 0
+
+
+@pytest.mark.parametrize("hq,hkv,ctx,pos", [
+    (32, 8, 4224, 4096), (32, 8, 4224, 0), (32, 8, 4224, 63), (32, 8, 4224, 64), (32, 8, 4224, 4223),
+    (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 1000), (4, 4, 5000, 4999), (16, 2, 64, 63)])
+def test_fused_rope_append_attention(orc, hq, hkv, ctx, pos):
+    """decode_attention_qkv == qk_rope_append + attention, cache rows included."""
+    k, v = random_cache(hkv, ctx, seed=ctx * 3 + pos)
+    rng = np.random.default_rng(pos + 11)
+    qkv = (rng.standard_normal((hq + 2 * hkv) * 128) * 30).astype(np.float32)
+    qg = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kg = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kd, vd = dev(k), dev(v)
+    theta = F.theta_scale_f32()
+    out, q8 = ops.decode_attention_qkv(dev(qkv), dev(qg), dev(kg), state_tensor(pos=pos), kd, vd, hq, theta)
+    q_ref, k_row, v_row = orc.qk_rope_append(qkv, hq, hkv, qg, kg, pos, theta)
+    kh, vh = k.view(np.uint16).copy(), v.view(np.uint16).copy()
+    kh[:, pos, :] = k_row.reshape(hkv, 128)
+    vh[:, pos, :] = v_row.reshape(hkv, 128)
+    ref = orc.attention(q_ref, kh, vh, pos + 1, hq, hkv)
+    got = out.cpu().numpy()
+    assert_within_tolerance(got, ref, f"fused attention pos={pos}")
+    assert (got.view(np.uint32) == ref.view(np.uint32)).mean() > 0.999
+    assert np.array_equal(q8.cpu().numpy(), np.frombuffer(orc.quantize_q8_1(got), dtype=np.uint8))
+    got_k = kd.cpu().numpy().view(np.uint16)
+    assert (got_k[:, pos] == kh[:, pos]).mean() > 0.999
+    assert np.array_equal(vd.cpu().numpy().view(np.uint16), vh)
+    others = np.ones(ctx, dtype=bool)
+    others[pos] = False
+    assert np.array_equal(got_k[:, others], kh[:, others])
+    assert ops.device_error() == 0
+
+
+def test_fused_attention_overflow_appends_nothing():
+    hq, hkv, ctx = 8, 4, 40
+    k, v = random_cache(hkv, ctx, seed=2)
+    kd, vd = dev(k), dev(v)
+    qkv = torch.ones((hq + 2 * hkv) * 128, device="cuda")
+    g = torch.ones(128, device="cuda")
+    out, _ = ops.decode_attention_qkv(qkv, g, g, state_tensor(pos=ctx), kd, vd, hq)
+    assert ops.device_error(clear=True) & 16
+    assert np.array_equal(kd.cpu().numpy(), k) and np.array_equal(vd.cpu().numpy(), v)
+    assert torch.isfinite(out).all()
 
 
 def test_attention_peaked_and_subnormal_values(orc):

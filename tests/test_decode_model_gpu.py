@@ -31,13 +31,14 @@ def host_cache(t):
     return t.cpu().numpy().view(np.uint16).copy()
 
 
-def run_against_oracle(cfg, steps, token=17, graph=False):
+def run_against_oracle(cfg, steps, token=17, graph=False, fused=True):
     w, k, v = build(cfg)
     host = OD.host_model(w)
     kh, vh = host_cache(k), host_cache(v)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        dec = D.Decoder(w, k, v)
+        dec = D.Decoder(w, k, v, fused=fused)
+        assert dec.fused == fused
         dec.reset(token)
         if graph:
             dec.capture()
@@ -62,8 +63,9 @@ def run_against_oracle(cfg, steps, token=17, graph=False):
 
 
 @pytest.mark.parametrize("cfg", [SMALL, ODD], ids=["qwen-2layer", "odd-shapes"])
-def test_decode_steps_match_oracle(orc, cfg):
-    run_against_oracle(cfg, steps=3)
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "unfused"])
+def test_decode_steps_match_oracle(orc, cfg, fused):
+    run_against_oracle(cfg, steps=3, fused=fused)
 
 
 def test_graph_replay_matches_oracle(orc):

@@ -76,3 +76,66 @@ def test_sharded_over_all_gpus(kind, rows):
             p.kill()
     assert codes == [0] * world, codes
     assert q.get(timeout=10) is True
+
+
+def _spawn(target, world, *args):
+    ctx = mp.get_context("spawn")
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    codes = [p.exitcode for p in procs]
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    assert codes == [0] * world, codes
+
+
+def _decode_worker(rank, world, port, out):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from mojo_llm_lab_b200 import decode as D
+        cfg = D.DecodeConfig(layers=2, vocab=4096, context=300, new_tokens=6)
+        w = D.generate_weights(cfg, "cuda", world=world, rank=rank)
+        k, v = D.generate_kv_cache(cfg, "cuda")
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            dec = D.Decoder(w, k, v, group=dist.group.WORLD)
+            dec.reset(17)
+            dec.capture()
+            tokens = dec.generate(17, 5)
+            logits = torch.empty(w.vocab_shard.per_rank * world, device="cuda")
+            dist.all_gather_into_tensor(logits, dec.b.logits)
+            s.synchronize()
+            dec.graph = None
+        if rank == 0:
+            torch.save({"tokens": tokens, "logits": logits[:cfg.vocab].cpu()}, out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_decode_matches_single_gpu(tmp_path):
+    """gate/up + vocab row-sharded over the GPUs: the same tokens and logits as one GPU."""
+    import torch
+    from mojo_llm_lab_b200 import decode as D
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    out = tmp_path / "decode.pt"
+    _spawn(_decode_worker, world, out)
+    got = torch.load(out)
+    cfg = D.DecodeConfig(layers=2, vocab=4096, context=300, new_tokens=6)
+    w = D.generate_weights(cfg, "cuda")
+    k, v = D.generate_kv_cache(cfg, "cuda")
+    dec = D.Decoder(w, k, v)
+    tokens = dec.generate(17, 5)
+    assert got["tokens"] == tokens
+    assert torch.equal(got["logits"], dec.b.logits.cpu())
