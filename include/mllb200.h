@@ -298,6 +298,23 @@ int mllb_decode_attention_qkv(const float *qkv, const float *q_gamma, const floa
                               int64_t ctx, unsigned flags, void *stream);
 
 /*
+ * mllb_decode_attention_qkv without a scratch argument: the chunk partials go
+ * to a 1 MiB array inside the library (q_heads x splits x 130 doubles must
+ * fit in 131072; the decode shape, 32 heads x 18 chunks, uses 74880).  For
+ * callers that cannot allocate a buffer (an interposer that only sees the
+ * host framework's tensors and stream).  No counterpart in the reference.
+ * Allocates nothing: the array's device address is looked up once per device
+ * (cudaGetSymbolAddress) on the first call with that device current, so make
+ * one call per device before capturing a stream.  Nothing in the array needs
+ * to start at zero.  Calls that overlap in time share the array and race;
+ * larger shapes return MLLB_EUNSUPPORTED.
+ */
+int mllb_decode_attention_qkv_noalloc(const float *qkv, const float *q_gamma, const float *k_gamma,
+                                      double theta_scale, const mllb_decode_state *state, void *k_cache,
+                                      void *v_cache, float *out, void *q8, int64_t q_heads, int64_t kv_heads,
+                                      int64_t ctx, unsigned flags, void *stream);
+
+/*
  * *key = max(*key, max over i of key(x[i], index_offset + i)) with the packed
  * key of mllb_token_key (the greedy argmax; for a row shard pass the shard's
  * first row as index_offset).  *key must hold INT64_MIN or an earlier

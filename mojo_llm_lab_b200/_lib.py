@@ -65,6 +65,8 @@ SIGNATURES = {
     "mllb_decode_attention": (C.c_int, [_P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, C.c_uint, _P]),
     "mllb_decode_attention_qkv": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64,
                                             C.c_uint, _P]),
+    "mllb_decode_attention_qkv_noalloc": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _P, _I64, _I64, _I64,
+                                                    C.c_uint, _P]),
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
     "mllb_q4k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),

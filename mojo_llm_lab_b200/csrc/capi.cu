@@ -555,6 +555,32 @@ int attention_impl(AttentionArgs a, double* scratch, int64_t scratch_doubles, fl
                   "attention combine kernel");
 }
 
+// Scratch of mllb_decode_attention_qkv_noalloc: chunk partials in a
+// file-scope device array (1 MiB), so that entry allocates nothing.  Every
+// partial is written before it is read within a call: nothing needs to start
+// at zero.  Calls that overlap in time (other streams, other host threads)
+// share it and would race.
+constexpr int64_t kNoAllocScratchDoubles = 131072;
+static __device__ __align__(256) double g_attn_noalloc_scratch[kNoAllocScratchDoubles];
+
+// Device address of g_attn_noalloc_scratch for the current device, looked up
+// with cudaGetSymbolAddress on the first call per device and cached.
+int noalloc_scratch(double** out) {
+  static double* cache[kMaxDevices] = {nullptr};
+  static std::mutex m;
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  std::lock_guard<std::mutex> lock(m);
+  if (!cache[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess) return fail(MLLB_ECUDA, "cudaGetSymbolAddress(attention scratch): %s", cudaGetErrorString(e));
+    cache[dev] = static_cast<double*>(p);
+  }
+  *out = cache[dev];
+  return MLLB_OK;
+}
+
 int rmsnorm_q8_1_launch(const float* x, const float* delta, float* x_out, const float* gamma, double eps, void* q8,
                         int64_t k, int s_mode, mllb::DecodeState* advance, unsigned flags, void* stream) {
   if (!x || !gamma || !q8) return fail(MLLB_EINVAL, "null pointer");
@@ -754,3 +780,22 @@ int mllb_q6k_matvec_act(const void* weights, const mllb_act_f32* act, float* out
 }
 
 }  // extern "C"
+
+extern "C" int mllb_decode_attention_qkv_noalloc(const float* qkv, const float* q_gamma, const float* k_gamma,
+                                                 double theta_scale, const mllb_decode_state* state, void* k_cache,
+                                                 void* v_cache, float* out, void* q8, int64_t q_heads,
+                                                 int64_t kv_heads, int64_t ctx, unsigned flags, void* stream) {
+  const int64_t need = mllb_decode_attention_scratch(q_heads, kv_heads, ctx);
+  if (need < 0) return static_cast<int>(need);
+  if (need > kNoAllocScratchDoubles)
+    return fail(MLLB_EUNSUPPORTED,
+                "attention needs %lld doubles of scratch for q_heads=%lld kv_heads=%lld ctx=%lld; the built-in "
+                "scratch holds %lld (use mllb_decode_attention_qkv with a caller buffer)",
+                static_cast<long long>(need), static_cast<long long>(q_heads), static_cast<long long>(kv_heads),
+                static_cast<long long>(ctx), static_cast<long long>(kNoAllocScratchDoubles));
+  double* scratch = nullptr;
+  const int rc = noalloc_scratch(&scratch);
+  if (rc) return rc;
+  return mllb_decode_attention_qkv(qkv, q_gamma, k_gamma, theta_scale, state, k_cache, v_cache, scratch, need, out,
+                                   q8, q_heads, kv_heads, ctx, flags, stream);
+}
