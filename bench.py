@@ -26,6 +26,13 @@ start of the step), replaying one captured CUDA graph per token.  Metric:
 tokens/s of the whole job; with N ranks the gate/up and vocabulary matvecs
 are row-sharded (NCCL all-gather / all-reduce) and every rank decodes the
 same token stream (strong scaling).
+
+--workload imrope: the fused RMSNorm + gamma + IMROPE op of configs[0] (32
+heads x 128 fp32, gamma[128], runtime fp32 theta scale 0x3f492c27, positions
+(7, 13, 29, 0)): µs/op over a CUDA graph of 128 serial launches on 128
+distinct input copies (the reference's measurement, benchmark/bench.c:33);
+--workload imrope_batched: the same op over 4096 tokens x 32 heads (134 MB
+per launch, HBM-bound throughput mode).  One GPU; N ranks are replicas.
 """
 from __future__ import annotations
 
@@ -647,13 +654,222 @@ def run_decode(args, rank: int, world: int):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- IMROPE workloads
+
+
+def run_imrope_reference(args, rank: int, world: int, batched: bool):
+    if rank != 0:
+        return
+    c = imrope_cpu_reference(4096 if batched else 1, target_s=max(3.0, min(20.0, args.steps)))
+    if batched:
+        value, unit, hib = imrope_bytes(1) / c["per_token_s"] / 1e9, "GB/s", True
+        metric = "fused RMSNorm+gamma+IMROPE throughput (4096 tokens x 32 heads x 128) GB/s"
+    else:
+        value, unit, hib = c["us_per_token_op"], "us/op", False
+        metric = "fused RMSNorm+gamma+IMROPE 32x128 us/op"
+    line = {"metric": metric, "value": round(value, 4), "unit": unit, "impl": "reference", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": c["per_token_s"] * 1e3,
+            "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
+            "data": "synthetic (seeded)", "config": {"workload": "imrope batched" if batched else "imrope 32x128"},
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": 1, "kind": "port",
+                             "sample": c["sample"]},
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+IMROPE_PUBLISHED_US = 2.072   # reference, Mojo fused kernel on RTX A2000 (README.md:17-21)
+
+
+def imrope_bytes(tokens: int, heads: int = 32) -> int:
+    """q in + out (fp32) + gamma + positions + theta scale."""
+    return tokens * heads * 128 * 4 * 2 + 128 * 4 + tokens * 16 + 4
+
+
+def imrope_cpu_reference(tokens: int, target_s: float = 5.0):
+    import oracle
+    from mojo_llm_lab_b200 import fixtures as fx
+
+    inp = fx.imrope_seeded_inputs(fx.SEEDED_IMROPE_CASES["distinct_axes"], seed=1)
+    theta = oracle.runtime_theta_scale()
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < target_s:
+        oracle.imrope(inp["q"], inp["gamma"], inp["positions_axis_major"], theta)
+        reps += 1
+    el = time.perf_counter() - t0
+    per_token = el / reps
+    return {"us_per_token_op": per_token * 1e6, "cores": 1, "kind": "port",
+            "sample": f"{reps} x (32 heads x 128, one token) in {el:.1f} s (oracle/oracle.c orc_imrope, 1 thread)",
+            "per_token_s": per_token}
+
+
+def run_imrope(args, rank: int, world: int, batched: bool):
+    import torch
+    import torch.distributed as dist
+
+    from mojo_llm_lab_b200 import fixtures as fx
+    from mojo_llm_lab_b200 import formats as F
+    from mojo_llm_lab_b200 import ops
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    tokens, heads = (4096, 32) if batched else (1, 32)
+    copies = 4 if batched else 128
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    inp = fx.imrope_seeded_inputs(fx.SEEDED_IMROPE_CASES["distinct_axes"], seed=1, heads=heads * tokens)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(5)
+    qs = [torch.from_numpy(inp["q"]).to(device).view(-1)]
+    qs += [torch.randn(tokens * heads * 128, generator=gen, device=device) for _ in range(copies - 1)]
+    gamma = torch.from_numpy(inp["gamma"]).to(device)
+    pos = torch.tensor(list(fx.SEEDED_IMROPE_CASES["distinct_axes"]) * tokens, dtype=torch.int32, device=device)
+    theta = torch.tensor([F.theta_scale_f32()], dtype=torch.float32, device=device)
+    outs = torch.empty(copies, tokens * heads * 128, device=device)
+
+    def launch(i, pdl=True):
+        # PDL-chained through the batched entry (theta from device memory, as
+        # the reference ABI passes it); pdl=False is the reference entry.
+        if batched or pdl:
+            ops.rmsnorm_imrope_q(qs[i], gamma, pos, theta, out=outs[i], heads_per_token=heads, pdl=pdl)
+        else:
+            ops.fused_q_imrope_runtime_fastpow(qs[i], gamma, pos, outs[i], theta)
+
+    # Correctness gate: the three position cases of configs[0] against the oracle.
+    if not args.skip_check:
+        import oracle
+        for name, case in fx.SEEDED_IMROPE_CASES.items():
+            c = fx.imrope_seeded_inputs(case, seed=2)
+            got = ops.fused_q_imrope_runtime_fastpow(
+                torch.from_numpy(c["q"]).to(device).view(-1), torch.from_numpy(c["gamma"]).to(device),
+                torch.tensor(case, dtype=torch.int32, device=device), torch.empty(32 * 128, device=device), theta)
+            ref = oracle.imrope(c["q"], c["gamma"], case, oracle.runtime_theta_scale())
+            g = got.cpu().numpy().astype(np.float64).reshape(ref.shape)
+            if not np.all(np.abs(g - ref) <= 1e-5 + 1e-5 * np.abs(ref)):
+                raise SystemExit(f"IMROPE correctness gate failed ({name})")
+        if batched:
+            launch(0)
+            torch.cuda.synchronize()
+            ref = oracle.imrope(inp["q"][:heads], inp["gamma"], list(fx.SEEDED_IMROPE_CASES["distinct_axes"]),
+                                oracle.runtime_theta_scale())
+            g = outs[0][:heads * 128].cpu().numpy().astype(np.float64).reshape(ref.shape)
+            if not np.all(np.abs(g - ref) <= 1e-5 + 1e-5 * np.abs(ref)):
+                raise SystemExit("IMROPE batched correctness gate failed")
+
+    for i in range(copies):
+        launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(copies):
+            launch(i)
+    # The reference's own measurement: serial launches of its entry in a graph.
+    serial = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(serial, stream=stream):
+        for i in range(copies):
+            launch(i, pdl=False)
+    for _ in range(args.warmup):
+        graph.replay()
+        serial.replay()
+    torch.cuda.synchronize()
+    s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s0.record(stream)
+    for _ in range(args.steps):
+        serial.replay()
+    s1.record(stream)
+    torch.cuda.synchronize()
+    serial_us = s0.elapsed_time(s1) / args.steps * 1e3 / copies
+    del serial
+    t0 = time.perf_counter()
+    while time.perf_counter() - t0 < 0.3:  # load before the timed region (clock samples)
+        graph.replay()
+        torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_op = ms * 1e3 / copies
+    per_op = imrope_bytes(tokens, heads)
+    gbs = per_op / (us_op * 1e-6) / 1e9
+
+    # e2e through the public API with host buffers: H2D of q, the op, D2H of the output.
+    q_pin = torch.from_numpy(inp["q"]).reshape(-1).pin_memory()
+    out_pin = torch.empty(tokens * heads * 128, dtype=torch.float32).pin_memory()
+    q_stage = torch.empty(tokens * heads * 128, device=device)
+    e_times = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        for _ in range(copies if not batched else 1):
+            q_stage.copy_(q_pin, non_blocking=True)
+            if batched:
+                ops.rmsnorm_imrope_q(q_stage, gamma, pos, theta, out=outs[0], heads_per_token=heads)
+            else:
+                ops.fused_q_imrope_runtime_fastpow(q_stage, gamma, pos, outs[0], theta)
+            out_pin.copy_(outs[0], non_blocking=True)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e_times.append((time.perf_counter() - t1) / (copies if not batched else 1))
+    e_us = statistics.median(e_times) * 1e6
+    if ops.device_error():
+        raise SystemExit("device error word set")
+    del graph
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        c = imrope_cpu_reference(tokens)
+        cpu = ({"value": round(c["us_per_token_op"], 3), "unit": "us/op", "cores": 1, "kind": "port",
+                "sample": c["sample"]} if not batched else
+               {"value": round(imrope_bytes(1, heads) / c["per_token_s"] / 1e9, 4), "unit": "GB/s", "cores": 1,
+                "kind": "port", "sample": c["sample"]})
+    if batched:
+        value, unit, hib = round(gbs, 2), "GB/s", True
+        e2e = {"value": round(per_op / (e_us * 1e-6) / 1e9, 2), "unit": "GB/s"}
+        metric = "fused RMSNorm+gamma+IMROPE throughput (4096 tokens x 32 heads x 128) GB/s"
+    else:
+        value, unit, hib = round(us_op, 4), "us/op", False
+        e2e = {"value": round(e_us, 3), "unit": "us/op"}
+        metric = "fused RMSNorm+gamma+IMROPE 32x128 us/op"
+    e2e.update({"h2d_bytes_per_step": tokens * heads * 512 * (1 if batched else copies),
+                "d2h_bytes_per_step": tokens * heads * 512 * (1 if batched else copies),
+                "path": "ops.fused_q_imrope_runtime_fastpow / ops.rmsnorm_imrope_q with pinned H2D/D2H, eager"})
+    line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
+            "scaling": "weak", "vs_baseline": None if batched else round(us_op / IMROPE_PUBLISHED_US, 4),
+            "dtype": "f32 in/out, f64 norm and angles", "data": "synthetic (seeded N(0,1) q, U(0.5,1.5) gamma)",
+            "config": {"workload": ("imrope batched" if batched else "imrope 32x128"), "tokens": tokens,
+                       "heads": heads, "launches_per_step": copies, "us_per_op": round(us_op, 4),
+                       "bytes_per_op": per_op, "positions": list(fx.SEEDED_IMROPE_CASES["distinct_axes"]),
+                       "chain": "PDL-chained launches in one CUDA graph",
+                       "us_per_op_serial_graph": round(serial_us, 4),
+                       "l2": ("4 copies x 67 MB in > 2x L2; no flush" if batched else
+                              "128 distinct 16 KB inputs (L2-resident, like the reference's graph)"),
+                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
+            "e2e": e2e,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 5), "peak_source": peak_kind, "traffic": None,
+                         "kernel": "imrope_q_kernel", "us_per_launch": round(us_op, 4)},
+            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode"], default="q4k_matvec")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched"],
+                    default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
     ap.add_argument("--copies", type=int, default=0)
     ap.add_argument("--no-pdl", action="store_true")
@@ -668,10 +884,14 @@ def main():
     if args.impl == "reference":
         if args.workload == "decode":
             run_decode_reference(args, rank, world)
+        elif args.workload.startswith("imrope"):
+            run_imrope_reference(args, rank, world, batched=args.workload == "imrope_batched")
         else:
             run_reference(args, rank, world)
         return
-    runner = run_decode if args.workload == "decode" else run_ours
+    runner = {"decode": run_decode,
+              "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
+              "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True)}.get(args.workload, run_ours)
     if world > 1:
         import datetime
 

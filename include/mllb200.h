@@ -137,6 +137,11 @@ int mllb_rmsnorm_imrope_q(const float *q, const float *gamma, const int32_t *pos
 int mllb_rmsnorm_imrope_q_batched(const float *q, const float *gamma, const int32_t *positions,
                                   const float *theta_scale, double theta_value, float *out, int64_t tokens,
                                   int64_t heads_per_token, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL: the kernel may start while the
+ * preceding kernel runs; it waits for it before reading anything). */
+int mllb_rmsnorm_imrope_q_batched_ex(const float *q, const float *gamma, const int32_t *positions,
+                                     const float *theta_scale, double theta_value, float *out, int64_t tokens,
+                                     int64_t heads_per_token, unsigned flags, void *stream);
 
 /*
  * Exact integer parts of the Q4_K x Q8_1 dot: dots[r * (k/32) + G] =

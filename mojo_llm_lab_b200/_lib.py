@@ -51,6 +51,7 @@ SIGNATURES = {
     "mllb_q6k_matvec": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
     "mllb_rmsnorm_imrope_q": (C.c_int, [_P, _P, _P, _P, _P, _I64, _P]),
     "mllb_rmsnorm_imrope_q_batched": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _I64, _I64, _P]),
+    "mllb_rmsnorm_imrope_q_batched_ex": (C.c_int, [_P, _P, _P, _P, C.c_double, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_subdots": (C.c_int, [_P, _P, _P, _P, _I64, _I64, _P]),
     "mllb_stream_read": (C.c_int, [_P, _I64, _P, _I64, _P]),
     "mllb_q8_1_quantize_ex": (C.c_int, [_P, _P, _I64, C.c_int, C.c_uint, _P]),

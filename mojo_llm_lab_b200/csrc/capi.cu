@@ -401,17 +401,26 @@ int mllb_q6k_matvec_ex(const void* weights, const void* q8, float* out, int64_t 
 int mllb_rmsnorm_imrope_q_batched(const float* q, const float* gamma, const int32_t* positions,
                                   const float* theta_scale, double theta_value, float* out, int64_t tokens,
                                   int64_t heads_per_token, void* stream) {
+  return mllb_rmsnorm_imrope_q_batched_ex(q, gamma, positions, theta_scale, theta_value, out, tokens, heads_per_token,
+                                          0u, stream);
+}
+
+int mllb_rmsnorm_imrope_q_batched_ex(const float* q, const float* gamma, const int32_t* positions,
+                                     const float* theta_scale, double theta_value, float* out, int64_t tokens,
+                                     int64_t heads_per_token, unsigned flags, void* stream) {
   if (!q || !gamma || !positions || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   if (tokens <= 0 || heads_per_token <= 0) return fail(MLLB_EINVAL, "empty shape");
   if (!aligned(q, 4) || !aligned(gamma, 4) || !aligned(positions, 4) || !aligned(out, 4) ||
       (theta_scale && !aligned(theta_scale, 4)))
     return fail(MLLB_EALIGN, "fp32/int32 pointers must be 4-byte aligned");
-  const int64_t heads = tokens * heads_per_token;
-  int64_t grid = (heads + 3) / 4;
-  if (grid > 65535) grid = 65535;
-  mllb::imrope_q_kernel<<<static_cast<int>(grid), 128, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, gamma, positions, theta_scale, theta_value, out, heads, heads_per_token);
-  return check_launch("imrope kernel");
+  const int64_t grid =
+      tokens * ((heads_per_token + mllb::kImropeHeadsPerCta - 1) / mllb::kImropeHeadsPerCta);
+  if (grid > 0x7fffffff) return fail(MLLB_EUNSUPPORTED, "too many heads");
+  return launched(launch(mllb::imrope_q_kernel, dim3(static_cast<unsigned>(grid)), dim3(mllb::kImropeHeadsPerCta * 32),
+                         0, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, q, gamma, positions,
+                         theta_scale, theta_value, out, tokens, heads_per_token),
+                  "imrope kernel");
 }
 
 int mllb_rmsnorm_imrope_q(const float* q, const float* gamma, const int32_t* positions, const float* theta_scale,

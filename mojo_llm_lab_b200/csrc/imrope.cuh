@@ -67,10 +67,11 @@ __device__ __forceinline__ double2 imrope_rotation(int p, int32_t p0, int32_t p1
   return make_double2(c, s);
 }
 
-// imrope_head_values with the 64 rotations precomputed (rot[p] = (cos, sin)).
-__device__ __forceinline__ void imrope_head_table(const float* __restrict__ x, const float* __restrict__ gamma,
-                                                  const double2* rot, int lane, double (&o)[4]) {
-  const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+// imrope_head_values with the 64 rotations precomputed (rot[p] = (cos, sin)),
+// from values already in registers: lane l holds x[l + 32 i] and gamma[l + 32 i].
+__device__ __forceinline__ void imrope_head_regs(float x0, float x1, float x2, float x3, float g0, float g1,
+                                                 float g2, float g3, const double2* rot, int lane,
+                                                 double (&o)[4]) {
   double ss = static_cast<double>(x0) * x0;
   ss = fma(static_cast<double>(x1), static_cast<double>(x1), ss);
   ss = fma(static_cast<double>(x2), static_cast<double>(x2), ss);
@@ -79,13 +80,19 @@ __device__ __forceinline__ void imrope_head_table(const float* __restrict__ x, c
   const double r = 1.0 / sqrt(ss / kHeadDim + 1e-6);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
-    const int p = lane + 32 * half;
-    const double2 cs = rot[p];
-    const double ya = static_cast<double>(half ? x1 : x0) * r * static_cast<double>(gamma[p]);
-    const double yb = static_cast<double>(half ? x3 : x2) * r * static_cast<double>(gamma[p + 64]);
+    const double2 cs = rot[lane + 32 * half];
+    const double ya = static_cast<double>(half ? x1 : x0) * r * static_cast<double>(half ? g1 : g0);
+    const double yb = static_cast<double>(half ? x3 : x2) * r * static_cast<double>(half ? g3 : g2);
     o[2 * half] = ya * cs.x - yb * cs.y;
     o[2 * half + 1] = ya * cs.y + yb * cs.x;
   }
+}
+
+// imrope_head_regs loading the head's values itself.
+__device__ __forceinline__ void imrope_head_table(const float* __restrict__ x, const float* __restrict__ gamma,
+                                                  const double2* rot, int lane, double (&o)[4]) {
+  imrope_head_regs(x[lane], x[lane + 32], x[lane + 64], x[lane + 96], gamma[lane], gamma[lane + 32],
+                   gamma[lane + 64], gamma[lane + 96], rot, lane, o);
 }
 
 // One head, computed by the 32 lanes of the calling warp, stored as fp32.
@@ -100,25 +107,48 @@ __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, co
   out[lane + 96] = static_cast<float>(o[3]);
 }
 
-// Grid-stride over heads, one warp each.  Head h belongs to token
-// h / heads_per_token and uses that token's 4 positions.  The theta scale
-// comes from device memory (fp32, the reference ABI) unless theta_ptr is null,
-// in which case theta_value is used.
-__global__ void __launch_bounds__(128) imrope_q_kernel(const float* __restrict__ q, const float* __restrict__ gamma,
-                                                       const int32_t* __restrict__ positions,
-                                                       const float* __restrict__ theta_ptr, double theta_value,
-                                                       float* __restrict__ out, int64_t heads,
-                                                       int64_t heads_per_token) {
-  const int lane = threadIdx.x & 31;
+// One CTA per (token, group of up to 8 heads), one warp per head.  Every
+// head of a token shares its 4 positions, so the CTA first builds the 64
+// rotations (one fp64 pow + sincos per thread) and the warps then only
+// normalise and rotate.  Head h belongs to token h / heads_per_token and
+// uses that token's 4 positions.  The theta scale comes from device memory
+// (fp32, the reference ABI) unless theta_ptr is null, in which case
+// theta_value is used.
+constexpr int kImropeHeadsPerCta = 8;
+
+__global__ void __launch_bounds__(kImropeHeadsPerCta * 32) imrope_q_kernel(
+    const float* __restrict__ q, const float* __restrict__ gamma, const int32_t* __restrict__ positions,
+    const float* __restrict__ theta_ptr, double theta_value, float* __restrict__ out, int64_t tokens,
+    int64_t heads_per_token) {
+  __shared__ double2 rot[kHeadDim / 2];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t ctas_per_token = (heads_per_token + kImropeHeadsPerCta - 1) / kImropeHeadsPerCta;
+  const int64_t token = blockIdx.x / ctas_per_token;
+  const int64_t h = (blockIdx.x % ctas_per_token) * kImropeHeadsPerCta + warp;
   pdl_wait_prerequisite();
   pdl_launch_dependents();
-  const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
-  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-  for (int64_t h = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); h < heads;
-       h += warps) {
-    imrope_head_warp(q + h * kHeadDim, gamma, positions + 4 * (h / heads_per_token), theta, out + h * kHeadDim,
-                     lane);
+  if (token >= tokens) return;
+  // The head's values are loaded first, so their latency overlaps the
+  // rotation table's pow / sincos.
+  const bool active = h < heads_per_token;
+  const size_t head = static_cast<size_t>(token * heads_per_token + (active ? h : 0));
+  const float* x = q + head * kHeadDim;
+  const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
+  const float g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
+  if (threadIdx.x < kHeadDim / 2) {
+    const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
+    const int32_t* pos = positions + 4 * token;
+    rot[threadIdx.x] = imrope_rotation(threadIdx.x, pos[0], pos[1], pos[2], pos[3], theta);
   }
+  __syncthreads();
+  if (!active) return;
+  double o[4];
+  imrope_head_regs(x0, x1, x2, x3, g0, g1, g2, g3, rot, lane, o);
+  float* dst = out + head * kHeadDim;
+  dst[lane] = static_cast<float>(o[0]);
+  dst[lane + 64] = static_cast<float>(o[1]);
+  dst[lane + 32] = static_cast<float>(o[2]);
+  dst[lane + 96] = static_cast<float>(o[3]);
 }
 
 }  // namespace mllb

@@ -509,3 +509,37 @@ class Decoder:
         st = self.read_state()
         seen = self.b.tokens[:n].cpu().tolist()
         return seen[1:] + [st["next_token"]]
+
+
+def main(argv=None) -> None:
+    """python -m mojo_llm_lab_b200.decode: run greedy decode steps of the
+    synthetic stack on the current GPU and print the tokens and µs/token."""
+    import argparse
+    import time
+
+    ap = argparse.ArgumentParser(description=main.__doc__)
+    ap.add_argument("--steps", type=int, default=2)
+    ap.add_argument("--layers", type=int, default=36)
+    ap.add_argument("--graph", action="store_true", help="replay one captured CUDA graph per token")
+    ap.add_argument("--fused", action="store_true", help="activations built inside the matvecs")
+    ap.add_argument("--no-pdl", action="store_true")
+    args = ap.parse_args(argv)
+    cfg = DecodeConfig(layers=args.layers)
+    w = generate_weights(cfg, "cuda")
+    k, v = generate_kv_cache(cfg, "cuda")
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dec = Decoder(w, k, v, pdl=not args.no_pdl, fused=args.fused)
+        dec.reset(17)
+        if args.graph:
+            dec.capture()
+            dec.reset(17)
+        stream.synchronize()
+        t0 = time.perf_counter()
+        tokens = dec.generate(17, args.steps)
+        el = time.perf_counter() - t0
+    print(f"tokens {tokens}  {el / args.steps * 1e6:.1f} us/token (host clock, {'graph' if args.graph else 'eager'})")
+
+
+if __name__ == "__main__":
+    main()

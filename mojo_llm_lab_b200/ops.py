@@ -196,7 +196,7 @@ def fused_q_imrope_runtime_fastpow(q: torch.Tensor, gamma: torch.Tensor, positio
 
 def rmsnorm_imrope_q(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tensor,
                      theta_scale: torch.Tensor | float | None = None, out: torch.Tensor | None = None,
-                     heads_per_token: int | None = None) -> torch.Tensor:
+                     heads_per_token: int | None = None, pdl: bool = False) -> torch.Tensor:
     """Batched form: q[tokens*heads_per_token, 128], positions int32[tokens, 4].
 
     theta_scale: a device fp32[1] tensor (reference ABI), a Python float used
@@ -225,8 +225,9 @@ def rmsnorm_imrope_q(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tens
     elif theta_scale is not None:
         value = float(theta_scale)
     _same_device(q, gamma, positions, out)
-    check(lib().mllb_rmsnorm_imrope_q_batched(q.data_ptr(), gamma.data_ptr(), positions.data_ptr(), ptr, value,
-                                              out.data_ptr(), tokens, heads_per_token, _stream(q)),
+    check(lib().mllb_rmsnorm_imrope_q_batched_ex(q.data_ptr(), gamma.data_ptr(), positions.data_ptr(), ptr, value,
+                                                 out.data_ptr(), tokens, heads_per_token, LAUNCH_PDL if pdl else 0,
+                                                 _stream(q)),
           "rmsnorm_imrope_q")
     return out
 
