@@ -636,7 +636,7 @@ def run_decode(args, rank: int, world: int):
             "config": {"workload": "36-layer Qwen3-style decode (hidden 2560, 32/8 heads x 128, SwiGLU 9728, "
                                    "vocab 151936), ctx 4096, 128 greedy tokens per step",
                        "us_per_token": round(us_per_token, 3), "bytes_per_token_per_gpu": int(rank_bytes),
-                       "parallelism": (f"gate/up + vocab rows/{world} per rank, NCCL" if world > 1 else "single GPU"),
+                       "parallelism": ((f"gate/up + vocab rows/{world} per rank; " + ("peer-store Q8_1 all-gather over NVLink" if dec.peer is not None else "NCCL all-gather") + ", NCCL all-reduce of the argmax key") if world > 1 else "single GPU"),
                        "l2": "2.4 GB of weights per token > L2; no flush", "pdl": not args.no_pdl,
                        "fused_activations": dec.fused,
                        "logit_agreement": agreement},

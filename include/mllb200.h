@@ -64,7 +64,8 @@ const char *mllb_last_error(void);
  * Device error word: bit 0/1/2 = a kernel gave up a bounded (~1 s) wait on
  * its TMA pipeline (see csrc/common.cuh); bit 3 = decode next-token key out
  * of range; bit 4 = decode position outside the KV cache; bit 5 = decode
- * attention gave up waiting for its K/V copies.  Copies the word of the
+ * attention gave up waiting for its K/V copies; bit 6 = a peer all-gather
+ * gave up waiting for another rank.  Copies the word of the
  * current device to *bits (synchronising), optionally clearing it.  0 in
  * normal runs.
  */
@@ -218,6 +219,30 @@ int mllb_q4k_gate_up_act(const void *up_weights, const void *gate_weights, const
                          float *gate, float *prod, int64_t n, int64_t k, unsigned flags, void *stream);
 int mllb_q6k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out, int64_t n, int64_t k,
                         unsigned flags, void *stream);
+
+/*
+ * Peer all-gather of a Q8_1 activation over NVLink (no NCCL): rank r
+ * quantises its slice x[0..k) (k = the full length / world, a multiple of
+ * 32) and stores the k/32 blocks into every rank's buffer at block offset
+ * r * k/32, then signals every rank; the call's kernel finishes on each rank
+ * only when all slices have arrived there.  buffers[i] / flags[i]: rank i's
+ * destination (world * k/32 * 36 bytes) and counter array (world uint32,
+ * zero before the first gather), as device addresses valid on this GPU
+ * (peer mappings, e.g. symmetric memory); count: this rank's gather counter
+ * (one uint32, zero before the first gather).  Every rank must issue the
+ * same sequence of gathers with the same k, each on its own GPU.  A rank
+ * that does not arrive within ~1 s sets device error bit 64.  Replaces the
+ * NCCL all-gather of the sharded SwiGLU product.  world <= 8.
+ */
+typedef struct mllb_peer_gather {
+    int32_t rank, world;
+    void *buffers[8];
+    uint32_t *flags[8];
+    uint32_t *count;
+} mllb_peer_gather;
+
+int mllb_q8_1_quantize_allgather(const float *x, int64_t k, const mllb_peer_gather *peers, unsigned flags,
+                                 void *stream);
 
 /* Host helpers for the packed next-token key: high 32 bits order the fp32
  * value, low 32 bits are 0xffffffff - index (ties go to the lower index).

@@ -38,6 +38,12 @@ class ActF32(C.Structure):
 
 _ACT = C.POINTER(ActF32)
 
+
+class PeerGather(C.Structure):
+    """mllb_peer_gather of include/mllb200.h."""
+    _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("buffers", C.c_void_p * 8),
+                ("flags", C.c_void_p * 8), ("count", C.c_void_p)]
+
 SIGNATURES = {
     "mllb_abi_version": (C.c_int, []),
     "mllb_last_error": (C.c_char_p, []),
@@ -69,6 +75,7 @@ SIGNATURES = {
     "mllb_decode_attention_qkv_noalloc": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                                                     C.c_uint, _P]),
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
+    "mllb_q8_1_quantize_allgather": (C.c_int, [_P, _I64, C.POINTER(PeerGather), C.c_uint, _P]),
     "mllb_q4k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q6k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),

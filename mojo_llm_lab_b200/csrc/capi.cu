@@ -414,10 +414,10 @@ int mllb_rmsnorm_imrope_q_batched_ex(const float* q, const float* gamma, const i
   if (!aligned(q, 4) || !aligned(gamma, 4) || !aligned(positions, 4) || !aligned(out, 4) ||
       (theta_scale && !aligned(theta_scale, 4)))
     return fail(MLLB_EALIGN, "fp32/int32 pointers must be 4-byte aligned");
-  const int64_t grid =
-      tokens * ((heads_per_token + mllb::kImropeHeadsPerCta - 1) / mllb::kImropeHeadsPerCta);
+  const int64_t per_cta = heads_per_token < mllb::kImropeMaxHeadsPerCta ? heads_per_token : mllb::kImropeMaxHeadsPerCta;
+  const int64_t grid = tokens * ((heads_per_token + per_cta - 1) / per_cta);
   if (grid > 0x7fffffff) return fail(MLLB_EUNSUPPORTED, "too many heads");
-  return launched(launch(mllb::imrope_q_kernel, dim3(static_cast<unsigned>(grid)), dim3(mllb::kImropeHeadsPerCta * 32),
+  return launched(launch(mllb::imrope_q_kernel, dim3(static_cast<unsigned>(grid)), dim3(static_cast<unsigned>(per_cta * 32)),
                          0, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, q, gamma, positions,
                          theta_scale, theta_value, out, tokens, heads_per_token),
                   "imrope kernel");
@@ -807,4 +807,31 @@ extern "C" int mllb_decode_attention_qkv_noalloc(const float* qkv, const float* 
   if (rc) return rc;
   return mllb_decode_attention_qkv(qkv, q_gamma, k_gamma, theta_scale, state, k_cache, v_cache, scratch, need, out,
                                    q8, q_heads, kv_heads, ctx, flags, stream);
+}
+
+extern "C" int mllb_q8_1_quantize_allgather(const float* x, int64_t k, const mllb_peer_gather* peers, unsigned flags,
+                                            void* stream) {
+  if (!x || !peers || !peers->count) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (k <= 0 || k % 32) return fail(MLLB_EINVAL, "k=%lld is not a positive multiple of 32", static_cast<long long>(k));
+  if (peers->world < 1 || peers->world > mllb::kMaxPeers || peers->rank < 0 || peers->rank >= peers->world)
+    return fail(MLLB_EINVAL, "rank %d / world %d out of range", peers->rank, peers->world);
+  mllb::PeerGather pg = {};
+  pg.rank = peers->rank;
+  pg.world = peers->world;
+  for (int r = 0; r < pg.world; ++r) {
+    if (!peers->buffers[r] || !peers->flags[r]) return fail(MLLB_EINVAL, "null peer pointer for rank %d", r);
+    if (!aligned(peers->buffers[r], 4) || !aligned(peers->flags[r], 4))
+      return fail(MLLB_EALIGN, "peer buffers and counters must be 4-byte aligned");
+    pg.buffers[r] = static_cast<uint8_t*>(peers->buffers[r]);
+    pg.flags[r] = peers->flags[r];
+  }
+  pg.count = peers->count;
+  if (!aligned(x, 4) || !aligned(pg.count, 4)) return fail(MLLB_EALIGN, "x and count must be 4-byte aligned");
+  const int64_t blocks = k / 32;
+  int64_t grid = (blocks + 7) / 8;
+  if (grid > 1024) grid = 1024;
+  return launched(launch(mllb::q8_1_allgather_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                         static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, blocks, pg),
+                  "q8_1 all-gather kernel");
 }

@@ -24,6 +24,7 @@ enum : uint32_t {
   kErrBadToken = 1u << 3,          // decode: next-token key outside the vocabulary (row 0 used)
   kErrKvOverflow = 1u << 4,        // decode: position at or past the KV capacity (nothing written)
   kErrKvWaitTimeout = 1u << 5,     // decode attention gave up waiting for its K/V copies
+  kErrPeerWaitTimeout = 1u << 6,   // peer all-gather gave up waiting for another rank's slice
 };
 
 // Device-resident state of a decode loop; mirrors mllb_decode_state of the
@@ -94,6 +95,23 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
   return false;
 }
+
+// ---- cross-GPU signalling (peer memory mapped over NVLink)
+
+// *addr += v on (possibly another GPU's) memory, relaxed, system scope; the
+// caller orders its data before it with fence_sys().
+__device__ __forceinline__ void red_relaxed_sys_add(uint32_t* addr, uint32_t v) {
+  asm volatile("red.relaxed.sys.global.add.u32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
+}
+
+// Polling load of a counter that other GPUs update (not cached in L1).
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void fence_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
 
 // L2 policy for data read exactly once (weights): evict first.
 __device__ __forceinline__ uint64_t l2_evict_first_policy() {

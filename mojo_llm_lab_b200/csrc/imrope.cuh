@@ -107,24 +107,26 @@ __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, co
   out[lane + 96] = static_cast<float>(o[3]);
 }
 
-// One CTA per (token, group of up to 8 heads), one warp per head.  Every
-// head of a token shares its 4 positions, so the CTA first builds the 64
-// rotations (one fp64 pow + sincos per thread) and the warps then only
-// normalise and rotate.  Head h belongs to token h / heads_per_token and
+// One CTA per (token, group of up to 32 heads), one warp per head (the
+// launcher sizes the CTA to min(heads per token, 32) warps).  Every head of a
+// token shares its 4 positions, so the CTA first builds the 64 rotations (one
+// fp64 pow + sincos per thread) and the warps then only normalise and rotate:
+// the fp64 table is built once per token, not once per few heads.  Head h belongs to token h / heads_per_token and
 // uses that token's 4 positions.  The theta scale comes from device memory
 // (fp32, the reference ABI) unless theta_ptr is null, in which case
 // theta_value is used.
-constexpr int kImropeHeadsPerCta = 8;
+constexpr int kImropeMaxHeadsPerCta = 32;
 
-__global__ void __launch_bounds__(kImropeHeadsPerCta * 32) imrope_q_kernel(
+__global__ void __launch_bounds__(kImropeMaxHeadsPerCta * 32) imrope_q_kernel(
     const float* __restrict__ q, const float* __restrict__ gamma, const int32_t* __restrict__ positions,
     const float* __restrict__ theta_ptr, double theta_value, float* __restrict__ out, int64_t tokens,
     int64_t heads_per_token) {
   __shared__ double2 rot[kHeadDim / 2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int64_t ctas_per_token = (heads_per_token + kImropeHeadsPerCta - 1) / kImropeHeadsPerCta;
+  const int heads_per_cta = static_cast<int>(blockDim.x >> 5);
+  const int64_t ctas_per_token = (heads_per_token + heads_per_cta - 1) / heads_per_cta;
   const int64_t token = blockIdx.x / ctas_per_token;
-  const int64_t h = (blockIdx.x % ctas_per_token) * kImropeHeadsPerCta + warp;
+  const int64_t h = (blockIdx.x % ctas_per_token) * heads_per_cta + warp;
   pdl_wait_prerequisite();
   pdl_launch_dependents();
   if (token >= tokens) return;
@@ -135,10 +137,10 @@ __global__ void __launch_bounds__(kImropeHeadsPerCta * 32) imrope_q_kernel(
   const float* x = q + head * kHeadDim;
   const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
   const float g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
-  if (threadIdx.x < kHeadDim / 2) {
+  for (int p = threadIdx.x; p < kHeadDim / 2; p += blockDim.x) {
     const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
     const int32_t* pos = positions + 4 * token;
-    rot[threadIdx.x] = imrope_rotation(threadIdx.x, pos[0], pos[1], pos[2], pos[3], theta);
+    rot[p] = imrope_rotation(p, pos[0], pos[1], pos[2], pos[3], theta);
   }
   __syncthreads();
   if (!active) return;

@@ -73,4 +73,64 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
   }
 }
 
+// Peer all-gather of a Q8_1 activation: every rank quantises its slice and
+// stores the blocks into every rank's buffer (NVLink stores), then (after one
+// system-scope fence per CTA) counts one arrival per CTA into every rank's
+// counter for its source slot.  CTA 0 of each rank polls its counters with
+// volatile loads, then fences (acquire) once; it waits until every source has
+// delivered this gather's CTAs (counters are cumulative: the target is
+// (gathers so far + 1) x CTAs), so the kernel completes only when the whole
+// activation is in local memory.  The wait is bounded (~1 s, then
+// kErrPeerWaitTimeout).  Ranks run on separate GPUs and launch the same
+// sequence with the same k, hence the same grid.
+constexpr int kMaxPeers = 8;
+
+struct PeerGather {
+  int rank, world;
+  uint8_t* buffers[kMaxPeers];  // every rank's destination, as seen from this GPU
+  uint32_t* flags[kMaxPeers];   // every rank's counters [world], as seen from this GPU
+  uint32_t* count;              // this rank's gathers so far (local)
+};
+
+__global__ void __launch_bounds__(256) q8_1_allgather_kernel(const float* __restrict__ x, int64_t blocks,
+                                                             const PeerGather pg) {
+  const int lane = threadIdx.x & 31;
+  pdl_wait_prerequisite();
+  pdl_launch_dependents();
+  const int64_t slice = static_cast<int64_t>(pg.rank) * blocks * 36;
+  const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); g < blocks;
+       g += warps) {
+    uint32_t d16, s16;
+    const int q = q8_1_quantize_lane(x[g * 32 + lane], kQ8SumDTimesSumQ, &d16, &s16);
+    for (int r = 0; r < pg.world; ++r) q8_1_store_block(pg.buffers[r] + slice + g * 36, q, d16, s16, lane);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    fence_sys();  // the CTA's blocks (ordered by the barrier) before its arrivals
+    for (int r = 0; r < pg.world; ++r) red_relaxed_sys_add(pg.flags[r] + pg.rank, 1u);
+  }
+  if (blockIdx.x != 0 || threadIdx.x != 0) return;
+  const uint32_t target = (*pg.count + 1u) * gridDim.x;
+  const uint32_t* mine = pg.flags[pg.rank];
+  const uint64_t start = global_timer_ns();
+  bool ok = true;
+  for (int s = 0; s < pg.world && ok; ++s) {
+    for (uint32_t i = 0;; ++i) {
+      if (static_cast<int32_t>(ld_volatile_u32(mine + s) - target) >= 0) break;
+      if ((i & 255u) == 255u && global_timer_ns() - start > kWaitLimitNs) {
+        ok = false;
+        break;
+      }
+      if (i >= kWaitMaxIters) {
+        ok = false;
+        break;
+      }
+    }
+  }
+  fence_sys();  // the peers' blocks are visible before this kernel completes
+  if (!ok) record_error(kErrPeerWaitTimeout);
+  *pg.count += 1u;
+}
+
 }  // namespace mllb

@@ -22,12 +22,14 @@ graph of PDL-chained launches and replayed per token.  Weights and the
 prefilled KV cache are random (seeded) in the distributions of the
 reference's fixtures; there is no checkpoint.
 
-Multi-GPU (one process per GPU, ``torch.distributed`` over NCCL): the
-gate/up and vocabulary matvecs are row-sharded.  Each rank quantises its
-slice of the SwiGLU product and an all-gather of the Q8_1 bytes gives every
-rank the down projection's input; each rank takes the argmax of its logit
-rows and an all-reduce MAX of the packed (value, index) keys gives every rank
-the next token.  Everything else is replicated.
+Multi-GPU (one process per GPU, ``torch.distributed``): the gate/up and
+vocabulary matvecs are row-sharded.  Each rank quantises its slice of the
+SwiGLU product and stores the Q8_1 blocks straight into every rank's buffer
+over NVLink (``mllb_q8_1_quantize_allgather`` on symmetric memory; NCCL
+all-gather when symmetric memory is unavailable), which gives every rank the
+down projection's input; each rank takes the argmax of its logit rows and an
+NCCL all-reduce MAX of the packed (value, index) keys gives every rank the
+next token.  Everything else is replicated.
 """
 from __future__ import annotations
 
@@ -38,7 +40,7 @@ import numpy as np
 import torch
 
 from . import formats as F
-from ._lib import LAUNCH_PDL, ActF32, check, lib
+from ._lib import LAUNCH_PDL, ActF32, PeerGather, check, lib
 from .shard import RowShard
 
 HEAD_DIM = 128
@@ -286,7 +288,7 @@ class Decoder:
     """
 
     def __init__(self, weights: DecodeWeights, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pdl: bool = True,
-                 fused: bool = False, group=None):
+                 fused: bool = False, group=None, gather: str = "peer"):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
@@ -320,6 +322,9 @@ class Decoder:
             scratch=torch.zeros(scratch_n, dtype=torch.float64, device=dev))
         if self.world > 1 and fused:
             self.b.extra["prod_full"] = torch.zeros(cfg.ffn, dtype=torch.float32, device=dev)
+        self.peer = None
+        if self.world > 1 and not fused and gather == "peer":
+            self.peer = self._setup_peer_gather()
         nb_h, nb_f = cfg.hidden // 256, cfg.ffn // 256
         # The in-kernel activations need streaming configurations for every
         # matvec they feed (otherwise the separate norm / quantise kernels run).
@@ -427,10 +432,10 @@ class Decoder:
                                         cfg.hidden, fl, s), "gate_up")
             if self.world == 1:
                 check(L.mllb_q8_1_quantize_ex(P(b.prod), P(b.q8_prod), cfg.ffn, 0, fl, s), "quantize prod")
+                q8_prod = P(b.q8_prod)
             else:
-                self._gather_prod(s, fl)
-            check(L.mllb_q4k_matvec_ex(P(lw.down), P(b.q8_prod), P(b.down_out), cfg.hidden, cfg.ffn, fl, s),
-                  "down")
+                q8_prod = self._gather_prod(s, fl, layer)
+            check(L.mllb_q4k_matvec_ex(P(lw.down), q8_prod, P(b.down_out), cfg.hidden, cfg.ffn, fl, s), "down")
         check(L.mllb_decode_final_norm(h[cur], P(b.down_out), h[1 - cur], P(w.out_norm), cfg.eps,
                                        P(b.q8_hidden), cfg.hidden, state, fl, s), "final_norm")
         check(L.mllb_q6k_matvec_ex(P(w.output), P(b.q8_hidden), P(b.logits), w.vocab_shard.local_rows, cfg.hidden,
@@ -450,7 +455,53 @@ class Decoder:
         return 1 + self.cfg.layers * 9 + 2 + 1
 
     # -- sharded pieces -----------------------------------------------------
-    def _gather_prod(self, s: int, fl: int) -> None:
+    def _setup_peer_gather(self):
+        """Symmetric buffer [half 0 | half 1 | counters[world] | gather count]
+        mapped on every rank; layer l gathers into half l % 2, so a rank can
+        run at most one gather ahead of a peer's down projection without
+        overwriting what it reads.  None if symmetric memory is unavailable."""
+        import os
+
+        import torch.distributed as dist
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+        except ImportError:
+            return None
+        os.environ.setdefault("TORCH_SYMM_MEM_DISABLE_MULTICAST", "1")
+        world, rank = self.world, self.w.ffn_shard.rank
+        half = -(-(self.cfg.ffn // 32 * 36) // 256) * 256
+        flags_off, count_off = 2 * half, 2 * half + 256
+        try:
+            buf = symm_mem.empty(count_off + 256, dtype=torch.uint8, device=self.device)
+            buf.zero_()
+            handle = symm_mem.rendezvous(buf, self.group)
+            ptrs = [int(p) for p in handle.buffer_ptrs]
+        except Exception:  # noqa: BLE001 -- no peer mappings here: NCCL all-gather instead
+            return None
+        torch.cuda.synchronize(self.device)
+        dist.barrier(group=self.group)  # every counter is zero before anyone signals
+        tables = []
+        for h in range(2):
+            t = PeerGather()
+            t.rank, t.world = rank, world
+            for r in range(world):
+                t.buffers[r] = ptrs[r] + h * half
+                t.flags[r] = ptrs[r] + flags_off
+            t.count = ptrs[rank] + count_off
+            tables.append(t)
+        return {"buf": buf, "handle": handle, "tables": tables, "half": half}
+
+    def _gather_prod(self, s: int, fl: int, layer: int = 0) -> int:
+        """Q8_1 of the full SwiGLU product on every rank; returns its address."""
+        if self.peer is not None:
+            h = layer % 2
+            check(lib().mllb_q8_1_quantize_allgather(self.b.prod.data_ptr(), self.w.ffn_shard.per_rank,
+                                                     self.peer["tables"][h], fl, s), "peer all-gather")
+            return self.peer["buf"].data_ptr() + h * self.peer["half"]
+        self._gather_prod_nccl(s, fl)
+        return self.b.q8_prod.data_ptr()
+
+    def _gather_prod_nccl(self, s: int, fl: int) -> None:
         import torch.distributed as dist
 
         b, L, shard = self.b, lib(), self.w.ffn_shard

@@ -93,10 +93,58 @@ def _spawn(target, world, *args):
     assert codes == [0] * world, codes
 
 
-def _decode_worker(rank, world, port, out):
+def _gather_worker(rank, world, port, out):
     import torch
     import torch.distributed as dist
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from mojo_llm_lab_b200 import decode as D
+        from mojo_llm_lab_b200 import ops
+        from mojo_llm_lab_b200._lib import check, lib
+        cfg = D.DecodeConfig(layers=1, vocab=4096, context=8, new_tokens=2)
+        w = D.generate_weights(cfg, "cuda", world=world, rank=rank)
+        k, v = D.generate_kv_cache(cfg, "cuda")
+        dec = D.Decoder(w, k, v, group=dist.group.WORLD)
+        assert dec.peer is not None, "symmetric memory unavailable"
+        per = w.ffn_shard.per_rank
+        results = []
+        for it in range(4):  # alternate halves, several gathers
+            g = torch.Generator(device="cuda")
+            g.manual_seed(100 + it)
+            full = torch.randn(cfg.ffn, generator=g, device="cuda") * (it + 1)
+            dec.b.prod.copy_(full[rank * per:(rank + 1) * per])
+            addr = dec._gather_prod(torch.cuda.current_stream().cuda_stream, 0, layer=it)
+            torch.cuda.synchronize()
+            got = torch.empty(cfg.ffn // 32 * 36, dtype=torch.uint8, device="cuda")
+            got.copy_(dec.peer["buf"][addr - dec.peer["buf"].data_ptr():][:got.numel()])
+            results.append(bool(torch.equal(got, ops.quantize_q8_1(full))))
+        assert ops.device_error() == 0
+        if rank == 0:
+            torch.save(results, out)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_allgather_matches_local_quantisation(tmp_path):
+    """Every rank's gathered Q8_1 equals the quantisation of the full vector, gather after gather."""
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs at least 2 GPUs")
+    out = tmp_path / "gather.pt"
+    _spawn(_gather_worker, world, out)
+    assert torch.load(out) == [True] * 4
+
+
+def _decode_worker(rank, world, port, out, gather="peer"):
+    import torch
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
+                      TORCH_SYMM_MEM_DISABLE_MULTICAST="1")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
@@ -107,7 +155,8 @@ def _decode_worker(rank, world, port, out):
         k, v = D.generate_kv_cache(cfg, "cuda")
         s = torch.cuda.Stream()
         with torch.cuda.stream(s):
-            dec = D.Decoder(w, k, v, group=dist.group.WORLD)
+            dec = D.Decoder(w, k, v, group=dist.group.WORLD, gather=gather)
+            assert (dec.peer is not None) == (gather == "peer")
             dec.reset(17)
             dec.capture()
             tokens = dec.generate(17, 5)
@@ -122,7 +171,8 @@ def _decode_worker(rank, world, port, out):
         dist.destroy_process_group()
 
 
-def test_sharded_decode_matches_single_gpu(tmp_path):
+@pytest.mark.parametrize("gather", ["peer", "nccl"])
+def test_sharded_decode_matches_single_gpu(tmp_path, gather):
     """gate/up + vocab row-sharded over the GPUs: the same tokens and logits as one GPU."""
     import torch
     from mojo_llm_lab_b200 import decode as D
@@ -130,7 +180,7 @@ def test_sharded_decode_matches_single_gpu(tmp_path):
     if world < 2:
         pytest.skip("needs at least 2 GPUs")
     out = tmp_path / "decode.pt"
-    _spawn(_decode_worker, world, out)
+    _spawn(_decode_worker, world, out, gather)
     got = torch.load(out)
     cfg = D.DecodeConfig(layers=2, vocab=4096, context=300, new_tokens=6)
     w = D.generate_weights(cfg, "cuda")
