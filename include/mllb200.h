@@ -244,6 +244,15 @@ typedef struct mllb_peer_gather {
 int mllb_q8_1_quantize_allgather(const float *x, int64_t k, const mllb_peer_gather *peers, unsigned flags,
                                  void *stream);
 
+/*
+ * Bring bytes [data, data + bytes) into L2 ahead of their use, marked
+ * evict-last (TMA bulk prefetch; returns as soon as the prefetches are
+ * issued, nothing to wait for).  bytes a multiple of 16, data 16-byte aligned.
+ * The decode step runs it on a side stream for the next layer's weights and
+ * KV rows while the current layer computes.  No reference counterpart.
+ */
+int mllb_prefetch_l2(const void *data, int64_t bytes, void *stream);
+
 /* Host helpers for the packed next-token key: high 32 bits order the fp32
  * value, low 32 bits are 0xffffffff - index (ties go to the lower index).
  * mllb_token_key(t) is a key that selects token t (to seed a decode loop);

@@ -835,3 +835,17 @@ extern "C" int mllb_q8_1_quantize_allgather(const float* x, int64_t k, const mll
                          static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, blocks, pg),
                   "q8_1 all-gather kernel");
 }
+
+extern "C" int mllb_prefetch_l2(const void* data, int64_t bytes, void* stream) {
+  if (!data) return fail(MLLB_EINVAL, "null pointer");
+  if (bytes <= 0 || bytes % 16) return fail(MLLB_EINVAL, "bytes must be a positive multiple of 16");
+  if (!aligned(data, 16)) return fail(MLLB_EALIGN, "data must be 16-byte aligned");
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  int64_t grid = (bytes + 65535) / 65536;
+  const int64_t cap = static_cast<int64_t>(sm_count(dev)) * 2;
+  if (grid > cap) grid = cap;
+  mllb::l2_prefetch_kernel<<<static_cast<unsigned>(grid), 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(data), bytes);
+  return check_launch("l2 prefetch kernel");
+}

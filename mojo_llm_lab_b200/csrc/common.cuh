@@ -120,6 +120,20 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   return policy;
 }
 
+// L2 policy for data fetched ahead of its use (next layer's weights): evict last.
+__device__ __forceinline__ uint64_t l2_evict_last_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}
+
+// TMA bulk prefetch global -> L2 (no shared memory, no completion to wait
+// for).  addr 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* addr, uint32_t bytes, uint64_t policy) {
+  asm volatile("cp.async.bulk.prefetch.L2.global.L2::cache_hint [%0], %1, %2;" ::"l"(addr), "r"(bytes), "l"(policy)
+               : "memory");
+}
+
 // TMA bulk copy global -> shared, completion signalled on `bar` (tx bytes).
 // dst and src must be 16-byte aligned and bytes a multiple of 16.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar,

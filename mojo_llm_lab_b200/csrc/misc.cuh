@@ -29,4 +29,18 @@ __global__ void __launch_bounds__(256) stream_read_kernel(const uint4* __restric
   out[static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x] = acc;
 }
 
+// Bring `bytes` (a multiple of 16, 16-byte aligned) into L2 ahead of their
+// use, marked evict-last: one thread per CTA issues bulk prefetches of up to
+// 64 KB, grid-stride.  Nothing waits for them; the kernel ends once issued.
+__global__ void __launch_bounds__(32) l2_prefetch_kernel(const uint8_t* __restrict__ data, int64_t bytes) {
+  if (threadIdx.x != 0) return;
+  constexpr int64_t kChunk = 64 * 1024;
+  const uint64_t policy = l2_evict_last_policy();
+  for (int64_t off = static_cast<int64_t>(blockIdx.x) * kChunk; off < bytes;
+       off += static_cast<int64_t>(gridDim.x) * kChunk) {
+    const int64_t n = bytes - off < kChunk ? bytes - off : kChunk;
+    bulk_prefetch_l2(data + off, static_cast<uint32_t>(n), policy);
+  }
+}
+
 }  // namespace mllb
