@@ -60,6 +60,9 @@ WORKLOADS = {
     "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,8,3,2>",
                     profile="q4k_gate_up_n9728_k2560"),
     # Q6_K vocabulary projection 151936x2560
+    # the Q5_K matvec at configs[1]'s shape
+    "q5k_matvec": dict(kind="q5k", rows=4096, k=2560, kernel="team_stream_kernel<Q5kFormat,10,1,4,6,4>",
+                       profile="q5k_matvec_n4096_k2560"),
     "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,8,6>",
                       profile="q6k_vocab_n151936_k2560"),
 }
@@ -69,7 +72,7 @@ DECODE = dict(kind="decode", profile="decode_36layer_ctx4096")
 
 
 def weight_bytes(kind: str, rows: int, k: int) -> int:
-    per_row = k // 256 * (210 if kind == "q6k" else 144)
+    per_row = k // 256 * {"q6k": 210, "q5k": 176}.get(kind, 144)
     return rows * per_row * (2 if kind == "gate_up" else 1)
 
 
@@ -163,6 +166,8 @@ def host_weights(kind: str, rows: int, k: int, seed: int):
     from mojo_llm_lab_b200 import fixtures as fx
     if kind == "q6k":
         return [fx.seeded_q6k_matrix(rows, k, seed)]
+    if kind == "q5k":
+        return [fx.seeded_q5k_matrix(rows, k, seed)]
     if kind == "gate_up":
         return [fx.seeded_q4k_matrix(rows, k, seed), fx.seeded_q4k_matrix(rows, k, seed + 1)]
     return [fx.seeded_q4k_matrix(rows, k, seed)]
@@ -172,6 +177,8 @@ def oracle_outputs(kind: str, ws, act: bytes, rows: int, k: int, threads: int = 
     import oracle
     if kind == "q6k":
         return [oracle.q6k_matvec(ws[0], act, rows, k, threads)]
+    if kind == "q5k":
+        return [oracle.q5k_matvec(ws[0], act, rows, k, threads)]
     if kind == "gate_up":
         return list(oracle.q4k_gate_up(ws[0], ws[1], act, rows, k, threads))
     return [oracle.q4k_matvec(ws[0], act, rows, k, threads)]
@@ -228,7 +235,8 @@ def describe(workload: str) -> str:
     wl = WORKLOADS[workload]
     return {"q4k": f"Q4_K x Q8_1 matvec N={wl['rows']} K={wl['k']}",
             "gate_up": f"fused gate/up Q4_K x Q8_1 2x{wl['rows']}x{wl['k']} + SwiGLU",
-            "q6k": f"Q6_K x Q8_1 vocab matvec N={wl['rows']} K={wl['k']}"}[wl["kind"]]
+            "q6k": f"Q6_K x Q8_1 vocab matvec N={wl['rows']} K={wl['k']}",
+            "q5k": f"Q5_K x Q8_1 matvec N={wl['rows']} K={wl['k']}"}[wl["kind"]]
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -279,6 +287,8 @@ def run_ours(args, rank: int, world: int):
         w, o = weights[i], outs[i]
         if kind == "q6k":
             ops.q6_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+        elif kind == "q5k":
+            ops.q5_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
         elif kind == "gate_up":
             ops.q4k_gate_up(w[0], w[1], acts[i], o[0], o[1], o[2], pdl=pdl)
         else:

@@ -118,6 +118,19 @@ int mllb_q6k_matvec_ex(const void *weights, const void *q8, float *out, int64_t 
                        void *stream);
 
 /*
+ * Q5_K x Q8_1 matvec: out[r] for n rows of K = 2048, 2560 or 4096 (others:
+ * MLLB_EUNSUPPORTED).  Q5_K: 176 B / 256 weights (GGML block_q5_K: fp16 d,
+ * fp16 dmin, 12 B of 6-bit scales / mins packed as Q4_K, qh[32], qs[128]).
+ * The next format of the family (the reference profiles GGML's Q5_K matvec
+ * at 10-15 % of a 2B decode, docs/qwen35-2b-profile.md:7-14; no kernel of
+ * its own).
+ */
+int mllb_q5k_matvec(const void *weights, const void *q8, float *out, int64_t n, int64_t k, void *stream);
+/* Same, with launch flags (MLLB_LAUNCH_PDL). */
+int mllb_q5k_matvec_ex(const void *weights, const void *q8, float *out, int64_t n, int64_t k, unsigned flags,
+                       void *stream);
+
+/*
  * Fused RMSNorm (eps 1e-6) * gamma[128] + IMROPE (sections 24/20/20/0,
  * split-half pairs (p, p+64)) on `heads` contiguous fp32 heads of 128.
  * positions: int32[4] (axis-major) shared by all heads; theta_scale: device

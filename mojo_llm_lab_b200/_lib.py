@@ -77,6 +77,8 @@ SIGNATURES = {
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
     "mllb_q8_1_quantize_allgather": (C.c_int, [_P, _I64, C.POINTER(PeerGather), C.c_uint, _P]),
     "mllb_prefetch_l2": (C.c_int, [_P, _I64, _P]),
+    "mllb_q5k_matvec": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
+    "mllb_q5k_matvec_ex": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q6k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),

@@ -43,6 +43,15 @@
 #ifndef MLLB_CFG_Q4K_DUAL_16
 #define MLLB_CFG_Q4K_DUAL_16 4, 4, 2
 #endif
+#ifndef MLLB_CFG_Q5K_8
+#define MLLB_CFG_Q5K_8 8, 8, 6
+#endif
+#ifndef MLLB_CFG_Q5K_10
+#define MLLB_CFG_Q5K_10 4, 6, 4
+#endif
+#ifndef MLLB_CFG_Q5K_16
+#define MLLB_CFG_Q5K_16 8, 4, 3
+#endif
 #ifndef MLLB_CFG_Q6K_8
 #define MLLB_CFG_Q6K_8 4, 8, 6
 #endif
@@ -175,19 +184,28 @@ int grid_cap(int dev, int grid, int per_sm) {
   return grid < cap ? grid : cap;
 }
 
-template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
-int launch_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1, float* o2,
-                int n, cudaStream_t stream, bool pdl) {
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE>
+int launch_team_kernel(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1,
+                       float* o2, int n, cudaStream_t stream, bool pdl) {
   using C = mllb::TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
   int dev, grid, per_sm, rc;
   if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::team_stream_kernel<Fmt, NB, MATS, V, S, TEAMS>;
+  auto kernel = mllb::team_stream_kernel<Fmt, NB, MATS, V, S, TEAMS, PRODUCE>;
   const int tiles = (n + C::kT - 1) / C::kT;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, tiles, &grid, &per_sm))) return rc;
   grid = grid_cap(dev, grid, per_sm);
   return launched(launch(kernel, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, pdl, w0, w1, src, o0, o1, o2,
                          n, pdl ? 1 : 0),
                   "streaming matvec kernel");
+}
+
+// Activation staged from Q8_1 (src.q8) or built in the kernel (src.x).
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
+int launch_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1, float* o2,
+                int n, cudaStream_t stream, bool pdl) {
+  if (src.x)
+    return launch_team_kernel<Fmt, NB, MATS, V, S, TEAMS, true>(w0, w1, src, o0, o1, o2, n, stream, pdl);
+  return launch_team_kernel<Fmt, NB, MATS, V, S, TEAMS, false>(w0, w1, src, o0, o1, o2, n, stream, pdl);
 }
 
 int check_rows(int64_t n, int64_t k, int64_t max_rows) {
@@ -848,4 +866,32 @@ extern "C" int mllb_prefetch_l2(const void* data, int64_t bytes, void* stream) {
   mllb::l2_prefetch_kernel<<<static_cast<unsigned>(grid), 32, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint8_t*>(data), bytes);
   return check_launch("l2 prefetch kernel");
+}
+
+extern "C" int mllb_q5k_matvec_ex(const void* weights, const void* q8, float* out, int64_t n, int64_t k,
+                                  unsigned flags, void* stream) {
+  if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, q8/out 4-byte alignment");
+  using F = mllb::Q5kFormat;
+  const auto* w = static_cast<const uint8_t*>(weights);
+  const mllb::ActSource src = q8_source(static_cast<const uint8_t*>(q8));
+  const int rows = static_cast<int>(n);
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool pdl = flags & MLLB_LAUNCH_PDL;
+  switch (k / 256) {
+    case 8: return launch_team<F, 8, 1, MLLB_CFG_Q5K_8>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
+    case 10: return launch_team<F, 10, 1, MLLB_CFG_Q5K_10>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
+    case 16: return launch_team<F, 16, 1, MLLB_CFG_Q5K_16>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
+    default:
+      return fail(MLLB_EUNSUPPORTED, "Q5_K matvec is built for K = 2048, 2560, 4096 (got %lld)",
+                  static_cast<long long>(k));
+  }
+}
+
+extern "C" int mllb_q5k_matvec(const void* weights, const void* q8, float* out, int64_t n, int64_t k, void* stream) {
+  return mllb_q5k_matvec_ex(weights, q8, out, n, k, 0u, stream);
 }

@@ -138,6 +138,78 @@ struct Q4kFormat {
   }
 };
 
+// Q5_K (GGML block_q5_K, 176 B / 256 weights): fp16 d, fp16 dmin, the 12
+// scale/min bytes of Q4_K, qh[32] (bit g of qh[l] is the fifth bit of element
+// l of group g) and qs[128] (nibbles as Q4_K).  Unit, header decode and
+// activation layout are Q4_K's; the fifth bits enter each nibble word before
+// dp4a, so the dots are exact integers of the 5-bit quants.
+struct Q5kFormat {
+  static constexpr int kBlockBytes = 176;
+  static constexpr int kDecBytes = 32;
+
+  template <int NB>
+  struct ActLayout : Q4kFormat::ActLayout<NB> {};
+
+  struct Slot {
+    uint4 a_lo, a_hi;
+    double delta;
+    int asum;
+    int qs_off, qh_off, dec_off;
+    int s;
+  };
+
+  template <int NB>
+  __device__ static void stage_activation(const uint8_t* q8, uint8_t* act, int tid, int nthreads) {
+    stage_q8_1<NB * 8>(q8, act, tid, nthreads);
+  }
+
+  template <int NB>
+  __device__ static void store_group(uint8_t* act, int g, int lane, int q, uint32_t d16, uint32_t s16) {
+    Q4kFormat::store_group<NB>(act, g, lane, q, d16, s16);
+  }
+
+  template <int NB>
+  __device__ static Slot load_slot(const uint8_t* act, int p) {
+    constexpr int G = NB * 8;
+    Slot sl;
+    const int b = p >> 3, s = p & 7, j = s >> 1, h = s & 1;
+    sl.a_lo = *reinterpret_cast<const uint4*>(act + (b * 8 + 2 * j) * 32 + 16 * h);
+    sl.a_hi = *reinterpret_cast<const uint4*>(act + (b * 8 + 2 * j + 1) * 32 + 16 * h);
+    sl.delta = reinterpret_cast<const double*>(act + G * 32)[b * 8 + s];
+    sl.asum = reinterpret_cast<const int*>(act + G * 40)[b * 8 + s];
+    sl.qs_off = b * kBlockBytes + 48 + 16 * s;
+    sl.qh_off = b * kBlockBytes + 16 + 16 * h;
+    sl.dec_off = b * kDecBytes;
+    sl.s = s;
+    return sl;
+  }
+
+  __device__ static void decode(const uint8_t* raw_block, uint8_t* dec) { q4k_decode_header(raw_block, dec); }
+
+  __device__ static double term(const uint8_t* row_raw, const uint8_t* row_dec, const Slot& sl) {
+    const uint4 wq = lds128(row_raw + sl.qs_off);
+    const uint4 wh = lds128(row_raw + sl.qh_off);
+    const double2 dd = *reinterpret_cast<const double2*>(row_dec + sl.dec_off);
+    const uint32_t scmn = *reinterpret_cast<const unsigned short*>(row_dec + sl.dec_off + 16 + 2 * sl.s);
+    const int lo_bit = sl.s & 6, hi_bit = lo_bit + 1;  // groups 2j and 2j + 1
+    const uint32_t q[4] = {wq.x, wq.y, wq.z, wq.w}, hb[4] = {wh.x, wh.y, wh.z, wh.w};
+    const uint32_t al[4] = {sl.a_lo.x, sl.a_lo.y, sl.a_lo.z, sl.a_lo.w};
+    const uint32_t ah[4] = {sl.a_hi.x, sl.a_hi.y, sl.a_hi.z, sl.a_hi.w};
+    int dlo = 0, dhi = 0;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const uint32_t lo = (q[w] & 0x0f0f0f0fu) | (((hb[w] >> lo_bit) & 0x01010101u) << 4);
+      const uint32_t hi = ((q[w] >> 4) & 0x0f0f0f0fu) | (((hb[w] >> hi_bit) & 0x01010101u) << 4);
+      dlo = dp4a_us(lo, al[w], dlo);
+      dhi = dp4a_us(hi, ah[w], dhi);
+    }
+    const bool h = sl.s & 1;  // keep group 2j+h; the partner holds its other 16 weights
+    const int dot = (h ? dhi : dlo) + __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
+    const int sc = static_cast<int>(scmn & 0xffu), mn = static_cast<int>(scmn >> 8);
+    return sl.delta * fma(dd.x, i2d_exact(sc * dot), -dd.y * i2d_exact(mn * sl.asum));
+  }
+};
+
 // Q6_K: unit = 8 consecutive l of one (half, 16-column run): 32 weights in
 // four Q8_1 groups; lane pairs hold the two 8-column halves of a run.
 struct Q6kFormat {
@@ -319,7 +391,10 @@ struct TeamConfig {
 // the producer streams every stage at once; otherwise it sends one stage, then
 // holds the rest until the activation is staged so that the activation read
 // does not queue behind a flood of weight requests.
-template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
+// PRODUCE: the activation is built in the kernel from fp32 (ActSource.x);
+// otherwise it is staged from Q8_1 bytes.  A separate instantiation, so the
+// plain kernels carry none of the producer's registers.
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE = false>
 __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThreads,
                                   TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kMinBlocks)
     team_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1, const ActSource src,
@@ -426,7 +501,7 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
   const int twarp = warp % W;  // warp index inside the team
   pdl_wait_prerequisite();     // the activation may come from the preceding kernel
   MLLB_TRACE_POINT(1);
-  if (src.x)
+  if constexpr (PRODUCE)
     produce_activation<Fmt, NB, C::kConsumers>(src, act, reinterpret_cast<double*>(smem + C::kRedOffset),
                                                threadIdx.x);
   else

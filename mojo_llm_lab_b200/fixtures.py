@@ -238,6 +238,23 @@ def seeded_q4k_matrix(rows: int, k: int, seed: int) -> np.ndarray:
     return out.reshape(-1)
 
 
+def seeded_q5k_matrix(rows: int, k: int, seed: int) -> np.ndarray:
+    """rows x (k/256) Q5_K blocks with Q4_K's distributions (d ~ U(1e-3,1e-2),
+    dmin ~ U(0,5e-3), uniform 6-bit scales/mins) and uniform qh / qs bytes."""
+    nb = rows * (k // F.QK_K)
+    rng = np.random.default_rng(seed)
+    d = F.f16_bits(rng.uniform(1e-3, 1e-2, nb))
+    dmin = F.f16_bits(rng.uniform(0.0, 5e-3, nb))
+    scales = rng.integers(0, 64, (nb, 8), dtype=np.uint8)
+    minima = rng.integers(0, 64, (nb, 8), dtype=np.uint8)
+    out = np.empty((nb, F.Q5K_BLOCK_BYTES), dtype=np.uint8)
+    out[:, 0:2] = d.view(np.uint8).reshape(nb, 2)
+    out[:, 2:4] = dmin.view(np.uint8).reshape(nb, 2)
+    out[:, 4:16] = F.pack_q4k_scale_array(scales, minima)
+    out[:, 16:] = rng.integers(0, 256, (nb, 160), dtype=np.uint8)
+    return out.reshape(-1)
+
+
 def seeded_q6k_matrix(rows: int, k: int, seed: int) -> np.ndarray:
     """rows x (k/256) Q6_K blocks: d ~ U(1e-3,1e-2), int8 scales ~ U{-32..31},
     uniform ql/qh bytes.  Returns a flat uint8 array."""

@@ -27,6 +27,7 @@ import numpy as np
 QK_K = 256
 Q4K_BLOCK_BYTES = 144
 Q6K_BLOCK_BYTES = 210
+Q5K_BLOCK_BYTES = 176
 Q8_1_BLOCK_BYTES = 36
 Q8_1_GROUP = 32
 
@@ -45,6 +46,12 @@ def q4k_row_bytes(k: int) -> int:
     if k <= 0 or k % QK_K:
         raise ValueError("Q4_K rows need a positive multiple of 256 weights")
     return k // QK_K * Q4K_BLOCK_BYTES
+
+
+def q5k_row_bytes(k: int) -> int:
+    if k <= 0 or k % QK_K:
+        raise ValueError("Q5_K rows need a positive multiple of 256 weights")
+    return k // QK_K * Q5K_BLOCK_BYTES
 
 
 def q6k_row_bytes(k: int) -> int:

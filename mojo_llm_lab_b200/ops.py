@@ -29,7 +29,7 @@ __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
     "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
     "rmsnorm_q8_1", "decode_embed", "decode_final_norm", "decode_qk_rope_append", "decode_attention",
-    "decode_attention_qkv", "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32",
+    "decode_attention_qkv", "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32", "q5_k_q8_1_matvec",
     "argmax_key", "token_key", "key_token", "S_D_SUMQ", "S_SUM_X",
 ]
 
@@ -471,4 +471,23 @@ def q6k_matvec_act(weights: torch.Tensor, act: ActF32, k: int, output: torch.Ten
     rows = _rows(weights, F.q6k_row_bytes(k), "Q6_K")
     check(lib().mllb_q6k_matvec_act(weights.data_ptr(), act, output.data_ptr(), rows, k, _flags(pdl),
                                     _stream(weights)), "q6k_matvec_act")
+    return output
+
+
+
+def q5_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor, output: torch.Tensor | None = None,
+                     pdl: bool = False) -> torch.Tensor:
+    """Q5_K x Q8_1 matvec (K = 2048, 2560 or 4096)."""
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(weights, F.q5k_row_bytes(k), "Q5_K")
+    if output is None:
+        output = torch.empty(rows, dtype=torch.float32, device=weights.device)
+    _need(output, "output", torch.float32)
+    if output.numel() != rows:
+        raise ValueError(f"output must have {rows} values")
+    _same_device(weights, activations, output)
+    check(lib().mllb_q5k_matvec_ex(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k,
+                                   _flags(pdl), _stream(weights)), "q5_k_q8_1_matvec")
     return output

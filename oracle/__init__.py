@@ -19,6 +19,8 @@ wrappers whose names follow the reference:
                                        benchmark/q4_compare.c:328-357
 * ``q6k_matvec``                       public GGML Q6_K layout (parity unpinned:
                                        the reference has no Q6_K oracle)
+* ``q5k_matvec``                       public GGML Q5_K layout (parity unpinned:
+                                       the reference has no Q5_K code)
 """
 from __future__ import annotations
 
@@ -78,6 +80,8 @@ def lib() -> C.CDLL:
             "orc_imrope": (C.c_int, [P, P, P, C.c_double, C.c_int, P]),
             "orc_reference_theta_scale": (C.c_double, []),
             "orc_rmsnorm": (C.c_int, [P, P, i64, C.c_double, P]),
+            "orc_q5k_decode_block": (None, [P, P]),
+            "orc_q5k_matvec": (C.c_int, [P, P, i64, i64, P, C.c_int]),
             "orc_embed_q6k": (C.c_int, [P, i64, i64, P]),
             "orc_rmsnorm_q8_1": (C.c_int, [P, P, i64, P, C.c_double, P, P]),
             "orc_qk_rope_append": (C.c_int, [P, C.c_int, C.c_int, P, P, C.c_int32, C.c_double, P, P, P]),
@@ -203,6 +207,27 @@ def q4k_gate_up(up_weights, gate_weights, activations, rows: int, k: int, thread
 
 def swiglu(up: float, gate: float) -> float:
     return lib().orc_swiglu(up, gate)
+
+
+# ----------------------------------------------------------------- Q5_K
+
+def q5k_decode_block(payload) -> list:
+    """Public GGML Q5_K layout (parity unpinned: the reference has no Q5_K code)."""
+    p = _bytes(payload)
+    if p.size != 176:
+        raise ValueError("Q5_K block must have exactly 176 bytes")
+    out = np.zeros(256, dtype=np.float64)
+    lib().orc_q5k_decode_block(_ptr(p), _ptr(out))
+    return out.tolist()
+
+
+def q5k_matvec(weights, activations, rows: int, k: int, threads: int = 0) -> np.ndarray:
+    w, a = _bytes(weights), _bytes(activations)
+    if w.size != rows * (k // 256) * 176 or a.size != k // 32 * 36 or k % 256:
+        raise ValueError("Mismatched Q5_K/Q8_1 block counts")
+    out = np.zeros(rows, dtype=np.float64)
+    _check(lib().orc_q5k_matvec(_ptr(w), _ptr(a), rows, k, _ptr(out), threads), "q5k_matvec")
+    return out
 
 
 # ----------------------------------------------------------------- Q6_K
