@@ -26,19 +26,19 @@
 #define MLLB_CFG_Q4K_8 8, 8, 6
 #endif
 #ifndef MLLB_CFG_Q4K_10
-#define MLLB_CFG_Q4K_10 4, 6, 4
+#define MLLB_CFG_Q4K_10 8, 4, 3
 #endif
 #ifndef MLLB_CFG_Q4K_16
 #define MLLB_CFG_Q4K_16 8, 4, 3
 #endif
 #ifndef MLLB_CFG_Q4K_38
-#define MLLB_CFG_Q4K_38 4, 2, 1
+#define MLLB_CFG_Q4K_38 8, 2, 1
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_8
 #define MLLB_CFG_Q4K_DUAL_8 8, 4, 4
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_10
-#define MLLB_CFG_Q4K_DUAL_10 8, 3, 2
+#define MLLB_CFG_Q4K_DUAL_10 4, 4, 4
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_16
 #define MLLB_CFG_Q4K_DUAL_16 4, 4, 2
