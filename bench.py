@@ -54,10 +54,10 @@ FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
     # the headline metric's configuration
-    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="team_stream_kernel<Q4kFormat,10,1,4,6,4>",
+    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="team_stream_kernel<Q4kFormat,10,1,8,4,3>",
                        profile="q4k_matvec_n4096_k2560"),
     # fused gate/up, two 9728x2560 matrices, outputs up, gate, up*silu(gate)
-    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,8,3,2>",
+    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,4,4,4>",
                     profile="q4k_gate_up_n9728_k2560"),
     # Q6_K vocabulary projection 151936x2560
     # the Q5_K matvec at configs[1]'s shape
