@@ -57,7 +57,7 @@ WORKLOADS = {
     "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="team_stream_kernel<Q4kFormat,10,1,8,2,2>",
                        profile="q4k_matvec_n4096_k2560"),
     # fused gate/up, two 9728x2560 matrices, outputs up, gate, up*silu(gate)
-    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,4,4,4>",
+    "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,4,6,3>",
                     profile="q4k_gate_up_n9728_k2560"),
     # the Q5_K matvec at the headline shape (4096 x 2560)
     "q5k_matvec": dict(kind="q5k", rows=4096, k=2560, kernel="team_stream_kernel<Q5kFormat,10,1,8,2,2>",

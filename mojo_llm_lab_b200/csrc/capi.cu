@@ -45,7 +45,7 @@
 #define MLLB_CFG_Q4K_DUAL_8 8, 4, 4
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_10
-#define MLLB_CFG_Q4K_DUAL_10 4, 4, 4
+#define MLLB_CFG_Q4K_DUAL_10 4, 6, 3
 #endif
 #ifndef MLLB_CFG_Q4K_DUAL_16
 #define MLLB_CFG_Q4K_DUAL_16 4, 4, 2
