@@ -234,6 +234,21 @@ int mllb_q6k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out
                         unsigned flags, void *stream);
 
 /*
+ * mllb_q4k_gate_up_q8: mllb_q4k_gate_up_ex that also writes the Q8_1 of prod
+ * (s = d * sum q, the bytes mllb_q8_1_quantize would write) into q8_out
+ * (n / 32 blocks): the launch that would follow the gate/up in a decode step
+ * is folded into it.  The CTA whose stored rows complete a 32-row group
+ * quantises that group.  prod must not be NULL; n a multiple of 32;
+ * counters: n / 32 uint32, zero before the first call and left zero by each
+ * call; calls that share them must not overlap on the GPU.  K/256 in
+ * {8, 10, 16}, otherwise MLLB_EUNSUPPORTED.  No counterpart in the reference:
+ * there the quantiser is a GGML graph node of its own.
+ */
+int mllb_q4k_gate_up_q8(const void *up_weights, const void *gate_weights, const void *q8, float *up, float *gate,
+                        float *prod, void *q8_out, uint32_t *counters, int64_t n, int64_t k, unsigned flags,
+                        void *stream);
+
+/*
  * Peer all-gather of a Q8_1 activation over NVLink (no NCCL): rank r
  * quantises its slice x[0..k) (k = the full length / world, a multiple of
  * 32) and stores the k/32 blocks into every rank's buffer at block offset

@@ -39,6 +39,7 @@ class ActF32(C.Structure):
 _ACT = C.POINTER(ActF32)
 
 
+
 class PeerGather(C.Structure):
     """mllb_peer_gather of include/mllb200.h."""
     _fields_ = [("rank", C.c_int32), ("world", C.c_int32), ("buffers", C.c_void_p * 8),
@@ -82,6 +83,7 @@ SIGNATURES = {
     "mllb_q4k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q6k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q4k_gate_up_q8": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
 }
 
 _lock = threading.Lock()

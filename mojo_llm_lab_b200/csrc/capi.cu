@@ -196,18 +196,18 @@ int grid_cap(int dev, int grid, int per_sm) {
   return grid < cap ? grid : cap;
 }
 
-template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE>
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE, int EPI = mllb::kEpiNone>
 int launch_team_kernel(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, float* o0, float* o1,
-                       float* o2, int n, cudaStream_t stream, bool pdl) {
+                       float* o2, int n, cudaStream_t stream, bool pdl, const mllb::Epilogue& epi = {}) {
   using C = mllb::TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
   int dev, grid, per_sm, rc;
   if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::team_stream_kernel<Fmt, NB, MATS, V, S, TEAMS, PRODUCE>;
+  auto kernel = mllb::team_stream_kernel<Fmt, NB, MATS, V, S, TEAMS, PRODUCE, EPI>;
   const int tiles = (n + C::kT - 1) / C::kT;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, tiles, &grid, &per_sm))) return rc;
   grid = grid_cap(dev, grid, per_sm);
   return launched(launch(kernel, dim3(grid), dim3(C::kThreads), C::kSmemBytes, stream, pdl, w0, w1, src, o0, o1, o2,
-                         n, pdl ? 1 : 0),
+                         n, pdl ? 1 : 0, epi),
                   "streaming matvec kernel");
 }
 
@@ -265,6 +265,23 @@ int q4k_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, f
   }
   return fail(MLLB_EUNSUPPORTED, "no streaming configuration for K=%lld%s", static_cast<long long>(k),
               w1 ? " (gate/up)" : "");
+}
+
+// Q4_K gate/up streaming launch with the Q8_1 of the product fused in
+// (Q8_1 activation).
+int q4k_gate_up_q8_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
+                        int64_t n, int64_t k, cudaStream_t stream, bool pdl, const mllb::Epilogue& epi) {
+  using F = mllb::Q4kFormat;
+  constexpr int E = mllb::kEpiQuantProduct;
+  const mllb::ActSource src = q8_source(q8);
+  const int rows = static_cast<int>(n);
+  switch (k / 256) {
+    case 8: return launch_team_kernel<F, 8, 2, MLLB_CFG_Q4K_DUAL_8, false, E>(w0, w1, src, o0, o1, o2, rows, stream, pdl, epi);
+    case 10: return launch_team_kernel<F, 10, 2, MLLB_CFG_Q4K_DUAL_10, false, E>(w0, w1, src, o0, o1, o2, rows, stream, pdl, epi);
+    case 16: return launch_team_kernel<F, 16, 2, MLLB_CFG_Q4K_DUAL_16, false, E>(w0, w1, src, o0, o1, o2, rows, stream, pdl, epi);
+    default: break;
+  }
+  return fail(MLLB_EUNSUPPORTED, "no gate/up configuration for K=%lld", static_cast<long long>(k));
 }
 
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
@@ -823,6 +840,25 @@ int mllb_q6k_matvec_act(const void* weights, const mllb_act_f32* act, float* out
   if (!aligned(weights, 16) || !aligned(out, 4)) return fail(MLLB_EALIGN, "weights need 16-byte, out 4-byte alignment");
   return q6k_team(static_cast<const uint8_t*>(weights), src, out, n, k, static_cast<cudaStream_t>(stream),
                   flags & MLLB_LAUNCH_PDL);
+}
+
+int mllb_q4k_gate_up_q8(const void* up_weights, const void* gate_weights, const void* q8, float* up, float* gate,
+                        float* prod, void* q8_out, uint32_t* counters, int64_t n, int64_t k, unsigned flags,
+                        void* stream) {
+  if (!up_weights || !gate_weights || !q8 || !prod || !q8_out || !counters) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (n % 32) return fail(MLLB_EINVAL, "the product's Q8_1 needs a multiple of 32 rows");
+  if (!aligned(up_weights, 16) || !aligned(gate_weights, 16) || !aligned(q8, 4) || !aligned(up, 4) ||
+      !aligned(gate, 4) || !aligned(prod, 4) || !aligned(q8_out, 4) || !aligned(counters, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, the rest 4-byte alignment");
+  mllb::Epilogue epi = {};
+  epi.counters = counters;
+  epi.q8_out = static_cast<uint8_t*>(q8_out);
+  return q4k_gate_up_q8_team(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
+                             static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
+                             flags & MLLB_LAUNCH_PDL, epi);
 }
 
 }  // extern "C"

@@ -161,6 +161,15 @@ __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t threads) {
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* p) { return *reinterpret_cast<const uint4*>(p); }
+
+// fp32 global load cached in L2 only: for values that other CTAs of the same
+// grid wrote (ordered by a fence and an atomic arrival), which this SM's L1
+// may hold stale.
+__device__ __forceinline__ float ld_cg_f32(const float* p) {
+  float v;
+  asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
+  return v;
+}
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 // Streaming 16-byte global load that does not allocate in L1.

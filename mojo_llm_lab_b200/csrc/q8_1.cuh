@@ -23,7 +23,13 @@ enum : int { kQ8SumDTimesSumQ = 0, kQ8SumX = 1 };
 // Quantise the 32 values held one per lane; returns this lane's int8 q and
 // fills d16 / s16 (identical in every lane).
 __device__ __forceinline__ int q8_1_quantize_lane(float x, int s_mode, uint32_t* d16, uint32_t* s16) {
-  const float amax = warp_max_float(fabsf(x));
+  // max |x| over the warp as the fmaxf butterfly defines it (NaN lanes lose
+  // unless every lane is NaN), in one warp reduction: non-negative floats
+  // order as their bit patterns.
+  const float ax = fabsf(x);
+  const bool nan = ax != ax;
+  const uint32_t mbits = __reduce_max_sync(0xffffffffu, nan ? 0u : __float_as_uint(ax));
+  const float amax = __all_sync(0xffffffffu, nan) ? ax : __uint_as_float(mbits);
   const float d = __fdiv_rn(amax, 127.0f);
   const int q = amax == 0.0f ? 0 : static_cast<int>(roundf(__fdiv_rn(x, d)));
   const __half dh = __float2half_rn(d);
@@ -31,7 +37,7 @@ __device__ __forceinline__ int q8_1_quantize_lane(float x, int s_mode, uint32_t*
   if (s_mode == kQ8SumX) {
     s = warp_sum_float_butterfly(x);
   } else {
-    s = __half2float(dh) * static_cast<float>(warp_sum_int(q));  // exact product
+    s = __half2float(dh) * static_cast<float>(__reduce_add_sync(0xffffffffu, q));  // exact product
   }
   *d16 = __half_as_ushort(dh);
   *s16 = __half_as_ushort(__float2half_rn(s));

@@ -58,6 +58,22 @@ struct ActSource {
   DecodeState* advance;
 };
 
+// Work a streaming kernel does after its rows are out, in place of a separate
+// launch (each dependent launch of a decode step costs more than its own
+// duration):
+//  * kEpiQuantProduct (fused gate/up): the Q8_1 blocks of out2 (the SwiGLU
+//    product).  counters[g] counts the stored tiles of the 32 rows of group
+//    g; after its last tile each CTA arrives once per tile, and the CTA whose
+//    arrival completes a group quantises it (as q8_1_quantize: s = d * sum q)
+//    into q8_out and zeroes the counter.
+// Counters must be zero before the first launch; every launch leaves them
+// zero.  Launches that share counters must not overlap on the GPU.
+struct Epilogue {
+  uint32_t* counters;
+  uint8_t* q8_out;
+};
+enum : int { kEpiNone = 0, kEpiQuantProduct = 1 };
+
 // ============================================================== formats
 
 // Q4_K: unit = 16 nibble bytes (halves h of groups 2j, 2j+1 of a super-block).
@@ -395,13 +411,14 @@ struct TeamConfig {
 // PRODUCE: the activation is built in the kernel from fp32 (ActSource.x);
 // otherwise it is staged from Q8_1 bytes.  A separate instantiation, so the
 // plain kernels carry none of the producer's registers.
-template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE = false>
+template <class Fmt, int NB, int MATS, int V, int S, int TEAMS, bool PRODUCE = false, int EPI = kEpiNone>
 __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThreads,
                                   TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kMinBlocks)
     team_stream_kernel(const uint8_t* __restrict__ w0, const uint8_t* __restrict__ w1, const ActSource src,
                        float* __restrict__ out0, float* __restrict__ out1, float* __restrict__ out2, int n_rows,
-                       int pdl) {
+                       int pdl, const Epilogue epi) {
   using C = TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
+  static_assert(EPI != kEpiQuantProduct || (MATS == 2 && 32 % C::kT == 0), "product groups of whole tiles");
   constexpr int W = C::kW, RG = C::kRG, T = C::kT, P = C::kP, ROWB = C::kRowBytes;
   constexpr int kFirstBatch = TEAMS > 2 ? TEAMS : 2;
   constexpr int DECB = Fmt::kDecBytes;
@@ -601,6 +618,37 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     }
   }
   MLLB_TRACE_POINT(7);
+  if constexpr (EPI == kEpiQuantProduct) {
+    // One arrival per stored tile, then the groups this CTA completed.
+    __shared__ uint32_t s_done[32];
+    __shared__ int s_ndone;
+    __threadfence();  // this CTA's out2 rows before its arrivals
+    named_barrier(1, C::kConsumers);
+    if (threadIdx.x == 0) s_ndone = 0;
+    named_barrier(1, C::kConsumers);
+    const int tid = threadIdx.x;
+    for (int k0 = 0; k0 < my_tiles; k0 += 32) {
+      if (tid < 32 && k0 + tid < my_tiles) {
+        const int g = (blockIdx.x + (k0 + tid) * gridDim.x) * T / 32;
+        if (atomicAdd(&epi.counters[g], 1u) == 32 / T - 1) s_done[atomicAdd(&s_ndone, 1)] = g;
+      }
+      named_barrier(1, C::kConsumers);
+      const int nd = s_ndone;
+      if (nd > 0) {
+        __threadfence();
+        for (int i = tid >> 5; i < nd; i += C::kConsumers / 32) {
+          const int g = s_done[i];
+          uint32_t d16, s16;
+          const int q = q8_1_quantize_lane(ld_cg_f32(out2 + g * 32 + lane), kQ8SumDTimesSumQ, &d16, &s16);
+          q8_1_store_block(epi.q8_out + static_cast<size_t>(g) * kQ8BlockBytes, q, d16, s16, lane);
+          if (lane == 0) epi.counters[g] = 0;
+        }
+      }
+      named_barrier(1, C::kConsumers);
+      if (tid == 0) s_ndone = 0;
+      named_barrier(1, C::kConsumers);
+    }
+  }
 }
 
 }  // namespace mllb

@@ -18,7 +18,9 @@ profiles, docs/decode-profile.md:5-11): a stack of ``layers`` blocks
 
 Everything that changes from token to token (the token, its position, the
 KV rows) lives in device memory, so one step is captured once as a CUDA
-graph of PDL-chained launches and replayed per token.  Weights and the
+graph of PDL-chained launches and replayed per token.  On one GPU the
+gate/up launch also writes Q8_1(f) (``mllb_q4k_gate_up_q8``), so a layer is
+8 launches.  Weights and the
 prefilled KV cache are random (seeded) in the distributions of the
 reference's fixtures; there is no checkpoint.
 
@@ -288,7 +290,7 @@ class Decoder:
     """
 
     def __init__(self, weights: DecodeWeights, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pdl: bool = True,
-                 fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False):
+                 fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False, quant_tail: bool = True):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
@@ -335,6 +337,13 @@ class Decoder:
         # matvec they feed (otherwise the separate norm / quantise kernels run).
         self.fused = (fused and nb_h in (8, 10, 16) and nb_f in (8, 10, 16, 38)
                       and weights.vocab_shard.local_rows % 8 == 0)
+        # On one GPU the gate/up writes the Q8_1 of its product itself (the
+        # CTA that completes a 32-row group quantises it) instead of a
+        # separate quantiser launch: 8 launches per layer instead of 9.
+        self.quant_tail = (quant_tail and not self.fused and self.world == 1 and nb_h in (8, 10, 16)
+                           and ffn_local % 32 == 0)
+        if self.quant_tail:
+            self.b.extra["prod_counters"] = torch.zeros(ffn_local // 32, dtype=torch.int32, device=dev)
         self.graph = None
 
     # -- state ------------------------------------------------------------
@@ -450,13 +459,19 @@ class Decoder:
                                               cfg.ctx_capacity, fl, s), "attention")
             check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
             norm(P(b.o_out), lw.ffn_norm, "ffn_norm")
-            check(L.mllb_q4k_gate_up_ex(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod), ffn_local,
-                                        cfg.hidden, fl, s), "gate_up")
-            if self.world == 1:
-                check(L.mllb_q8_1_quantize_ex(P(b.prod), P(b.q8_prod), cfg.ffn, 0, fl, s), "quantize prod")
+            if self.quant_tail:
+                check(L.mllb_q4k_gate_up_q8(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod),
+                                            P(b.q8_prod), P(b.extra["prod_counters"]), ffn_local, cfg.hidden, fl, s),
+                      "gate_up + Q8_1")
                 q8_prod = P(b.q8_prod)
             else:
-                q8_prod = self._gather_prod(s, fl, layer)
+                check(L.mllb_q4k_gate_up_ex(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod), ffn_local,
+                                            cfg.hidden, fl, s), "gate_up")
+                if self.world == 1:
+                    check(L.mllb_q8_1_quantize_ex(P(b.prod), P(b.q8_prod), cfg.ffn, 0, fl, s), "quantize prod")
+                    q8_prod = P(b.q8_prod)
+                else:
+                    q8_prod = self._gather_prod(s, fl, layer)
             check(L.mllb_q4k_matvec_ex(P(lw.down), q8_prod, P(b.down_out), cfg.hidden, cfg.ffn, fl, s), "down")
         check(L.mllb_decode_final_norm(h[cur], P(b.down_out), h[1 - cur], P(w.out_norm), cfg.eps,
                                        P(b.q8_hidden), cfg.hidden, state, fl, s), "final_norm")
@@ -475,7 +490,7 @@ class Decoder:
         # final norm (unfused) and logits; argmax.
         if self.fused:
             return 1 + self.cfg.layers * 6 + 1 + 1
-        return 1 + self.cfg.layers * 9 + 2 + 1
+        return 1 + self.cfg.layers * (8 if self.quant_tail else 9) + 2 + 1
 
     # -- sharded pieces -----------------------------------------------------
     def _setup_peer_gather(self):

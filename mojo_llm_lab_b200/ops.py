@@ -475,6 +475,38 @@ def q6k_matvec_act(weights: torch.Tensor, act: ActF32, k: int, output: torch.Ten
 
 
 
+# ------------------------------------- gate/up with the Q8_1 of its product
+
+def q4k_gate_up_q8(up_weights: torch.Tensor, gate_weights: torch.Tensor, activations: torch.Tensor,
+                   prod: torch.Tensor, q8_out: torch.Tensor, counters: torch.Tensor,
+                   up: torch.Tensor | None = None, gate: torch.Tensor | None = None, pdl: bool = False):
+    """Fused gate/up that also writes the Q8_1 of prod = up * silu(gate) (counters: rows / 32 zeroed int32,
+    left zero by every call)."""
+    _need(up_weights, "up_weights", torch.uint8)
+    _need(gate_weights, "gate_weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(up_weights, F.q4k_row_bytes(k), "Q4_K")
+    if gate_weights.numel() != up_weights.numel():
+        raise ValueError("up and gate matrices differ in size")
+    for name, t in (("prod", prod), ("up", up), ("gate", gate)):
+        if t is not None:
+            _need(t, name, torch.float32)
+            if t.numel() != rows:
+                raise ValueError(f"{name} has the wrong size")
+    _need(q8_out, "q8_out", torch.uint8)
+    if q8_out.numel() != F.q8_1_bytes(rows):
+        raise ValueError("q8_out has the wrong size")
+    _need(counters, "counters", torch.int32)
+    if counters.numel() < rows // 32:
+        raise ValueError("counters needs rows / 32 entries")
+    _same_device(up_weights, gate_weights, activations, prod, q8_out, counters, up, gate)
+    check(lib().mllb_q4k_gate_up_q8(up_weights.data_ptr(), gate_weights.data_ptr(), activations.data_ptr(),
+                                    _ptr(up), _ptr(gate), prod.data_ptr(), q8_out.data_ptr(), counters.data_ptr(),
+                                    rows, k, _flags(pdl), _stream(up_weights)), "q4k_gate_up_q8")
+    return q8_out
+
+
 def q5_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor, output: torch.Tensor | None = None,
                      pdl: bool = False) -> torch.Tensor:
     """Q5_K x Q8_1 matvec (K = 2048, 2560 or 4096)."""

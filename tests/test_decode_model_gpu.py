@@ -31,14 +31,15 @@ def host_cache(t):
     return t.cpu().numpy().view(np.uint16).copy()
 
 
-def run_against_oracle(cfg, steps, token=17, graph=False, fused=True):
+def run_against_oracle(cfg, steps, token=17, graph=False, mode="quant_tail"):
     w, k, v = build(cfg)
     host = OD.host_model(w)
     kh, vh = host_cache(k), host_cache(v)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        dec = D.Decoder(w, k, v, fused=fused)
-        assert dec.fused == fused
+        dec = D.Decoder(w, k, v, fused=mode == "fused", quant_tail=mode == "quant_tail")
+        assert dec.fused == (mode == "fused")
+        assert dec.quant_tail == (mode == "quant_tail")
         dec.reset(token)
         if graph:
             dec.capture()
@@ -63,9 +64,9 @@ def run_against_oracle(cfg, steps, token=17, graph=False, fused=True):
 
 
 @pytest.mark.parametrize("cfg", [SMALL, ODD], ids=["qwen-2layer", "odd-shapes"])
-@pytest.mark.parametrize("fused", [True, False], ids=["fused", "unfused"])
-def test_decode_steps_match_oracle(orc, cfg, fused):
-    run_against_oracle(cfg, steps=3, fused=fused)
+@pytest.mark.parametrize("mode", ["quant_tail", "separate", "fused"])
+def test_decode_steps_match_oracle(orc, cfg, mode):
+    run_against_oracle(cfg, steps=3, mode=mode)
 
 
 def test_graph_replay_matches_oracle(orc):

@@ -1,0 +1,56 @@
+"""The fused gate/up that also writes the Q8_1 of its product
+(mllb_q4k_gate_up_q8), against the plain gate/up and the oracle's quantiser:
+the product is bit-identical to mllb_q4k_gate_up_ex's and its Q8_1 bytes equal
+the oracle's.  Called twice in a row: the group counters come back to zero.
+"""
+import numpy as np
+import pytest
+import torch
+
+from gpu_util import dev
+from mojo_llm_lab_b200 import fixtures as fx
+from mojo_llm_lab_b200 import formats as F
+from mojo_llm_lab_b200 import ops
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("rows,k", [(9728, 2560), (4864, 2560), (4096, 2048), (2048, 4096)])
+def test_gate_up_q8_tail(orc, rows, k):
+    up = dev(fx.seeded_q4k_matrix(rows, k, seed=21))
+    gate = dev(fx.seeded_q4k_matrix(rows, k, seed=22))
+    a = ops.quantize_q8_1(dev(fx.seeded_activation(k, seed=23)))
+    _, _, prod_ref = ops.q4k_gate_up(up, gate, a, want=("prod",))
+    prod_ref = prod_ref.cpu().numpy()
+    q8_ref = orc.quantize_q8_1(prod_ref)
+    counters = torch.zeros(rows // 32, dtype=torch.int32, device="cuda")
+    for call in range(2):
+        prod = torch.full((rows,), 3.0, device="cuda")
+        q8 = torch.zeros(F.q8_1_bytes(rows), dtype=torch.uint8, device="cuda")
+        ops.q4k_gate_up_q8(up, gate, a, prod, q8, counters, pdl=call == 1)
+        torch.cuda.synchronize()
+        assert np.array_equal(prod.cpu().numpy().view(np.uint32), prod_ref.view(np.uint32)), f"call {call}"
+        assert q8.cpu().numpy().tobytes() == q8_ref, f"call {call}: Q8_1 of the product"
+        assert not counters.cpu().numpy().any()
+    assert ops.device_error() == 0
+
+
+def test_gate_up_q8_rejects_bad_shapes():
+    from mojo_llm_lab_b200._lib import lib
+    k = 2560
+    w = torch.zeros(48 * F.q4k_row_bytes(k), dtype=torch.uint8, device="cuda")
+    a = torch.zeros(F.q8_1_bytes(k), dtype=torch.uint8, device="cuda")
+    prod = torch.zeros(48, device="cuda")
+    q8 = torch.zeros(F.q8_1_bytes(64), dtype=torch.uint8, device="cuda")
+    counters = torch.zeros(2, dtype=torch.int32, device="cuda")
+    L = lib()
+    # 48 rows: not whole Q8_1 groups
+    assert L.mllb_q4k_gate_up_q8(w.data_ptr(), w.data_ptr(), a.data_ptr(), None, None, prod.data_ptr(),
+                                 q8.data_ptr(), counters.data_ptr(), 48, k, 0, None) != 0
+    # no product buffer / no counters
+    assert L.mllb_q4k_gate_up_q8(w.data_ptr(), w.data_ptr(), a.data_ptr(), None, None, None, q8.data_ptr(),
+                                 counters.data_ptr(), 32, k, 0, None) != 0
+    assert L.mllb_q4k_gate_up_q8(w.data_ptr(), w.data_ptr(), a.data_ptr(), None, None, prod.data_ptr(),
+                                 q8.data_ptr(), None, 32, k, 0, None) != 0
+    torch.cuda.synchronize()
+    assert not counters.cpu().numpy().any()
