@@ -4,6 +4,9 @@
                               translation unit holding every kernel)
 * lib/mllb200_compat.cubin -- reference-named kernel entries for driver-API
                               harnesses (csrc/compat.cu)
+* lib/libmllb200_interpose.so -- LD_PRELOAD library that sends GGML's fused
+                              Q4_K gate/up launch to libmllb200.so
+                              (csrc/interpose.cpp, host code only)
 
 Both target `-gencode arch=compute_100a,code=sm_100a` only (B200).  The build
 is incremental on source mtimes; `python -m mojo_llm_lab_b200.build` forces it.
@@ -23,6 +26,7 @@ LIBDIR = PKG / "lib"
 INCLUDE = ROOT / "include"
 LIB = LIBDIR / "libmllb200.so"
 CUBIN = LIBDIR / "mllb200_compat.cubin"
+INTERPOSE = LIBDIR / "libmllb200_interpose.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xptxas", "-v", f"-I{INCLUDE}", f"-I{CSRC}"]
@@ -36,7 +40,7 @@ def nvcc() -> str:
 
 
 def _sources() -> list[Path]:
-    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + [INCLUDE / "mllb200.h"]
+    return sorted(CSRC.glob("*.cu")) + sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.cpp")) + [INCLUDE / "mllb200.h"]
 
 
 def _stale(target: Path) -> bool:
@@ -69,6 +73,14 @@ def build(force: bool = False, verbose: bool = False) -> dict:
              LIBDIR / "build_lib.log", verbose)
         tmp.replace(LIB)
         built["lib"] = str(LIB)
+    if force or _stale(INTERPOSE) or INTERPOSE.stat().st_mtime < LIB.stat().st_mtime:
+        tmp = INTERPOSE.with_suffix(".so.tmp")
+        cuda_inc = Path(nvcc()).resolve().parent.parent / "include"
+        _run([shutil.which("g++") or "g++", "-O2", "-std=c++17", "-fPIC", "-shared", f"-I{INCLUDE}", f"-I{cuda_inc}",
+              "-o", str(tmp), str(CSRC / "interpose.cpp"), f"-L{LIBDIR}", "-lmllb200", "-ldl",
+              "-Wl,-rpath,$ORIGIN"], LIBDIR / "build_interpose.log", verbose)
+        tmp.replace(INTERPOSE)
+        built["interpose"] = str(INTERPOSE)
     if force or _stale(CUBIN):
         tmp = CUBIN.with_suffix(".cubin.tmp")
         _run([nvcc(), *COMMON, *ARCH, "-cubin", "-o", str(tmp), str(CSRC / "compat.cu")],

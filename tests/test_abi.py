@@ -53,3 +53,20 @@ def test_compat_cubin_built_for_sm100a():
     for entry in (b"fused_q_imrope_runtime_fastpow", b"q4_k_q8_1_matvec_dp4a_128", b"q4_k_q8_1_gate_order",
                   b"q4_k_q8_1_matvec_dp4a", b"stream_read_roofline", b"q6_k_q8_1_matvec"):
         assert entry in data
+
+
+def test_interposer_exports_the_runtime_launch_hooks():
+    """lib/libmllb200_interpose.so (LD_PRELOAD) defines the CUDA runtime's two
+    launch entries and links to libmllb200.so, not to a CUDA runtime of its own."""
+    import shutil
+    import subprocess
+    build.build()
+    nm = shutil.which("nm")
+    if nm is None:
+        pytest.skip("nm not available")
+    out = subprocess.run([nm, "-D", "--defined-only", str(build.INTERPOSE)], capture_output=True, text=True,
+                         check=True).stdout
+    defined = {line.split()[-1] for line in out.splitlines() if line.strip()}
+    assert {"cudaLaunchKernel", "cudaLaunchKernelExC", "mllb_interpose_counts"} <= defined
+    needed = subprocess.run(["readelf", "-d", str(build.INTERPOSE)], capture_output=True, text=True).stdout
+    assert "libmllb200.so" in needed and "libcudart" not in needed
