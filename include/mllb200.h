@@ -234,6 +234,23 @@ int mllb_q6k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out
                         unsigned flags, void *stream);
 
 /*
+ * Batched tokens (prompt processing): out[t][r] = (W @ x_t)[r] for T tokens,
+ * W a Q4_K matrix of `rows` rows (a multiple of 128) and K columns, x_t the
+ * t-th of T consecutive Q8_1 rows (K/32 blocks each); out is [T][rows] fp32,
+ * each value within 1e-5 + 1e-5 |ref| of the exact sum.  The integer group
+ * dots run on the tensor cores (tcgen05, int8); see csrc/prefill.cuh.  The
+ * grid may split K; then `workspace` must hold
+ * mllb_q4k_matmul_tokens_workspace(rows, k, tokens) bytes (0 when no split;
+ * the plan depends on the current device's SM count).  The reference's
+ * counterpart is llama.cpp's MMQ, which it profiles but does not replace
+ * (docs/prefill-baseline.md).  flags: as mllb_q4k_matvec_ex (PDL is not
+ * used).
+ */
+int64_t mllb_q4k_matmul_tokens_workspace(int64_t rows, int64_t k, int64_t tokens);
+int mllb_q4k_matmul_tokens(const void *weights, const void *q8, float *out, int64_t rows, int64_t k, int64_t tokens,
+                           void *workspace, int64_t workspace_bytes, unsigned flags, void *stream);
+
+/*
  * mllb_q4k_gate_up_q8: mllb_q4k_gate_up_ex that also writes the Q8_1 of prod
  * (s = d * sum q, the bytes mllb_q8_1_quantize would write) into q8_out
  * (n / 32 blocks): the launch that would follow the gate/up in a decode step

@@ -18,6 +18,7 @@
 #include "q8_1.cuh"
 #include "stream.cuh"
 #include "decode.cuh"
+#include "prefill.cuh"
 
 // Streaming-kernel configurations: V (row groups per tile), S (stages),
 // TEAMS (consumer teams per CTA) per format, matrices and K/256.  Each can
@@ -859,6 +860,91 @@ int mllb_q4k_gate_up_q8(const void* up_weights, const void* gate_weights, const 
   return q4k_gate_up_q8_team(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
                              static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
                              flags & MLLB_LAUNCH_PDL, epi);
+}
+
+// ---------------------------------------------------------------- prefill
+
+}  // extern "C"
+
+namespace {
+
+struct PrefillPlan {
+  int row_tiles, tok_tiles, splits, bps;
+  int64_t workspace;  // bytes of fp64 partials (0 with one split)
+};
+
+PrefillPlan prefill_plan(int dev, int64_t rows, int64_t k, int64_t tokens) {
+  PrefillPlan p;
+  const int nb = static_cast<int>(k / 256);
+  p.row_tiles = static_cast<int>(rows / mllb::kPfRows);
+  p.tok_tiles = static_cast<int>((tokens + mllb::kPfTok - 1) / mllb::kPfTok);
+  const int ctas = p.row_tiles * p.tok_tiles;
+  int splits = sm_count(dev) / (ctas > 0 ? ctas : 1);
+  const int min_splits = (nb + mllb::kPfMaxGroups / 8 - 1) / (mllb::kPfMaxGroups / 8);
+  if (splits < min_splits) splits = min_splits;
+  if (splits > nb) splits = nb;
+  if (splits < 1) splits = 1;
+  p.bps = (nb + splits - 1) / splits;
+  p.splits = (nb + p.bps - 1) / p.bps;
+  p.workspace = p.splits > 1 ? static_cast<int64_t>(p.splits) * tokens * rows * 8 : 0;
+  return p;
+}
+
+int check_prefill(int64_t rows, int64_t k, int64_t tokens) {
+  if (rows <= 0 || rows % mllb::kPfRows || rows > (1 << 24))
+    return fail(MLLB_EINVAL, "rows=%lld is not a positive multiple of %d", static_cast<long long>(rows), mllb::kPfRows);
+  if (k <= 0 || k % 256 || k / 256 > 4096) return fail(MLLB_EINVAL, "K=%lld is not a positive multiple of 256", static_cast<long long>(k));
+  if (tokens <= 0 || tokens > (1 << 20)) return fail(MLLB_EINVAL, "token count %lld out of range", static_cast<long long>(tokens));
+  if (rows * tokens > (int64_t{1} << 31)) return fail(MLLB_EUNSUPPORTED, "output too large");
+  return MLLB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t mllb_q4k_matmul_tokens_workspace(int64_t rows, int64_t k, int64_t tokens) {
+  int rc = check_prefill(rows, k, tokens);
+  if (rc) return rc;
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  return prefill_plan(dev, rows, k, tokens).workspace;
+}
+
+int mllb_q4k_matmul_tokens(const void* weights, const void* q8, float* out, int64_t rows, int64_t k, int64_t tokens,
+                           void* workspace, int64_t workspace_bytes, unsigned flags, void* stream) {
+  if (!weights || !q8 || !out) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_prefill(rows, k, tokens);
+  if (rc) return rc;
+  if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4) || !aligned(workspace, 8))
+    return fail(MLLB_EALIGN, "weights need 16-byte, q8/out 4-byte, workspace 8-byte alignment");
+  int dev;
+  if ((rc = current_device(&dev))) return rc;
+  const PrefillPlan p = prefill_plan(dev, rows, k, tokens);
+  if (p.workspace > 0 && (!workspace || workspace_bytes < p.workspace))
+    return fail(MLLB_EINVAL, "workspace of %lld bytes needed (mllb_q4k_matmul_tokens_workspace)",
+                static_cast<long long>(p.workspace));
+  static bool attr_set[kMaxDevices] = {false};
+  if (!attr_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(mllb::prefill_q4k_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         mllb::kPfSmemBytes);
+    if (e != cudaSuccess) return fail(MLLB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    attr_set[dev] = true;
+  }
+  const auto s = static_cast<cudaStream_t>(stream);
+  double* partial = p.splits > 1 ? static_cast<double*>(workspace) : nullptr;
+  mllb::prefill_q4k_kernel<<<dim3(p.row_tiles, p.tok_tiles, p.splits), mllb::kPfThreads, mllb::kPfSmemBytes, s>>>(
+      static_cast<const uint8_t*>(weights), static_cast<const uint8_t*>(q8), static_cast<int>(rows),
+      static_cast<int>(k / 256), static_cast<int>(tokens), p.bps, out, partial);
+  if ((rc = check_launch("prefill q4k kernel"))) return rc;
+  if (partial) {
+    const int64_t n = rows * tokens;
+    const int grid = static_cast<int>((n + 255) / 256 < 4 * sm_count(dev) ? (n + 255) / 256 : 4 * sm_count(dev));
+    mllb::prefill_sum_kernel<<<grid, 256, 0, s>>>(partial, p.splits, n, out);
+    return check_launch("prefill sum kernel");
+  }
+  return MLLB_OK;
 }
 
 }  // extern "C"

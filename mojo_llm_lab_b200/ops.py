@@ -507,6 +507,42 @@ def q4k_gate_up_q8(up_weights: torch.Tensor, gate_weights: torch.Tensor, activat
     return q8_out
 
 
+# ------------------------------------------------------- batched tokens (prefill)
+
+def q4k_matmul_tokens(weights: torch.Tensor, activations: torch.Tensor, output: torch.Tensor | None = None,
+                      k: int | None = None) -> torch.Tensor:
+    """out[t] = W @ x_t for T tokens at once (tensor-core int8 group dots, fp64 scaling).
+
+    weights: Q4_K bytes of `rows` (a multiple of 128) rows; activations: T consecutive Q8_1
+    rows ([T, K/32*36] or flat, then `k` gives K); output: fp32 [T, rows]."""
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    if activations.dim() == 2:
+        k = activations.shape[1] // F.Q8_1_BLOCK_BYTES * F.Q8_1_GROUP
+    elif k is None:
+        raise ValueError("flat activations need k")
+    q8_row = k // F.Q8_1_GROUP * F.Q8_1_BLOCK_BYTES
+    if k <= 0 or k % 256 or activations.numel() % q8_row:
+        raise ValueError("activations are not whole Q8_1 rows of K = a multiple of 256")
+    tokens = activations.numel() // q8_row
+    rows = _rows(weights, F.q4k_row_bytes(k), "Q4_K")
+    if output is None:
+        output = torch.empty(tokens, rows, dtype=torch.float32, device=weights.device)
+    _need(output, "output", torch.float32)
+    if output.numel() != tokens * rows:
+        raise ValueError("output must hold tokens x rows values")
+    _same_device(weights, activations, output)
+    L = lib()
+    with torch.cuda.device(weights.device):
+        need = int(L.mllb_q4k_matmul_tokens_workspace(rows, k, tokens))
+    if need < 0:
+        check(need, "q4k_matmul_tokens_workspace")
+    work = torch.empty(max(need, 8), dtype=torch.uint8, device=weights.device) if need > 0 else None
+    check(L.mllb_q4k_matmul_tokens(weights.data_ptr(), activations.data_ptr(), output.data_ptr(), rows, k, tokens,
+                                   _ptr(work), need, 0, _stream(weights)), "q4k_matmul_tokens")
+    return output
+
+
 def q5_k_q8_1_matvec(weights: torch.Tensor, activations: torch.Tensor, output: torch.Tensor | None = None,
                      pdl: bool = False) -> torch.Tensor:
     """Q5_K x Q8_1 matvec (K = 2048, 2560 or 4096)."""
