@@ -17,9 +17,9 @@
 // in the single-token kernels, so the result is within 1e-5 + 1e-5 |ref| of
 // the exact sums.
 //
-// CTA (416 threads, one per SM): warps 0-7 scale (warp w reads TMEM lanes
-// 32 (w % 4).. for tokens 16 (w / 4)..), warps 8-11 unpack the weights (one
-// row per thread), warp 12 owns the TMEM allocation and its lane 0 issues the
+// CTA (672 threads, one per SM): warps 0-15 scale (warp w reads TMEM lanes
+// 32 (w % 4).. for tokens 8 (w / 4)..), warps 16-19 unpack the weights (one
+// row per thread), warp 20 owns the TMEM allocation and its lane 0 issues the
 // MMAs.  The tokens' Q8_1 quants of the CTA's groups are staged once; the
 // weight rows are read block by block with 16-byte loads, unpacked in
 // registers into the canonical no-swizzle K-major layout (8-row x 16-byte
@@ -36,10 +36,11 @@ namespace mllb {
 
 constexpr int kPfRows = 128;                 // weight rows per CTA (MMA M)
 constexpr int kPfTok = 32;                   // tokens per CTA (MMA N)
-constexpr int kPfScaleWarps = 8;             // warps 0..7: fp64 scaling (TMEM readers)
-constexpr int kPfUnpackWarps = 4;            // warps 8..11: weight unpack, one row per thread
-constexpr int kPfMmaWarp = kPfScaleWarps + kPfUnpackWarps;  // warp 12: TMEM owner, lane 0 issues MMAs
-constexpr int kPfThreads = (kPfMmaWarp + 1) * 32;          // 416
+constexpr int kPfScaleWarps = 16;            // warps 0..15: fp64 scaling (TMEM readers)
+constexpr int kPfUnpackWarps = 4;            // warps 16..19: weight unpack, one row per thread
+constexpr int kPfMmaWarp = kPfScaleWarps + kPfUnpackWarps;  // warp 20: TMEM owner, lane 0 issues MMAs
+constexpr int kPfThreads = (kPfMmaWarp + 1) * 32;          // 672
+constexpr int kPfTokPerWarp = kPfTok / (kPfScaleWarps / 4); // tokens a scaling warp covers: 8
 constexpr int kPfMaxGroups = 80;             // groups (32-element K steps) per CTA: 10 blocks
 constexpr int kPfATile = kPfRows * 32;       // bytes of one group's A tile
 constexpr int kPfBTile = kPfTok * 32;        // bytes of one group's B tile
@@ -83,19 +84,15 @@ __device__ __forceinline__ void tc_commit(uint64_t* bar) {
                : "memory");
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane.
-__device__ __forceinline__ void tc_ld32(uint32_t taddr, int32_t (&v)[32]) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
-      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
-      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
-        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
-        "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
-        "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
-      : "r"(taddr)
-      : "memory");
-  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+// 8 consecutive 32-bit TMEM columns of this thread's lane (issue only;
+// tc_wait_ld completes every load issued before it).
+__device__ __forceinline__ void tc_ld8(uint32_t taddr, int32_t (&v)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+               : "r"(taddr)
+               : "memory");
 }
+__device__ __forceinline__ void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
 // Byte offset of element (row m, k) of a K-major no-swizzle tile whose 8-row
 // x 16-byte core matrices sit k-chunk-minor: LBO = 128 B, SBO = 256 B.
@@ -238,14 +235,29 @@ __global__ void __launch_bounds__(kPfThreads, 1)
     }
   } else {
     // ------------------------------------------------ fp64 scaling
-    const int lgrp = warp & 3;                     // TMEM lanes 32 lgrp..
-    const int r = lgrp * 32 + lane;                // row of the tile
-    const int th = warp >> 2;                      // token half: 16 th..
+    // Warp w: TMEM lanes 32 (w % 4).. (its rows) and tokens 8 (w / 4)..; the
+    // next group's TMEM columns load while this group's are scaled.
+    const int lgrp = warp & 3;
+    const int r = lgrp * 32 + lane;
+    const int tq = warp >> 2;
     const double2* tok_scale = reinterpret_cast<const double2*>(smem + kPfTokScaleOff);
     const float2* row_scale = reinterpret_cast<const float2*>(smem + kPfRowScaleOff);
-    double acc[16];
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(lgrp * 32) << 16) + tq * kPfTokPerWarp;
+    double acc[kPfTokPerWarp];
 #pragma unroll
-    for (int t = 0; t < 16; ++t) acc[t] = 0.0;
+    for (int t = 0; t < kPfTokPerWarp; ++t) acc[t] = 0.0;
+    auto scale_group = [&](const int32_t (&dv)[kPfTokPerWarp], int i, int buf, int s) {
+      const float2 rs = row_scale[(buf * 8 + s) * kPfRows + r];
+      const double as = rs.x, bs = rs.y;
+      const double2* ts = tok_scale + (i * 8 + s) * kPfTok + tq * kPfTokPerWarp;
+#pragma unroll
+      for (int t = 0; t < kPfTokPerWarp; ++t) {
+        const double2 sc = ts[t];
+        const double x = as * static_cast<double>(dv[t]);  // exact
+        acc[t] = fma(x, sc.x, acc[t]);
+        acc[t] = fma(-bs, sc.y, acc[t]);
+      }
+    };
     for (int i = 0; i < nblk; ++i) {
       const int buf = i & 1;
       if (!mbar_wait_bounded(&d_full[buf], (i >> 1) & 1)) {
@@ -254,28 +266,26 @@ __global__ void __launch_bounds__(kPfThreads, 1)
       }
       tc_fence_after();
       if (!*abort_flag) {
-#pragma unroll 1
-        for (int s = 0; s < 8; ++s) {
-          int32_t dv[32];
-          tc_ld32(tmem + (static_cast<uint32_t>(lgrp * 32) << 16) + buf * 256 + s * 32, dv);
-          const float2 rs = row_scale[(buf * 8 + s) * kPfRows + r];
-          const double as = rs.x, bs = rs.y;
-          const double2* ts = tok_scale + (i * 8 + s) * kPfTok + th * 16;
+        const uint32_t base = lane_base + buf * 256;
+        int32_t d0[kPfTokPerWarp], d1[kPfTokPerWarp];
+        tc_ld8(base, d0);
+        tc_wait_ld();
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            const double2 sc = ts[t];
-            const double x = as * static_cast<double>(dv[th * 16 + t]);  // exact
-            acc[t] = fma(x, sc.x, acc[t]);
-            acc[t] = fma(-bs, sc.y, acc[t]);
-          }
+        for (int s = 0; s < 8; s += 2) {
+          tc_ld8(base + (s + 1) * 32, d1);
+          scale_group(d0, i, buf, s);
+          tc_wait_ld();
+          if (s + 2 < 8) tc_ld8(base + (s + 2) * 32, d0);
+          scale_group(d1, i, buf, s + 1);
+          tc_wait_ld();
         }
       }
       tc_fence_before();
       mbar_arrive(&d_free[buf]);
     }
-    // Write this thread's row for its 16 tokens.
-    for (int t = 0; t < 16; ++t) {
-      const int tg = tok0 + th * 16 + t;
+    // Write this thread's row for its tokens.
+    for (int t = 0; t < kPfTokPerWarp; ++t) {
+      const int tg = tok0 + tq * kPfTokPerWarp + t;
       if (tg >= tokens) break;
       if (partial)
         partial[(static_cast<size_t>(blockIdx.z) * tokens + tg) * rows + row0 + r] = acc[t];
