@@ -93,3 +93,18 @@ def test_graph_and_eager_generate_identical_tokens():
 def test_full_size_decode_matches_oracle(orc):
     """The 36-layer, 151936-vocab stack at context 4096: two greedy steps."""
     run_against_oracle(D.DecodeConfig(), steps=2)
+
+
+def test_gguf_loaded_stack_decodes_identically(tmp_path):
+    """The stack written as a GGUF file (llama.cpp's tensor names) and read
+    back decodes the same tokens with the same logits."""
+    from mojo_llm_lab_b200 import gguf
+    w, k, v = build(SMALL)
+    path = tmp_path / "small.gguf"
+    gguf.save_decode_weights(path, w)
+    w2 = gguf.load_decode_weights(path, "cuda", context=SMALL.context, new_tokens=SMALL.new_tokens)
+    k2, v2 = k.clone(), v.clone()
+    a = D.Decoder(w, k, v)
+    b = D.Decoder(w2, k2, v2)
+    assert a.generate(123, 4) == b.generate(123, 4)
+    assert torch.equal(a.b.logits, b.b.logits)
