@@ -33,6 +33,9 @@ heads x 128 fp32, gamma[128], runtime fp32 theta scale 0x3f492c27, positions
 distinct input copies (the reference's measurement, benchmark/bench.c:33);
 --workload imrope_batched: the same op over 4096 tokens x 32 heads (134 MB
 per launch, HBM-bound throughput mode).  One GPU; N ranks are replicas.
+
+--workload prefill: the batched-token form, 512 tokens x 4096 x 2560 Q4_K on
+the tensor cores (mllb_q4k_matmul_tokens); metric int8 TOP/s.
 """
 from __future__ import annotations
 
@@ -471,6 +474,176 @@ def run_ours(args, rank: int, world: int):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- prefill workload
+
+PREFILL = dict(rows=4096, k=2560, tokens=512, profile="prefill_q4k_n4096_k2560_t512")
+
+
+def prefill_describe() -> str:
+    return f"batched Q4_K x Q8_1 {PREFILL['tokens']} tokens x {PREFILL['rows']}x{PREFILL['k']} (tcgen05 int8)"
+
+
+def prefill_cpu_reference(target_s: float = 10.0):
+    """The oracle's matvec over tokens of the same workload, all host threads, ~target_s."""
+    import oracle
+    from mojo_llm_lab_b200 import fixtures as fx
+    rows, k = PREFILL["rows"], PREFILL["k"]
+    threads = os.cpu_count() or 1
+    w = fx.seeded_q4k_matrix(rows, k, seed=1)
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        a = oracle.quantize_q8_1(fx.seeded_activation(k, seed=3 + reps))
+        oracle.q4k_matvec(w, a, rows, k, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s or reps >= PREFILL["tokens"]:
+            break
+    return {"value": 2.0 * reps * rows * k / el / 1e12, "unit": "int8 TOP/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} tokens x {rows}x{k} (oracle/oracle.c matvec per token incl. Q8_1 quantise, "
+                      f"OpenMP {threads} threads) in {el:.1f} s", "seconds": el, "tokens": reps}
+
+
+def run_prefill_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    ref = prefill_cpu_reference(target_s=max(3.0, min(30.0, 1.5 * args.steps)))
+    line = {"metric": f"{prefill_describe()} int8 TOP/s", "value": round(ref["value"], 6), "unit": "int8 TOP/s",
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ref["seconds"] / ref["tokens"] * PREFILL["tokens"] * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8 dot / f64 sum", "data": "synthetic (seeded)",
+            "config": {"workload": prefill_describe()},
+            "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(ref["value"], 6), "unit": "int8 TOP/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_prefill(args, rank: int, world: int):
+    """One step = `copies` batched launches over distinct weight and activation copies (> 2x L2)."""
+    import torch
+
+    from mojo_llm_lab_b200 import fixtures as fx
+    from mojo_llm_lab_b200 import ops
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    rows, k, tokens = PREFILL["rows"], PREFILL["k"], PREFILL["tokens"]
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    w_host = fx.seeded_q4k_matrix(rows, k, seed=1)
+    per_copy = w_host.size + tokens * k // 32 * 36
+    copies = args.copies or max(2, -(-int(2.2 * L2_BYTES) // per_copy))
+    w0 = torch.from_numpy(w_host).to(device)
+    ws = [w0] + [w0.clone() for _ in range(copies - 1)]
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    xs = torch.randn(copies, tokens * k, generator=gen, device=device)
+    acts = torch.stack([ops.quantize_q8_1(xs[i]) for i in range(copies)])   # per-token Q8_1 rows
+    outs = torch.empty(copies, tokens, rows, dtype=torch.float32, device=device)
+
+    if not args.skip_check:
+        import oracle
+        ops.q4k_matmul_tokens(ws[0], acts[0], outs[0], k=k)
+        torch.cuda.synchronize()
+        a_host = acts[0].cpu().numpy().reshape(tokens, -1)
+        got = outs[0].cpu().numpy()
+        for t in (0, tokens // 2, tokens - 1):
+            ref = oracle.q4k_matvec(w_host, a_host[t].tobytes(), rows, k)
+            if not np.all(np.abs(got[t] - ref) <= 1e-5 + 1e-5 * np.abs(ref)):
+                raise SystemExit(f"correctness gate failed: token {t} differs from the oracle")
+
+    def step():
+        for i in range(copies):
+            ops.q4k_matmul_tokens(ws[i], acts[i], outs[i], k=k)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        for _ in range(3):
+            graph.replay()
+        torch.cuda.synchronize()
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    ops_per_launch = 2.0 * rows * k * tokens
+    value = copies * ops_per_launch / (ms * 1e-3) / 1e12
+
+    # e2e: fp32 activations from pinned host memory, one quantiser launch over
+    # all tokens, the batched launch, the fp32 outputs back; graph-captured.
+    x_pin = xs[0].cpu().pin_memory()
+    out_pin = torch.empty(tokens, rows, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty(tokens * k, dtype=torch.float32, device=device)
+    a_dev = torch.empty(tokens * k // 32 * 36, dtype=torch.uint8, device=device)
+
+    def e2e_step():
+        x_dev.copy_(x_pin, non_blocking=True)
+        ops.quantize_q8_1(x_dev, a_dev)
+        ops.q4k_matmul_tokens(ws[0], a_dev, outs[0], k=k)
+        out_pin.copy_(outs[0], non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e_graph, stream=stream):
+        e2e_step()
+    for _ in range(args.warmup):
+        e_graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e_graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1) / args.steps
+    del graph, e_graph
+    if ops.device_error():
+        raise SystemExit("device error word set")
+    if rank == 0:
+        peak = None
+        try:
+            peak = 2.0 * float(json.loads((ROOT / "MEASURED_PEAKS.json").read_text())["bf16_tflops"])
+        except Exception:  # noqa: BLE001
+            pass
+        cpu = None if args.no_cpu_baseline else prefill_cpu_reference(10.0)
+        achieved = ops_per_launch / (ms / copies * 1e-3) / 1e12
+        line = {
+            "metric": f"{prefill_describe()} int8 TOP/s", "value": round(value * world, 3), "unit": "int8 TOP/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "u8 x s8 tcgen05 MMA (s32 per group), f64 scaling", "data": "synthetic (seeded)",
+            "config": {"workload": prefill_describe(), "rows": rows, "k": k, "tokens": tokens,
+                       "launches_per_step": copies, "us_per_launch": round(ms * 1e3 / copies, 3),
+                       "l2": f"{copies} weight + activation copies ({copies * per_copy / 2**20:.0f} MiB) > 2x L2",
+                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+            "e2e": {"value": round(ops_per_launch / (e_ms * 1e-3) / 1e12 * world, 3), "unit": "int8 TOP/s",
+                    "h2d_bytes_per_step": tokens * k * 4, "d2h_bytes_per_step": tokens * rows * 4,
+                    "ms_per_step": round(e_ms, 6),
+                    "path": "ops.quantize_q8_1 + ops.q4k_matmul_tokens with pinned H2D/D2H, graph-captured"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 3), "peak": peak, "unit": "int8 TOP/s",
+                         "frac": round(achieved / peak, 5) if peak else None,
+                         "peak_source": "2 x measured bf16 dense (the int8 dense rate)" if peak else None,
+                         "traffic": profiled_traffic(PREFILL["profile"]), "kernel": "prefill_q4k_kernel",
+                         "us_per_launch": round(ms * 1e3 / copies, 3),
+                         "note": "bound in practice by the fp64 scaling of every group's int32 dots"},
+            "cpu_baseline": None if cpu is None else {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * copies,
+        }
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- decode workload
 
 DECODE_TOKENS = 128
@@ -887,7 +1060,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched", "prefill"],
                     default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
     ap.add_argument("--copies", type=int, default=0)
@@ -903,12 +1076,14 @@ def main():
     if args.impl == "reference":
         if args.workload == "decode":
             run_decode_reference(args, rank, world)
+        elif args.workload == "prefill":
+            run_prefill_reference(args, rank, world)
         elif args.workload.startswith("imrope"):
             run_imrope_reference(args, rank, world, batched=args.workload == "imrope_batched")
         else:
             run_reference(args, rank, world)
         return
-    runner = {"decode": run_decode,
+    runner = {"decode": run_decode, "prefill": run_prefill,
               "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
               "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True)}.get(args.workload, run_ours)
     if world > 1:
