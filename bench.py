@@ -649,7 +649,30 @@ def run_prefill(args, rank: int, world: int):
 DECODE_TOKENS = 128
 
 
-def decode_cpu_reference(target_s: float = 15.0):
+def decode_host_cache(cfg, kv: str, dev):
+    """Host copy of the seeded KV cache for the oracle: fp16 bits (k, v) or,
+    for kv == "q4_0", None, None and the Q4_0 planes (k_qs, v_qs, d bits)."""
+    from mojo_llm_lab_b200 import decode as D
+
+    if kv == "f16":
+        k, v = D.generate_kv_cache(cfg, dev)
+        return k.cpu().numpy().view(np.uint16).copy(), v.cpu().numpy().view(np.uint16).copy(), None
+    if str(dev).startswith("cuda"):
+        c = D.generate_kv_cache_q4_0(cfg, dev)
+        planes = (c.k_qs.cpu().numpy().copy(), c.v_qs.cpu().numpy().copy(), c.d.cpu().numpy().view(np.uint16).copy())
+    else:  # no GPU: the oracle's quantiser over the same seeded rows
+        import oracle
+
+        qs = (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, 64)
+        planes = (np.zeros(qs, np.uint8), np.zeros(qs, np.uint8), np.zeros(qs[:3] + (8,), np.uint16))
+        for layer in range(cfg.layers):
+            for slot, p, lo in ((9, planes[0], 0), (10, planes[1], 4)):
+                rows = D._kv_values(cfg, layer, slot, dev).numpy()
+                p[layer, :, :cfg.context], planes[2][layer, :, :cfg.context, lo:lo + 4] = oracle.kv_q4_0_rows(rows)
+    return None, None, planes
+
+
+def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16"):
     """Time the oracle's decode step (oracle/decode.py over oracle/oracle.c, OpenMP over all
     host threads) on the 36-layer stack: whole tokens from the prefilled context."""
     import torch
@@ -661,21 +684,20 @@ def decode_cpu_reference(target_s: float = 15.0):
     # Data preparation only (torch's CPU generator takes ~30 s for 2.4 GB).
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     w = D.generate_weights(cfg, dev)
-    k, v = D.generate_kv_cache(cfg, dev)
     host = OD.host_model(w)
-    kh, vh = k.cpu().numpy().view(np.uint16).copy(), v.cpu().numpy().view(np.uint16).copy()
-    del w, k, v
+    kh, vh, planes = decode_host_cache(cfg, kv, dev)
+    del w
     threads = os.cpu_count() or 1
     token, pos, n, t0 = 17, cfg.context, 0, time.perf_counter()
     while True:
-        _, token = OD.reference_step(host, kh, vh, token, pos, threads)
+        _, token = OD.reference_step(host, kh, vh, token, pos, threads, q4_0=planes)
         pos, n = pos + 1, n + 1
         el = time.perf_counter() - t0
         if el >= target_s or pos >= cfg.ctx_capacity:
             break
     del torch
     return {"value": n / el, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} greedy tokens of the 36-layer stack from context 4096 in {el:.1f} s "
+            "sample": f"{n} greedy tokens of the 36-layer stack from context 4096 ({kv} KV) in {el:.1f} s "
                       f"(oracle/decode.py + oracle/oracle.c, OpenMP {threads} threads, float64)",
             "seconds_per_token": el / n}
 
@@ -683,12 +705,13 @@ def decode_cpu_reference(target_s: float = 15.0):
 def run_decode_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    ref = decode_cpu_reference(target_s=max(5.0, min(30.0, 2.0 * args.steps)))
+    ref = decode_cpu_reference(target_s=max(5.0, min(30.0, 2.0 * args.steps)), kv=args.kv)
     line = {"metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(ref["value"], 4),
             "unit": "tokens/s", "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ref["seconds_per_token"] * DECODE_TOKENS * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
-            "config": {"workload": "36-layer Qwen3-style decode, ctx 4096, 128 greedy tokens"},
+            "config": {"workload": "36-layer Qwen3-style decode, ctx 4096, 128 greedy tokens"
+                                   + ("" if args.kv == "f16" else ", Q4_0 KV cache")},
             "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(ref["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
@@ -708,7 +731,10 @@ def run_decode(args, rank: int, world: int):
     cfg = D.DecodeConfig()
     group = dist.group.WORLD if world > 1 else None
     weights = D.generate_weights(cfg, device, world=world, rank=rank)
-    k_cache, v_cache = D.generate_kv_cache(cfg, device)
+    if args.kv == "q4_0":
+        k_cache, v_cache = D.generate_kv_cache_q4_0(cfg, device), None
+    else:
+        k_cache, v_cache = D.generate_kv_cache(cfg, device)
     stream = torch.cuda.Stream(device)
     stream.wait_stream(torch.cuda.current_stream(device))
     torch.cuda.set_stream(stream)
@@ -732,17 +758,14 @@ def run_decode(args, rank: int, world: int):
         full = weights if world == 1 else D.generate_weights(cfg, device)
         host = OD.host_model(full)
         del full
-        kh0, vh0 = D.generate_kv_cache(cfg, device)
-        kh = kh0.cpu().numpy().view(np.uint16).copy()
-        vh = vh0.cpu().numpy().view(np.uint16).copy()
-        del kh0, vh0
-        ref, ref_next = OD.reference_step(host, kh, vh, start_token, cfg.context)
+        kh, vh, planes = decode_host_cache(cfg, args.kv, device)
+        ref, ref_next = OD.reference_step(host, kh, vh, start_token, cfg.context, q4_0=planes)
         agreement = OD.logit_agreement(ref, logits.cpu().numpy())
         if agreement["violations"] or not agreement["top_match"]:
             raise SystemExit(f"decode correctness gate failed: {agreement}")
         if dec.read_state()["next_token"] != ref_next:
             raise SystemExit("decode correctness gate failed: next token differs from the oracle")
-        del host, kh, vh
+        del host, kh, vh, planes
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -815,18 +838,21 @@ def run_decode(args, rank: int, world: int):
         mean_keys = cfg.context + (DECODE_TOKENS + 1) / 2
         rank_bytes = (cfg.q4k_bytes() - 2 * cfg.layers * (cfg.ffn - weights.ffn_shard.local_rows) * cfg.hidden
                       // 256 * 144 + weights.vocab_shard.local_rows * cfg.hidden // 256 * 210
-                      + cfg.kv_bytes_read(int(mean_keys)))
+                      + cfg.kv_bytes_read(int(mean_keys), args.kv))
         us_per_token = ms * 1e3 / DECODE_TOKENS
         achieved = rank_bytes / (us_per_token * 1e-6) / 1e9
-        cpu = None if args.no_cpu_baseline or world > 1 else decode_cpu_reference(target_s=10.0)
+        cpu = None if args.no_cpu_baseline or world > 1 else decode_cpu_reference(target_s=10.0, kv=args.kv)
         line = {
             "metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "Q4_K/Q6_K x Q8_1 dp4a, f64 accumulate; fp16 KV, f64 attention",
+            "dtype": "Q4_K/Q6_K x Q8_1 dp4a, f64 accumulate; " + ("fp16" if args.kv == "f16" else "Q4_0")
+                     + " KV, f64 attention",
             "data": "synthetic (seeded random weights, N(0,1) KV prefill)",
             "config": {"workload": "36-layer Qwen3-style decode (hidden 2560, 32/8 heads x 128, SwiGLU 9728, "
-                                   "vocab 151936), ctx 4096, 128 greedy tokens per step",
+                                   "vocab 151936), ctx 4096, 128 greedy tokens per step"
+                                   + ("" if args.kv == "f16" else ", Q4_0 KV cache"),
+                       "kv_cache": args.kv,
                        "us_per_token": round(us_per_token, 3), "bytes_per_token_per_gpu": int(rank_bytes),
                        "parallelism": ((f"gate/up + vocab rows/{world} per rank; " + ("peer-store Q8_1 all-gather over NVLink" if dec.peer is not None else "NCCL all-gather") + ", NCCL all-reduce of the argmax key") if world > 1 else "single GPU"),
                        "l2": "2.4 GB of weights per token > L2; no flush", "pdl": not args.no_pdl,
@@ -1063,6 +1089,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched", "prefill"],
                     default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
+    ap.add_argument("--kv", choices=["f16", "q4_0"], default="f16",
+                    help="decode: KV cache type (q4_0: GGML Q4_0, the reference's llama.cpp setting)")
     ap.add_argument("--copies", type=int, default=0)
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--skip-check", action="store_true")

@@ -399,6 +399,52 @@ int mllb_decode_attention_qkv_noalloc(const float *qkv, const float *q_gamma, co
                                       int64_t ctx, unsigned flags, void *stream);
 
 /*
+ * Q4_0 KV cache: the KV type of the reference's llama.cpp contexts
+ * (integration/resident_decode.cpp:70, cp.type_k = cp.type_v =
+ * GGML_TYPE_Q4_0; "-ctk q4_0 -ctv q4_0" in tools/run_prefill_bench.py:26).
+ * GGML's Q4_0 block (fp16 d, 32 x 4 bits, value d * (q - 8)), held as three
+ * planes so that every cache row is a 16-byte multiple:
+ *   k_qs [kv_heads][ctx][64]  nibbles of the 4 blocks of a K row (16 bytes
+ *                             per block: element e < 16 in the low nibble of
+ *                             byte e, element e + 16 in its high nibble)
+ *   v_qs [kv_heads][ctx][64]  the same for V
+ *   kv_d [kv_heads][ctx][8]   fp16 d of K blocks 0..3, then of V blocks 0..3
+ * All three 16-byte aligned for the attention entries.
+ */
+
+/*
+ * Quantise rows [row0, row0 + rows) of every KV head into the Q4_0 cache from
+ * fp32 k and v ([kv_heads][rows][128] each) by GGML's quantize_row_q4_0 rule
+ * (the element of largest magnitude, first on ties, gives d = max / -8;
+ * q = min(15, trunc(x * (1 / d) + 8.5)), the product and the sum each
+ * rounded to fp32; 1 / d taken as 0 when d is 0).  The prefill write of the cache; llama.cpp's
+ * set_rows into a Q4_0 cache.
+ */
+int mllb_kv_q4_0_store(const float *k, const float *v, void *k_qs, void *v_qs, void *kv_d, int64_t kv_heads,
+                       int64_t ctx, int64_t row0, int64_t rows, unsigned flags, void *stream);
+
+/*
+ * mllb_decode_attention over the Q4_0 cache (row state->pos already stored,
+ * e.g. by mllb_kv_q4_0_store).  Cache values enter the fp64 arithmetic
+ * exactly (d * (q - 8)); scratch as mllb_decode_attention_scratch.
+ */
+int mllb_decode_attention_q4_0(const float *q, const void *k_qs, const void *v_qs, const void *kv_d,
+                               const mllb_decode_state *state, double *scratch, int64_t scratch_doubles, float *out,
+                               void *q8, int64_t q_heads, int64_t kv_heads, int64_t ctx, unsigned flags,
+                               void *stream);
+
+/*
+ * mllb_decode_attention_qkv over the Q4_0 cache: the K row (RMSNorm + k_gamma
+ * + IMROPE, fp32) and the V row (fp32) of the token are quantised by the
+ * mllb_kv_q4_0_store rule and appended at state->pos.  GGML flash_attn_ext
+ * with Q4_0 K/V, as the reference runs it (integration/resident_decode.cpp:70-71).
+ */
+int mllb_decode_attention_qkv_q4_0(const float *qkv, const float *q_gamma, const float *k_gamma, double theta_scale,
+                                   const mllb_decode_state *state, void *k_qs, void *v_qs, void *kv_d,
+                                   double *scratch, int64_t scratch_doubles, float *out, void *q8, int64_t q_heads,
+                                   int64_t kv_heads, int64_t ctx, unsigned flags, void *stream);
+
+/*
  * *key = max(*key, max over i of key(x[i], index_offset + i)) with the packed
  * key of mllb_token_key (the greedy argmax; for a row shard pass the shard's
  * first row as index_offset).  *key must hold INT64_MIN or an earlier

@@ -75,6 +75,10 @@ SIGNATURES = {
                                             C.c_uint, _P]),
     "mllb_decode_attention_qkv_noalloc": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _P, _I64, _I64, _I64,
                                                     C.c_uint, _P]),
+    "mllb_kv_q4_0_store": (C.c_int, [_P, _P, _P, _P, _P, _I64, _I64, _I64, _I64, C.c_uint, _P]),
+    "mllb_decode_attention_q4_0": (C.c_int, [_P, _P, _P, _P, _P, _P, _I64, _P, _P, _I64, _I64, _I64, C.c_uint, _P]),
+    "mllb_decode_attention_qkv_q4_0": (C.c_int, [_P, _P, _P, C.c_double, _P, _P, _P, _P, _P, _I64, _P, _P, _I64,
+                                                 _I64, _I64, C.c_uint, _P]),
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
     "mllb_q8_1_quantize_allgather": (C.c_int, [_P, _I64, C.POINTER(PeerGather), C.c_uint, _P]),
     "mllb_prefetch_l2": (C.c_int, [_P, _I64, _P]),

@@ -559,24 +559,26 @@ struct AttentionArgs {
   double theta;
   int64_t q_heads, kv_heads, ctx;
   const mllb::DecodeState* state;
-  uint8_t* k_cache;
-  uint8_t* v_cache;
+  uint8_t* k_cache;      // fp16 rows, or the Q4_0 K nibble plane
+  uint8_t* v_cache;      // fp16 rows, or the Q4_0 V nibble plane
+  uint8_t* kv_d;         // Q4_0 scale plane (nullptr for fp16)
+  int kv;                // mllb::kKvF16 or mllb::kKvQ4_0
   double* part_acc;
   double* part_ml;
   int64_t splits;
 };
 
-template <int G>
+template <int G, int KV>
 int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
-  using C = mllb::AttnConfig<G>;
+  using C = mllb::AttnConfig<G, KV>;
   int dev, rc, grid, per_sm;
   if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::attn_split_kernel<G>;
+  auto kernel = mllb::attn_split_kernel<G, KV>;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, 1, &grid, &per_sm))) return rc;
   return launched(launch(kernel, dim3(static_cast<unsigned>(a.splits), static_cast<unsigned>(a.kv_heads)),
                          dim3(C::kThreads), C::kSmemBytes, stream, pdl, a.q, a.qkv, a.q_gamma, a.k_gamma, a.theta,
                          static_cast<int>(a.q_heads), static_cast<int>(a.kv_heads), a.state, a.k_cache, a.v_cache,
-                         a.part_acc, a.part_ml, static_cast<int>(a.ctx), static_cast<int>(a.splits),
+                         a.kv_d, a.part_acc, a.part_ml, static_cast<int>(a.ctx), static_cast<int>(a.splits),
                          1.0 / sqrt(128.0)),
                   "decode attention kernel");
 }
@@ -585,6 +587,8 @@ int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
 int attention_impl(AttentionArgs a, double* scratch, int64_t scratch_doubles, float* out, void* q8, unsigned flags,
                    void* stream) {
   if (!a.k_cache || !a.v_cache || !a.state || !scratch) return fail(MLLB_EINVAL, "null pointer");
+  if (a.kv == mllb::kKvQ4_0 && (!a.kv_d || !aligned(a.kv_d, 16)))
+    return fail(!a.kv_d ? MLLB_EINVAL : MLLB_EALIGN, "the Q4_0 scale plane must be non-null and 16-byte aligned");
   if (!out && !q8) return fail(MLLB_EINVAL, "no output requested");
   if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   int rc = check_attention_shape(a.q_heads, a.kv_heads, a.ctx);
@@ -605,11 +609,12 @@ int attention_impl(AttentionArgs a, double* scratch, int64_t scratch_doubles, fl
   a.part_ml = scratch + a.q_heads * a.splits * 128;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = flags & MLLB_LAUNCH_PDL;
+  const bool q4 = a.kv == mllb::kKvQ4_0;
   switch (a.q_heads / a.kv_heads) {
-    case 1: rc = launch_attention<1>(a, s, pdl); break;
-    case 2: rc = launch_attention<2>(a, s, pdl); break;
-    case 4: rc = launch_attention<4>(a, s, pdl); break;
-    default: rc = launch_attention<8>(a, s, pdl); break;
+    case 1: rc = q4 ? launch_attention<1, mllb::kKvQ4_0>(a, s, pdl) : launch_attention<1, mllb::kKvF16>(a, s, pdl); break;
+    case 2: rc = q4 ? launch_attention<2, mllb::kKvQ4_0>(a, s, pdl) : launch_attention<2, mllb::kKvF16>(a, s, pdl); break;
+    case 4: rc = q4 ? launch_attention<4, mllb::kKvQ4_0>(a, s, pdl) : launch_attention<4, mllb::kKvF16>(a, s, pdl); break;
+    default: rc = q4 ? launch_attention<8, mllb::kKvQ4_0>(a, s, pdl) : launch_attention<8, mllb::kKvF16>(a, s, pdl); break;
   }
   if (rc) return rc;
   return launched(launch(mllb::attn_combine_kernel, dim3(static_cast<unsigned>(a.q_heads)), dim3(128),
@@ -776,6 +781,67 @@ int mllb_decode_attention_qkv(const float* qkv, const float* q_gamma, const floa
   a.state = reinterpret_cast<const mllb::DecodeState*>(state);
   a.k_cache = static_cast<uint8_t*>(k_cache);
   a.v_cache = static_cast<uint8_t*>(v_cache);
+  return attention_impl(a, scratch, scratch_doubles, out, q8, flags, stream);
+}
+
+int mllb_kv_q4_0_store(const float* k, const float* v, void* k_qs, void* v_qs, void* kv_d, int64_t kv_heads,
+                       int64_t ctx, int64_t row0, int64_t rows, unsigned flags, void* stream) {
+  if (!k || !v || !k_qs || !v_qs || !kv_d) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (kv_heads <= 0 || kv_heads > 65535) return fail(MLLB_EINVAL, "kv_heads=%lld out of range", static_cast<long long>(kv_heads));
+  if (ctx <= 0 || ctx > (1 << 24)) return fail(MLLB_EINVAL, "ctx=%lld out of range", static_cast<long long>(ctx));
+  if (rows <= 0 || row0 < 0 || row0 + rows > ctx)
+    return fail(MLLB_EINVAL, "rows [%lld, %lld) outside the cache's %lld", static_cast<long long>(row0),
+                static_cast<long long>(row0 + rows), static_cast<long long>(ctx));
+  if (!aligned(k, 4) || !aligned(v, 4) || !aligned(kv_d, 2))
+    return fail(MLLB_EALIGN, "k/v need 4-byte, kv_d 2-byte alignment");
+  const int64_t warps = 2 * kv_heads * rows;
+  if (warps / 4 >= (1ll << 31)) return fail(MLLB_EINVAL, "too many rows");
+  return launched(launch(mllb::kv_q4_0_store_kernel, dim3(static_cast<unsigned>((warps + 3) / 4)), dim3(128), 0,
+                         static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, k, v,
+                         static_cast<uint8_t*>(k_qs), static_cast<uint8_t*>(v_qs), static_cast<uint16_t*>(kv_d),
+                         static_cast<int>(kv_heads), static_cast<int>(ctx), static_cast<int>(row0),
+                         static_cast<int>(rows)),
+                  "Q4_0 KV store kernel");
+}
+
+int mllb_decode_attention_q4_0(const float* q, const void* k_qs, const void* v_qs, const void* kv_d,
+                               const mllb_decode_state* state, double* scratch, int64_t scratch_doubles, float* out,
+                               void* q8, int64_t q_heads, int64_t kv_heads, int64_t ctx, unsigned flags,
+                               void* stream) {
+  if (!q) return fail(MLLB_EINVAL, "null pointer: q");
+  AttentionArgs a = {};
+  a.q = q;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.ctx = ctx;
+  a.state = reinterpret_cast<const mllb::DecodeState*>(state);
+  a.k_cache = static_cast<uint8_t*>(const_cast<void*>(k_qs));
+  a.v_cache = static_cast<uint8_t*>(const_cast<void*>(v_qs));
+  a.kv_d = static_cast<uint8_t*>(const_cast<void*>(kv_d));
+  a.kv = mllb::kKvQ4_0;
+  return attention_impl(a, scratch, scratch_doubles, out, q8, flags, stream);
+}
+
+int mllb_decode_attention_qkv_q4_0(const float* qkv, const float* q_gamma, const float* k_gamma, double theta_scale,
+                                   const mllb_decode_state* state, void* k_qs, void* v_qs, void* kv_d,
+                                   double* scratch, int64_t scratch_doubles, float* out, void* q8, int64_t q_heads,
+                                   int64_t kv_heads, int64_t ctx, unsigned flags, void* stream) {
+  if (!qkv || !q_gamma || !k_gamma) return fail(MLLB_EINVAL, "null pointer");
+  if (!(theta_scale > 0.0)) return fail(MLLB_EINVAL, "theta_scale must be positive");
+  AttentionArgs a = {};
+  a.qkv = qkv;
+  a.q_gamma = q_gamma;
+  a.k_gamma = k_gamma;
+  a.theta = theta_scale;
+  a.q_heads = q_heads;
+  a.kv_heads = kv_heads;
+  a.ctx = ctx;
+  a.state = reinterpret_cast<const mllb::DecodeState*>(state);
+  a.k_cache = static_cast<uint8_t*>(k_qs);
+  a.v_cache = static_cast<uint8_t*>(v_qs);
+  a.kv_d = static_cast<uint8_t*>(kv_d);
+  a.kv = mllb::kKvQ4_0;
   return attention_impl(a, scratch, scratch_doubles, out, q8, flags, stream);
 }
 

@@ -7,8 +7,9 @@
 //   rmsnorm_q8_1_kernel     h = x + delta (fp32); y = h * r * gamma -> Q8_1
 //   qk_rope_append_kernel   per-head RMSNorm + gamma + IMROPE of the Q and K
 //                           heads; K and V appended to the fp16 cache
-//   attn_split_kernel<G>    one (KV head, context chunk) per CTA: scores,
-//                           chunk softmax, P.V partials
+//   kv_q4_0_store_kernel    fp32 K/V rows -> the Q4_0 cache (GGML rule)
+//   attn_split_kernel<G,KV> one (KV head, context chunk) per CTA: scores,
+//                           chunk softmax, P.V partials; fp16 or Q4_0 cache
 //   attn_combine_kernel     merge the chunk partials -> fp32 -> Q8_1
 //   argmax_kernel           greedy next token as a packed (value, index) key
 //
@@ -214,6 +215,78 @@ __global__ void __launch_bounds__(128) qk_rope_append_kernel(const float* __rest
   }
 }
 
+// --------------------------------------------------------- Q4_0 KV cache
+
+// The Q4_0 cache (GGML's Q4_0 block: fp16 d and 32 4-bit q, value
+// d * (q - 8); the KV type the reference's llama.cpp contexts use,
+// integration/resident_decode.cpp:70) is kept as three planes per layer so
+// that every cache row is a 16-byte multiple and whole row ranges move with
+// one bulk copy:
+//   k_qs [kv_head][ctx][64]  the 4 blocks' 16 nibble bytes of the K row
+//   v_qs [kv_head][ctx][64]  the same for V
+//   kv_d [kv_head][ctx][8]   fp16 d of the K blocks 0..3, then of V 0..3
+// Within a block's 16 bytes, element e < 16 is the low nibble of byte e and
+// element e + 16 its high nibble (GGML's order).
+constexpr int kKvF16 = 0;
+constexpr int kKvQ4_0 = 1;
+constexpr int kQ4_0RowBytes = kHeadDim / 2;  // nibbles of one K or V row
+constexpr int kQ4_0DRowBytes = 16;           // the 8 fp16 block scales of one row
+
+// GGML's quantize_row_q4_0 (llama.cpp ggml-quants.c) for the block whose
+// element `lane` this lane holds: the element of largest magnitude (the
+// first on ties; NaN never wins) is vmax, d = vmax / -8, id = 1 / d (0 when
+// d == 0), q = min(15, trunc(x * id + 8.5)) with the product and the sum
+// each rounded to fp32 (no contraction).  Returns q | q(lane + 16) << 4 --
+// byte `lane` of the block on lanes 0..15 -- and d as fp16 bits.
+__device__ __forceinline__ uint32_t q4_0_quantize_lane(float x, uint16_t* d16) {
+  const uint32_t key = isnan(x) ? 0u : __float_as_uint(fabsf(x));
+  const uint32_t m = __reduce_max_sync(0xffffffffu, key);
+  const int first = __ffs(__ballot_sync(0xffffffffu, key == m)) - 1;
+  float vmax = __shfl_sync(0xffffffffu, x, first);
+  if (m == 0u) vmax = 0.0f;  // no element above zero: GGML keeps its +0 start value
+  const float d = __fdiv_rn(vmax, -8.0f);
+  const float id = d != 0.0f ? __fdiv_rn(1.0f, d) : 0.0f;
+  const int q = min(15, __float2int_rz(__fadd_rn(__fmul_rn(x, id), 8.5f)));
+  *d16 = __half_as_ushort(__float2half_rn(d));
+  const int hi = __shfl_down_sync(0xffffffffu, q, 16);
+  return static_cast<uint32_t>(q | (hi << 4));
+}
+
+// One warp quantises one 128-value row (4 blocks; x[i] is element lane of
+// block i) into `qs` (64 bytes) and `d` (4 fp16).
+__device__ __forceinline__ void q4_0_store_row(const float (&x)[4], int lane, uint8_t* qs, uint16_t* d) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    uint16_t d16;
+    const uint32_t byte = q4_0_quantize_lane(x[i], &d16);
+    if (lane < 16) qs[i * 16 + lane] = static_cast<uint8_t>(byte);
+    if (lane == 0) d[i] = d16;
+  }
+}
+
+// Rows [row0, row0 + rows) of every KV head from fp32 k and v, each
+// [kv_head][rows][128]: one warp per (head, row, K or V).
+__global__ void __launch_bounds__(128) kv_q4_0_store_kernel(const float* __restrict__ k, const float* __restrict__ v,
+                                                            uint8_t* __restrict__ k_qs, uint8_t* __restrict__ v_qs,
+                                                            uint16_t* __restrict__ kv_d, int hkv, int ctx, int row0,
+                                                            int rows) {
+  pdl_wait_prerequisite();
+  pdl_launch_dependents();
+  const int lane = threadIdx.x & 31;
+  const long long w = static_cast<long long>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const long long per_head = 2ll * rows;
+  if (w >= per_head * hkv) return;
+  const int j = static_cast<int>(w / per_head);
+  const int r = static_cast<int>((w % per_head) >> 1);
+  const bool is_v = (w & 1) != 0;
+  const float* src = (is_v ? v : k) + (static_cast<size_t>(j) * rows + r) * kHeadDim;
+  float x[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] = src[lane + 32 * i];
+  const size_t row = static_cast<size_t>(j) * ctx + row0 + r;
+  q4_0_store_row(x, lane, (is_v ? v_qs : k_qs) + row * kQ4_0RowBytes, kv_d + row * 8 + (is_v ? 4 : 0));
+}
+
 // ------------------------------------------------------------- attention
 
 // fp16 bit pattern -> its value x 2^-1008, exactly, for every finite half
@@ -255,8 +328,9 @@ __device__ __forceinline__ double transpose_reduce32(double (&v)[32], int lane) 
 
 // One CTA per (context chunk, KV head); G query heads share the KV head.
 // 16 warps where 128 registers a thread suffice (G = 4, the decode shape,
-// and G = 1), otherwise 8.
-template <int G>
+// and G = 1), otherwise 8.  KV: kKvF16 (rows of 128 fp16) or kKvQ4_0 (the
+// three planes above; the scale rows travel with the K rows).
+template <int G, int KV = kKvF16>
 struct AttnConfig {
   static constexpr int kWarps = (G == 4 || G == 1) ? 16 : 8;
   static constexpr int kThreads = kWarps * 32;
@@ -264,12 +338,16 @@ struct AttnConfig {
   static constexpr int kMaxChunk = 256;                   // keys per CTA
   static constexpr int kSub = 64;                         // keys per staged sub-chunk
   static constexpr int kNumSub = kMaxChunk / kSub;
-  static constexpr int kRowBytes = kHeadDim * 2;          // one fp16 K or V row
+  static constexpr int kRowBytes = KV == kKvQ4_0 ? kQ4_0RowBytes : kHeadDim * 2;  // one K or V row
+  static constexpr int kDRowBytes = KV == kKvQ4_0 ? kQ4_0DRowBytes : 0;
   static constexpr int kKeysPerPass = 32 / G;             // keys per warp per score pass
   static constexpr int kWarpsPerHead = kWarps / G;
   static constexpr int kKOffset = 0;
   static constexpr int kVOffset = kMaxChunk * kRowBytes;
-  static constexpr int kScoreOffset = 2 * kMaxChunk * kRowBytes;            // fp64 [G][kMaxChunk]
+  static constexpr int kDOffset = 2 * kMaxChunk * kRowBytes;                // Q4_0 scale rows
+  static constexpr int kKvBytes = kDOffset + kMaxChunk * kDRowBytes;
+  static constexpr int kRedBytes = kWarps * G * kHeadDim * 8;               // P.V cross-warp sums
+  static constexpr int kScoreOffset = ((kKvBytes > kRedBytes ? kKvBytes : kRedBytes) + 127) & ~127;  // fp64 [G][kMaxChunk]
   static constexpr int kQOffset = kScoreOffset + G * kMaxChunk * 8;         // fp32 [G][128]
   static constexpr int kRotOffset = kQOffset + G * kHeadDim * 4;            // double2 [64]
   static constexpr int kRedOffset = kRotOffset + kHeadDim / 2 * 16;         // fp64 [2][kWarps]
@@ -277,8 +355,14 @@ struct AttnConfig {
   static constexpr int kSmemBytes = kBarOffset + 2 * kNumSub * 8;
   static_assert(32 % G == 0 && G <= kWarps && kWarps % G == 0, "query heads per KV head");
   static_assert(kSub % kKeysPerPass == 0, "score passes stay inside one sub-chunk");
-  static_assert(kWarps * G * kHeadDim * 8 <= kScoreOffset, "P.V reduction buffer fits in the K and V buffers");
+  static_assert(KV == kKvF16 || KV == kKvQ4_0, "KV cache type");
 };
+
+// 2^52 + n as a double (exact for 0 <= n < 2^32), minus 2^52 + 8: the
+// Q4_0 value n - 8 without an integer-to-fp64 conversion.
+__device__ __forceinline__ double q4_0_value(uint32_t n) {
+  return __hiloint2double(0x43300000, static_cast<int>(n)) - 0x1.0000000000008p52;
+}
 
 // Chunk c of the n = pos + 1 keys: per = roundup16(ceil(n / splits)) keys
 // from c * per.  Writes, per query head hh = kv_head * G + g and chunk c:
@@ -294,20 +378,26 @@ struct AttnConfig {
 //  - qkv != nullptr (fused): this kernel does the per-head RMSNorm + gamma +
 //    IMROPE of the G query heads from the raw QKV projection, and the CTA
 //    whose chunk holds pos also forms the K row (RMSNorm + k_gamma + IMROPE
-//    -> fp32 -> fp16) and the V row (fp16), appends both to the caches and
-//    uses them directly.  The 64 rotations are built before the wait.
-template <int G>
-__global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasPerSm)
+//    -> fp32 -> fp16 or Q4_0) and the V row (fp32 -> fp16 or Q4_0), appends
+//    both to the caches and uses them directly.  The 64 rotations are built
+//    before the wait.
+// Q4_0 (KV == kKvQ4_0): k_cache / v_cache are the nibble planes and kv_d the
+// scale plane; cache values d * (q - 8) enter fp64 exactly (d through
+// half_bits_scaled, q - 8 through q4_0_value).
+template <int G, int KV>
+__global__ void __launch_bounds__(AttnConfig<G, KV>::kThreads, AttnConfig<G, KV>::kCtasPerSm)
     attn_split_kernel(const float* __restrict__ q, const float* __restrict__ qkv, const float* __restrict__ q_gamma,
                       const float* __restrict__ k_gamma, double theta, int hq, int hkv,
                       const DecodeState* __restrict__ state, uint8_t* __restrict__ k_cache,
-                      uint8_t* __restrict__ v_cache, double* __restrict__ part_acc, double* __restrict__ part_ml,
-                      int ctx, int splits, double scale) {
-  using C = AttnConfig<G>;
+                      uint8_t* __restrict__ v_cache, uint8_t* __restrict__ kv_d, double* __restrict__ part_acc,
+                      double* __restrict__ part_ml, int ctx, int splits, double scale) {
+  using C = AttnConfig<G, KV>;
   constexpr int W = C::kWarps, KB = C::kKeysPerPass, WG = C::kWarpsPerHead;
+  constexpr bool kQ4 = KV == kKvQ4_0;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* ks = smem + C::kKOffset;
   uint8_t* vs = smem + C::kVOffset;
+  uint8_t* ds = smem + C::kDOffset;
   double* sc = reinterpret_cast<double*>(smem + C::kScoreOffset);
   float* qs = reinterpret_cast<float*>(smem + C::kQOffset);
   double2* rot = reinterpret_cast<double2*>(smem + C::kRotOffset);
@@ -328,7 +418,8 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
   const int old_cnt = max(min(t1, pos) - t0, 0);
   const bool has_new = cnt > old_cnt;  // this chunk holds row pos
   const int sub_new = old_cnt / C::kSub;
-  const size_t row0 = (static_cast<size_t>(j) * ctx + t0) * C::kRowBytes;
+  const size_t first_row = static_cast<size_t>(j) * ctx + t0;
+  const size_t row0 = first_row * C::kRowBytes;
 
   if (tid == 0) {
     for (int s = 0; s < C::kNumSub; ++s) {
@@ -346,7 +437,14 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
       if (rows > 0) {
         const uint32_t bytes = static_cast<uint32_t>(rows) * C::kRowBytes;
         const size_t off = static_cast<size_t>(s) * C::kSub * C::kRowBytes;
-        mbar_arrive_expect_tx(&bar_k[s], bytes);
+        if constexpr (kQ4) {
+          const uint32_t dbytes = static_cast<uint32_t>(rows) * C::kDRowBytes;
+          const size_t doff = static_cast<size_t>(s) * C::kSub * C::kDRowBytes;
+          mbar_arrive_expect_tx(&bar_k[s], bytes + dbytes);
+          bulk_copy_g2s(ds + doff, kv_d + first_row * C::kDRowBytes + doff, dbytes, &bar_k[s], policy);
+        } else {
+          mbar_arrive_expect_tx(&bar_k[s], bytes);
+        }
         bulk_copy_g2s(ks + off, k_cache + row0 + off, bytes, &bar_k[s], policy);
       } else {
         mbar_arrive(&bar_k[s]);
@@ -385,24 +483,46 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
         dst[lane + 96] = static_cast<float>(o[3]);
       } else {
         const bool is_k = task == G;
-        __half hv[4];
+        float f[4];  // dims lane + 32 i, fp32
         if (is_k) {
           imrope_head_table(qkv + static_cast<size_t>(hq + j) * kHeadDim, k_gamma, rot, lane, o);
-          hv[0] = __float2half_rn(static_cast<float>(o[0]));  // dim lane
-          hv[1] = __float2half_rn(static_cast<float>(o[2]));  // dim lane + 32
-          hv[2] = __float2half_rn(static_cast<float>(o[1]));  // dim lane + 64
-          hv[3] = __float2half_rn(static_cast<float>(o[3]));  // dim lane + 96
+          f[0] = static_cast<float>(o[0]);
+          f[1] = static_cast<float>(o[2]);
+          f[2] = static_cast<float>(o[1]);
+          f[3] = static_cast<float>(o[3]);
         } else {
           const float* src = qkv + static_cast<size_t>(hq + hkv + j) * kHeadDim;
 #pragma unroll
-          for (int i = 0; i < 4; ++i) hv[i] = __float2half_rn(src[lane + 32 * i]);
+          for (int i = 0; i < 4; ++i) f[i] = src[lane + 32 * i];
         }
-        __half* srow = reinterpret_cast<__half*>((is_k ? ks : vs) + old_cnt * C::kRowBytes);
-        __half* grow = reinterpret_cast<__half*>((is_k ? k_cache : v_cache) + row0 + old_cnt * C::kRowBytes);
+        uint8_t* srow = (is_k ? ks : vs) + old_cnt * C::kRowBytes;
+        uint8_t* grow = (is_k ? k_cache : v_cache) + row0 + old_cnt * C::kRowBytes;
+        if constexpr (kQ4) {
+          const int dslot = is_k ? 0 : 4;
+          uint16_t* sd = reinterpret_cast<uint16_t*>(ds + old_cnt * C::kDRowBytes) + dslot;
+          uint16_t* gd = reinterpret_cast<uint16_t*>(kv_d + (first_row + old_cnt) * C::kDRowBytes) + dslot;
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          srow[lane + 32 * i] = hv[i];
-          grow[lane + 32 * i] = hv[i];
+          for (int i = 0; i < 4; ++i) {
+            uint16_t d16;
+            const uint32_t byte = q4_0_quantize_lane(f[i], &d16);
+            if (lane < 16) {
+              srow[i * 16 + lane] = static_cast<uint8_t>(byte);
+              grow[i * 16 + lane] = static_cast<uint8_t>(byte);
+            }
+            if (lane == 0) {
+              sd[i] = d16;
+              gd[i] = d16;
+            }
+          }
+        } else {
+          __half* sh = reinterpret_cast<__half*>(srow);
+          __half* gh = reinterpret_cast<__half*>(grow);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const __half hv = __float2half_rn(f[i]);
+            sh[lane + 32 * i] = hv;
+            gh[lane + 32 * i] = hv;
+          }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(is_k ? &bar_k[sub_new] : &bar_v[sub_new]);
@@ -411,14 +531,22 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
     if (pos >= ctx && split == 0 && j == 0 && tid == 0) record_error(kErrKvOverflow);
     __syncthreads();
   } else if (has_new && (tid == 0 || tid == 32)) {
+    // The appended row, read after the wait (K's thread also takes the Q4_0
+    // scale row, which holds the V scales too).
     const bool is_k = tid == 0;
+    constexpr int kChunks = C::kRowBytes / 16;
     const uint4* src = reinterpret_cast<const uint4*>((is_k ? k_cache : v_cache) + row0 + old_cnt * C::kRowBytes);
     uint4* dst = reinterpret_cast<uint4*>((is_k ? ks : vs) + old_cnt * C::kRowBytes);
-    uint4 row[16];
+    uint4 row[kChunks];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) row[i] = src[i];
+    for (int i = 0; i < kChunks; ++i) row[i] = src[i];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) dst[i] = row[i];
+    for (int i = 0; i < kChunks; ++i) dst[i] = row[i];
+    if constexpr (kQ4) {
+      if (is_k)
+        *reinterpret_cast<uint4*>(ds + old_cnt * C::kDRowBytes) =
+            *reinterpret_cast<const uint4*>(kv_d + (first_row + old_cnt) * C::kDRowBytes);
+    }
     mbar_arrive(is_k ? &bar_k[sub_new] : &bar_v[sub_new]);
   }
   // Lane l owns dims 4l..4l+3 of the G query heads, scaled by 2^1008.
@@ -432,6 +560,12 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
     qd[g][2] = static_cast<double>(v.z) * kTwo1008;
     qd[g][3] = static_cast<double>(v.w) * kTwo1008;
   }
+  // Q4_0: dims 4l..4l+3 are elements 4 (l % 8) .. + 3 of block l / 8, held
+  // in the low (l % 8 < 4) or high nibbles of the block's bytes 4 (l % 4)..+3.
+  const int q4_blk = lane >> 3;
+  const int q4_word = q4_blk * 16 + (lane & 3) * 4;
+  const int q4_shift = (lane & 4) ? 4 : 0;
+  const uint16_t* dsh = reinterpret_cast<const uint16_t*>(ds);
 
   MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 3);
   // Scores: a warp pass covers KB keys x G heads = 32 dot products; lane l
@@ -445,13 +579,27 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
 #pragma unroll
     for (int kp = 0; kp < KB; ++kp) {
       const int t = base + (kp ^ lane_key);
-      uint2 w = make_uint2(0u, 0u);
-      if (t < cnt) w = *reinterpret_cast<const uint2*>(ks + t * C::kRowBytes + lane * 8);
-      const double k0 = half_bits_scaled(w.x & 0xffffu), k1 = half_bits_scaled(w.x >> 16);
-      const double k2 = half_bits_scaled(w.y & 0xffffu), k3 = half_bits_scaled(w.y >> 16);
+      if constexpr (kQ4) {
+        uint32_t w = 0u, dh = 0u;
+        if (t < cnt) {
+          w = *reinterpret_cast<const uint32_t*>(ks + t * C::kRowBytes + q4_word) >> q4_shift;
+          dh = dsh[t * 8 + q4_blk];
+        }
+        const double k0 = q4_0_value(w & 15u), k1 = q4_0_value((w >> 8) & 15u);
+        const double k2 = q4_0_value((w >> 16) & 15u), k3 = q4_0_value((w >> 24) & 15u);
+        const double dk = half_bits_scaled(dh);
 #pragma unroll
-      for (int g = 0; g < G; ++g)
-        v[kp * G + g] = fma(qd[g][3], k3, fma(qd[g][2], k2, fma(qd[g][1], k1, qd[g][0] * k0)));
+        for (int g = 0; g < G; ++g)
+          v[kp * G + g] = dk * fma(qd[g][3], k3, fma(qd[g][2], k2, fma(qd[g][1], k1, qd[g][0] * k0)));
+      } else {
+        uint2 w = make_uint2(0u, 0u);
+        if (t < cnt) w = *reinterpret_cast<const uint2*>(ks + t * C::kRowBytes + lane * 8);
+        const double k0 = half_bits_scaled(w.x & 0xffffu), k1 = half_bits_scaled(w.x >> 16);
+        const double k2 = half_bits_scaled(w.y & 0xffffu), k3 = half_bits_scaled(w.y >> 16);
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+          v[kp * G + g] = fma(qd[g][3], k3, fma(qd[g][2], k2, fma(qd[g][1], k1, qd[g][0] * k0)));
+      }
     }
     const double total = transpose_reduce32<G>(v, lane);
     const int t = base + lane_key;
@@ -492,29 +640,49 @@ __global__ void __launch_bounds__(AttnConfig<G>::kThreads, AttnConfig<G>::kCtasP
   }
 
   MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 5);
-  // P.V: warp w takes keys w, w + W, ...; lane l owns dims 4l..4l+3.
-  for (int s = 0; s < C::kNumSub; ++s) ok = mbar_wait_bounded(&bar_v[s], 0) && ok;
+  // P.V: warp w takes keys w, w + W, ...; lane l owns dims 4l..4l+3.  (The
+  // Q4_0 V scales came with the K copies: those barriers are waited on too.)
+  for (int s = 0; s < C::kNumSub; ++s) {
+    ok = mbar_wait_bounded(&bar_v[s], 0) && ok;
+    if constexpr (kQ4) ok = mbar_wait_bounded(&bar_k[s], 0) && ok;
+  }
   double acc[G][4];
 #pragma unroll
   for (int g = 0; g < G; ++g) acc[g][0] = acc[g][1] = acc[g][2] = acc[g][3] = 0.0;
   for (int t = warp; t < cnt; t += W) {
-    const uint2 w = *reinterpret_cast<const uint2*>(vs + t * C::kRowBytes + lane * 8);
-    const double v0 = half_bits_scaled(w.x & 0xffffu), v1 = half_bits_scaled(w.x >> 16);
-    const double v2 = half_bits_scaled(w.y & 0xffffu), v3 = half_bits_scaled(w.y >> 16);
+    if constexpr (kQ4) {
+      const uint32_t w = *reinterpret_cast<const uint32_t*>(vs + t * C::kRowBytes + q4_word) >> q4_shift;
+      const double v0 = q4_0_value(w & 15u), v1 = q4_0_value((w >> 8) & 15u);
+      const double v2 = q4_0_value((w >> 16) & 15u), v3 = q4_0_value((w >> 24) & 15u);
+      const double dv = half_bits_scaled(dsh[t * 8 + 4 + q4_blk]);
 #pragma unroll
-    for (int g = 0; g < G; ++g) {
-      const double p = sc[g * C::kMaxChunk + t];
-      acc[g][0] = fma(p, v0, acc[g][0]);
-      acc[g][1] = fma(p, v1, acc[g][1]);
-      acc[g][2] = fma(p, v2, acc[g][2]);
-      acc[g][3] = fma(p, v3, acc[g][3]);
+      for (int g = 0; g < G; ++g) {
+        const double p = sc[g * C::kMaxChunk + t] * dv;
+        acc[g][0] = fma(p, v0, acc[g][0]);
+        acc[g][1] = fma(p, v1, acc[g][1]);
+        acc[g][2] = fma(p, v2, acc[g][2]);
+        acc[g][3] = fma(p, v3, acc[g][3]);
+      }
+    } else {
+      const uint2 w = *reinterpret_cast<const uint2*>(vs + t * C::kRowBytes + lane * 8);
+      const double v0 = half_bits_scaled(w.x & 0xffffu), v1 = half_bits_scaled(w.x >> 16);
+      const double v2 = half_bits_scaled(w.y & 0xffffu), v3 = half_bits_scaled(w.y >> 16);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        const double p = sc[g * C::kMaxChunk + t];
+        acc[g][0] = fma(p, v0, acc[g][0]);
+        acc[g][1] = fma(p, v1, acc[g][1]);
+        acc[g][2] = fma(p, v2, acc[g][2]);
+        acc[g][3] = fma(p, v3, acc[g][3]);
+      }
     }
   }
   if (!ok && tid == 0) record_error(kErrKvWaitTimeout);
   __syncthreads();
   MLLB_TRACE_CTA(blockIdx.y * gridDim.x + blockIdx.x, 6);
-  // Cross-warp sum in warp order through the K and V buffers (no longer read).
-  double* red = reinterpret_cast<double*>(ks);
+  // Cross-warp sum in warp order through the K / V / scale buffers (no
+  // longer read; the region holds at least kRedBytes).
+  double* red = reinterpret_cast<double*>(smem);
 #pragma unroll
   for (int g = 0; g < G; ++g) {
     double* dst = red + (warp * G + g) * kHeadDim + 4 * lane;

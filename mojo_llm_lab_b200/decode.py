@@ -8,7 +8,7 @@ profiles, docs/decode-profile.md:5-11): a stack of ``layers`` blocks
     per layer:
       a   = Q8_1(rmsnorm(h) * attn_gamma)
       qkv = Wqkv a                                    Q4_K, one fused matrix
-      q, k = rmsnorm(head) * q/k_gamma + IMROPE;  k, v -> fp16 KV cache
+      q, k = rmsnorm(head) * q/k_gamma + IMROPE;  k, v -> fp16 or Q4_0 KV cache
       o   = Wo Q8_1(attention(q, K, V))               Q4_K
       h  += o;  a = Q8_1(rmsnorm(h) * ffn_gamma)
       f   = up(a) * silu(gate(a))                     fused Q4_K gate/up
@@ -105,13 +105,15 @@ class DecodeConfig:
     def q6k_bytes(self) -> int:
         return self.vocab * self.hidden // 256 * F.Q6K_BLOCK_BYTES
 
-    def kv_bytes_read(self, n_keys: int) -> int:
-        """fp16 K and V bytes one step reads over n_keys cache rows."""
-        return self.layers * 2 * self.kv_heads * n_keys * HEAD_DIM * 2
+    def kv_bytes_read(self, n_keys: int, kv: str = "f16") -> int:
+        """K and V bytes one step reads over n_keys cache rows: fp16 rows, or
+        the Q4_0 planes (64 + 64 nibble bytes and 16 scale bytes a row)."""
+        per_row = 2 * HEAD_DIM * 2 if kv == "f16" else 2 * (HEAD_DIM // 2) + 16
+        return self.layers * self.kv_heads * n_keys * per_row
 
-    def bytes_per_token(self, n_keys: int) -> int:
+    def bytes_per_token(self, n_keys: int, kv: str = "f16") -> int:
         """Algorithmic HBM bytes of one step: every weight once, the KV rows once."""
-        return self.q4k_bytes() + self.q6k_bytes() + self.kv_bytes_read(n_keys)
+        return self.q4k_bytes() + self.q6k_bytes() + self.kv_bytes_read(n_keys, kv)
 
 
 def _seed(cfg: DecodeConfig, layer: int, slot: int) -> int:
@@ -237,6 +239,11 @@ def generate_weights(cfg: DecodeConfig, device, world: int = 1, rank: int = 0) -
                          output=output, embedding=embedding, ffn_shard=ffn_shard, vocab_shard=vocab_shard)
 
 
+def _kv_values(cfg: DecodeConfig, layer: int, slot: int, device) -> torch.Tensor:
+    g = _generator(torch.device(device), _seed(cfg, layer, slot))
+    return torch.randn((cfg.kv_heads, cfg.context, HEAD_DIM), generator=g, device=device, dtype=torch.float32)
+
+
 def generate_kv_cache(cfg: DecodeConfig, device) -> tuple[torch.Tensor, torch.Tensor]:
     """fp16 caches [layers, kv_heads, ctx_capacity, 128]: rows < context are
     N(0, 1) (seeded), the rest zero until decode appends them."""
@@ -245,10 +252,50 @@ def generate_kv_cache(cfg: DecodeConfig, device) -> tuple[torch.Tensor, torch.Te
     v = torch.zeros(shape, dtype=torch.float16, device=device)
     for layer in range(cfg.layers):
         for slot, cache in ((9, k), (10, v)):
-            g = _generator(torch.device(device), _seed(cfg, layer, slot))
-            cache[layer, :, :cfg.context] = torch.randn((cfg.kv_heads, cfg.context, HEAD_DIM), generator=g,
-                                                        device=device, dtype=torch.float32).half()
+            cache[layer, :, :cfg.context] = _kv_values(cfg, layer, slot, device).half()
     return k, v
+
+
+@dataclass
+class Q4_0Cache:
+    """The Q4_0 KV cache of every layer as three planes (the layout of
+    include/mllb200.h): GGML Q4_0 blocks, the KV type of the reference's
+    llama.cpp contexts (integration/resident_decode.cpp:70)."""
+
+    k_qs: torch.Tensor   # uint8 [layers, kv_heads, ctx, 64]: K nibbles
+    v_qs: torch.Tensor   # uint8 [layers, kv_heads, ctx, 64]: V nibbles
+    d: torch.Tensor      # fp16  [layers, kv_heads, ctx, 8]: K block scales, then V
+
+    @classmethod
+    def zeros(cls, layers: int, kv_heads: int, ctx: int, device) -> "Q4_0Cache":
+        qs = (layers, kv_heads, ctx, HEAD_DIM // 2)
+        return cls(torch.zeros(qs, dtype=torch.uint8, device=device), torch.zeros(qs, dtype=torch.uint8, device=device),
+                   torch.zeros((layers, kv_heads, ctx, 8), dtype=torch.float16, device=device))
+
+    @property
+    def device(self) -> torch.device:
+        return self.k_qs.device
+
+    def layer(self, i: int) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+        return self.k_qs[i], self.v_qs[i], self.d[i]
+
+    def clone(self) -> "Q4_0Cache":
+        return Q4_0Cache(self.k_qs.clone(), self.v_qs.clone(), self.d.clone())
+
+
+def generate_kv_cache_q4_0(cfg: DecodeConfig, device) -> Q4_0Cache:
+    """The Q4_0 cache of the same seeded N(0, 1) rows as generate_kv_cache
+    (quantised on the device by mllb_kv_q4_0_store, as a prefill writes it)."""
+    cache = Q4_0Cache.zeros(cfg.layers, cfg.kv_heads, cfg.ctx_capacity, device)
+    if cfg.context == 0:
+        return cache
+    stream = torch.cuda.current_stream(torch.device(device)).cuda_stream
+    for layer in range(cfg.layers):
+        k, v = _kv_values(cfg, layer, 9, device), _kv_values(cfg, layer, 10, device)
+        kq, vq, d = cache.layer(layer)
+        check(lib().mllb_kv_q4_0_store(k.data_ptr(), v.data_ptr(), kq.data_ptr(), vq.data_ptr(), d.data_ptr(),
+                                       cfg.kv_heads, cfg.ctx_capacity, 0, cfg.context, 0, stream), "kv_q4_0_store")
+    return cache
 
 
 def state_bytes(token: int, pos: int, steps: int = 0) -> bytes:
@@ -289,11 +336,13 @@ class Decoder:
     row-sharded as the module docstring describes.
     """
 
-    def __init__(self, weights: DecodeWeights, k_cache: torch.Tensor, v_cache: torch.Tensor, *, pdl: bool = True,
+    def __init__(self, weights: DecodeWeights, k_cache, v_cache: torch.Tensor | None = None, *, pdl: bool = True,
                  fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False, quant_tail: bool = True):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
+        # KV cache: fp16 K and V tensors, or one Q4_0Cache (v_cache None).
+        self.kv = "q4_0" if isinstance(k_cache, Q4_0Cache) else "f16"
         self.device = k_cache.device
         self.flags = LAUNCH_PDL if pdl else 0
         self.group = group
@@ -303,10 +352,17 @@ class Decoder:
                 raise ValueError("a sharded decoder needs a process group")
             if weights.ffn_shard.per_rank % 32 or weights.ffn_shard.per_rank * self.world != cfg.ffn:
                 raise ValueError("gate/up shards must be equal and a multiple of 32 rows")
-        if k_cache.shape != (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, HEAD_DIM) or k_cache.dtype != torch.float16:
-            raise ValueError("k_cache must be fp16 [layers, kv_heads, ctx_capacity, 128]")
-        if v_cache.shape != k_cache.shape or v_cache.dtype != torch.float16:
-            raise ValueError("v_cache must match k_cache")
+        if self.kv == "q4_0":
+            qs = (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, HEAD_DIM // 2)
+            if (v_cache is not None or k_cache.k_qs.shape != qs or k_cache.v_qs.shape != qs or
+                    k_cache.d.shape != qs[:3] + (8,) or k_cache.d.dtype != torch.float16):
+                raise ValueError("a Q4_0 cache comes alone, with planes [layers, kv_heads, ctx_capacity, 64 | 8]")
+        else:
+            if k_cache.shape != (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, HEAD_DIM) or \
+                    k_cache.dtype != torch.float16:
+                raise ValueError("k_cache must be fp16 [layers, kv_heads, ctx_capacity, 128]")
+            if v_cache is None or v_cache.shape != k_cache.shape or v_cache.dtype != torch.float16:
+                raise ValueError("v_cache must match k_cache")
         dev = self.device
         f32 = lambda n: torch.zeros(n, dtype=torch.float32, device=dev)  # noqa: E731
         u8 = lambda n: torch.zeros(n, dtype=torch.uint8, device=dev)  # noqa: E731
@@ -387,10 +443,7 @@ class Decoder:
             check(L.mllb_q4k_matvec_act(P(lw.qkv), act, P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s), "qkv")
             if out is not None:
                 cur = 1 - cur
-            check(L.mllb_decode_attention_qkv(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
-                                              P(self.k_cache[layer]), P(self.v_cache[layer]), P(b.scratch),
-                                              b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads, cfg.kv_heads,
-                                              cfg.ctx_capacity, fl, s), "attention")
+            self._attention(layer, lw, state, fl, s)
             check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
             act = ActF32(h[cur], P(b.o_out), P(lw.ffn_norm), h[1 - cur], cfg.eps, None)
             check(L.mllb_q4k_gate_up_act(P(lw.up), P(lw.gate), act, None, None, P(b.prod), ffn_local, cfg.hidden,
@@ -412,6 +465,23 @@ class Decoder:
         else:
             self._reduce_argmax(s, fl)
 
+    def _attention(self, layer: int, lw: LayerWeights, state: int, fl: int, s: int) -> None:
+        """q/k norm + IMROPE, KV append at the state's position, attention and
+        its combine (-> b.attn, b.q8_attn): two launches."""
+        cfg, b, L = self.cfg, self.b, lib()
+        P = lambda t: t.data_ptr()  # noqa: E731
+        if self.kv == "q4_0":
+            kq, vq, d = self.k_cache.layer(layer)
+            check(L.mllb_decode_attention_qkv_q4_0(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
+                                                   P(kq), P(vq), P(d), P(b.scratch), b.scratch.numel(), P(b.attn),
+                                                   P(b.q8_attn), cfg.q_heads, cfg.kv_heads, cfg.ctx_capacity, fl, s),
+                  "attention (Q4_0 cache)")
+        else:
+            check(L.mllb_decode_attention_qkv(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
+                                              P(self.k_cache[layer]), P(self.v_cache[layer]), P(b.scratch),
+                                              b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads, cfg.kv_heads,
+                                              cfg.ctx_capacity, fl, s), "attention")
+
     def _prefetch_layer(self, layer: int) -> None:
         """Issue the L2 prefetch of `layer` on the side stream once the main
         stream's work so far has completed."""
@@ -420,7 +490,8 @@ class Decoder:
         main = torch.cuda.current_stream(self.device)
         self.side.wait_stream(main)
         lw, L, sp = self.w.layers[layer], lib(), self.side.cuda_stream
-        for t in (lw.qkv, lw.o, lw.up, lw.gate, lw.down, self.k_cache[layer], self.v_cache[layer]):
+        kv = self.k_cache.layer(layer) if self.kv == "q4_0" else (self.k_cache[layer], self.v_cache[layer])
+        for t in (lw.qkv, lw.o, lw.up, lw.gate, lw.down, *kv):
             check(L.mllb_prefetch_l2(t.data_ptr(), t.numel() * t.element_size(), sp), "prefetch")
 
     def _join_side(self) -> None:
@@ -453,10 +524,7 @@ class Decoder:
             norm(None if layer == 0 else P(b.down_out), lw.attn_norm, "attn_norm")
             check(L.mllb_q4k_matvec_ex(P(lw.qkv), P(b.q8_hidden), P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s),
                   "qkv")
-            check(L.mllb_decode_attention_qkv(P(b.qkv), P(lw.q_norm), P(lw.k_norm), cfg.theta_scale, state,
-                                              P(self.k_cache[layer]), P(self.v_cache[layer]), P(b.scratch),
-                                              b.scratch.numel(), P(b.attn), P(b.q8_attn), cfg.q_heads, cfg.kv_heads,
-                                              cfg.ctx_capacity, fl, s), "attention")
+            self._attention(layer, lw, state, fl, s)
             check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
             norm(P(b.o_out), lw.ffn_norm, "ffn_norm")
             if self.quant_tail:
@@ -612,10 +680,11 @@ def main(argv=None) -> None:
     ap.add_argument("--graph", action="store_true", help="replay one captured CUDA graph per token")
     ap.add_argument("--fused", action="store_true", help="activations built inside the matvecs")
     ap.add_argument("--no-pdl", action="store_true")
+    ap.add_argument("--kv", choices=["f16", "q4_0"], default="f16", help="KV cache type")
     args = ap.parse_args(argv)
     cfg = DecodeConfig(layers=args.layers)
     w = generate_weights(cfg, "cuda")
-    k, v = generate_kv_cache(cfg, "cuda")
+    k, v = generate_kv_cache(cfg, "cuda") if args.kv == "f16" else (generate_kv_cache_q4_0(cfg, "cuda"), None)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
         dec = Decoder(w, k, v, pdl=not args.no_pdl, fused=args.fused)

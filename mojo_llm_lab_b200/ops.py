@@ -29,7 +29,8 @@ __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
     "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
     "rmsnorm_q8_1", "decode_embed", "decode_final_norm", "decode_qk_rope_append", "decode_attention",
-    "decode_attention_qkv", "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32", "q5_k_q8_1_matvec",
+    "decode_attention_qkv", "kv_q4_0_store", "decode_attention_q4_0", "decode_attention_qkv_q4_0",
+    "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32", "q5_k_q8_1_matvec",
     "argmax_key", "token_key", "key_token", "S_D_SUMQ", "S_SUM_X",
 ]
 
@@ -415,6 +416,88 @@ def decode_attention_qkv(qkv: torch.Tensor, q_gamma: torch.Tensor, k_gamma: torc
                                           state.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), scratch.data_ptr(),
                                           scratch.numel(), out.data_ptr(), q8.data_ptr(), q_heads, kv_heads, ctx,
                                           _flags(pdl), _stream(qkv)), "decode_attention_qkv")
+    return out, q8
+
+
+def _need_q4_0_cache(k_qs: torch.Tensor, v_qs: torch.Tensor, kv_d: torch.Tensor) -> tuple[int, int]:
+    _need(k_qs, "k_qs", torch.uint8)
+    _need(v_qs, "v_qs", torch.uint8)
+    _need(kv_d, "kv_d", torch.float16)
+    if k_qs.dim() != 3 or k_qs.shape[2] != F.HEAD_DIM // 2 or v_qs.shape != k_qs.shape:
+        raise ValueError("k_qs and v_qs must both be uint8 [kv_heads, ctx, 64]")
+    if kv_d.shape != (k_qs.shape[0], k_qs.shape[1], 8):
+        raise ValueError("kv_d must be fp16 [kv_heads, ctx, 8]")
+    return k_qs.shape[0], k_qs.shape[1]
+
+
+def kv_q4_0_store(k: torch.Tensor, v: torch.Tensor, k_qs: torch.Tensor, v_qs: torch.Tensor, kv_d: torch.Tensor,
+                  row0: int = 0, pdl: bool = False) -> None:
+    """Quantise fp32 K and V rows [kv_heads, rows, 128] into rows row0.. of
+    the Q4_0 cache planes (GGML quantize_row_q4_0 rule)."""
+    _need(k, "k", torch.float32)
+    _need(v, "v", torch.float32)
+    kv_heads, ctx = _need_q4_0_cache(k_qs, v_qs, kv_d)
+    if k.dim() != 3 or k.shape[0] != kv_heads or k.shape[2] != F.HEAD_DIM or v.shape != k.shape:
+        raise ValueError("k and v must both be fp32 [kv_heads, rows, 128]")
+    _same_device(k, v, k_qs, v_qs, kv_d)
+    check(lib().mllb_kv_q4_0_store(k.data_ptr(), v.data_ptr(), k_qs.data_ptr(), v_qs.data_ptr(), kv_d.data_ptr(),
+                                   kv_heads, ctx, row0, k.shape[1], _flags(pdl), _stream(k)), "kv_q4_0_store")
+
+
+def _attention_buffers(dev, q_heads: int, kv_heads: int, ctx: int, out, q8, scratch):
+    with torch.cuda.device(dev):
+        need = int(lib().mllb_decode_attention_scratch(q_heads, kv_heads, ctx))
+    if need < 0:
+        check(int(need), "decode_attention_scratch")
+    if scratch is None:
+        scratch = torch.empty(need, dtype=torch.float64, device=dev)
+    _need(scratch, "scratch", torch.float64)
+    width = q_heads * F.HEAD_DIM
+    if out is None:
+        out = torch.empty(width, dtype=torch.float32, device=dev)
+    if q8 is None:
+        q8 = torch.empty(F.q8_1_bytes(width), dtype=torch.uint8, device=dev)
+    return out, q8, scratch
+
+
+def decode_attention_q4_0(q: torch.Tensor, k_qs: torch.Tensor, v_qs: torch.Tensor, kv_d: torch.Tensor,
+                          state: torch.Tensor, out: torch.Tensor | None = None, q8: torch.Tensor | None = None,
+                          scratch: torch.Tensor | None = None, pdl: bool = False):
+    """decode_attention over the Q4_0 cache planes -> (out fp32, Q8_1 of out)."""
+    _need(q, "q", torch.float32)
+    _need_state(state)
+    kv_heads, ctx = _need_q4_0_cache(k_qs, v_qs, kv_d)
+    q_heads = q.numel() // F.HEAD_DIM
+    out, q8, scratch = _attention_buffers(q.device, q_heads, kv_heads, ctx, out, q8, scratch)
+    _same_device(q, k_qs, v_qs, kv_d, state, out, q8, scratch)
+    check(lib().mllb_decode_attention_q4_0(q.data_ptr(), k_qs.data_ptr(), v_qs.data_ptr(), kv_d.data_ptr(),
+                                           state.data_ptr(), scratch.data_ptr(), scratch.numel(), out.data_ptr(),
+                                           q8.data_ptr(), q_heads, kv_heads, ctx, _flags(pdl), _stream(q)),
+          "decode_attention_q4_0")
+    return out, q8
+
+
+def decode_attention_qkv_q4_0(qkv: torch.Tensor, q_gamma: torch.Tensor, k_gamma: torch.Tensor, state: torch.Tensor,
+                              k_qs: torch.Tensor, v_qs: torch.Tensor, kv_d: torch.Tensor, q_heads: int,
+                              theta_scale: float | None = None, out: torch.Tensor | None = None,
+                              q8: torch.Tensor | None = None, scratch: torch.Tensor | None = None,
+                              pdl: bool = False):
+    """decode_attention_qkv with the K/V rows appended to the Q4_0 cache planes."""
+    _need(qkv, "qkv", torch.float32)
+    _need(q_gamma, "q_gamma", torch.float32)
+    _need(k_gamma, "k_gamma", torch.float32)
+    _need_state(state)
+    kv_heads, ctx = _need_q4_0_cache(k_qs, v_qs, kv_d)
+    if qkv.numel() != (q_heads + 2 * kv_heads) * F.HEAD_DIM:
+        raise ValueError("qkv must hold (q_heads + 2 kv_heads) x 128 values")
+    out, q8, scratch = _attention_buffers(qkv.device, q_heads, kv_heads, ctx, out, q8, scratch)
+    theta = F.theta_scale_f32() if theta_scale is None else float(theta_scale)
+    _same_device(qkv, q_gamma, k_gamma, state, k_qs, v_qs, kv_d, out, q8, scratch)
+    check(lib().mllb_decode_attention_qkv_q4_0(qkv.data_ptr(), q_gamma.data_ptr(), k_gamma.data_ptr(), theta,
+                                               state.data_ptr(), k_qs.data_ptr(), v_qs.data_ptr(), kv_d.data_ptr(),
+                                               scratch.data_ptr(), scratch.numel(), out.data_ptr(), q8.data_ptr(),
+                                               q_heads, kv_heads, ctx, _flags(pdl), _stream(qkv)),
+          "decode_attention_qkv_q4_0")
     return out, q8
 
 

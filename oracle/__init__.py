@@ -21,6 +21,12 @@ wrappers whose names follow the reference:
                                        the reference has no Q6_K oracle)
 * ``q5k_matvec``                       public GGML Q5_K layout (parity unpinned:
                                        the reference has no Q5_K code)
+* ``quantize_q4_0`` / ``kv_q4_0_rows`` GGML quantize_row_q4_0 for the Q4_0 KV
+                                       cache the reference's contexts use
+                                       (integration/resident_decode.cpp:70);
+                                       parity unpinned (no reference Q4_0 code)
+* ``attention`` / ``attention_q4_0``   float64 softmax attention over an fp16 or
+                                       a Q4_0 cache
 """
 from __future__ import annotations
 
@@ -84,8 +90,11 @@ def lib() -> C.CDLL:
             "orc_q5k_matvec": (C.c_int, [P, P, i64, i64, P, C.c_int]),
             "orc_embed_q6k": (C.c_int, [P, i64, i64, P]),
             "orc_rmsnorm_q8_1": (C.c_int, [P, P, i64, P, C.c_double, P, P]),
-            "orc_qk_rope_append": (C.c_int, [P, C.c_int, C.c_int, P, P, C.c_int32, C.c_double, P, P, P]),
+            "orc_qk_rope_append": (C.c_int, [P, C.c_int, C.c_int, P, P, C.c_int32, C.c_double, P, P, P, P]),
             "orc_attention": (C.c_int, [P, P, P, i64, i64, C.c_int, C.c_int, P, C.c_int]),
+            "orc_q4_0_quantize": (C.c_int, [P, i64, P]),
+            "orc_q4_0_decode": (None, [P, P]),
+            "orc_attention_q4_0": (C.c_int, [P, P, P, P, i64, i64, C.c_int, C.c_int, P, C.c_int]),
             "orc_argmax": (i64, [P, i64]),
             "orc_version": (C.c_int, []),
         }
@@ -315,8 +324,20 @@ def qk_rope_append(qkv, q_heads: int, kv_heads: int, q_gamma, k_gamma, pos: int,
     v_row = np.empty(kv_heads * HEAD_DIM, dtype=np.uint16)
     qg, kg = _f32(q_gamma), _f32(k_gamma)
     _check(lib().orc_qk_rope_append(_ptr(qkv), q_heads, kv_heads, _ptr(qg), _ptr(kg), pos, theta_scale,
-                                    _ptr(q_out), _ptr(k_row), _ptr(v_row)), "qk_rope_append")
+                                    _ptr(q_out), _ptr(k_row), _ptr(v_row), None), "qk_rope_append")
     return q_out, k_row, v_row
+
+
+def qk_rope_f32(qkv, q_heads: int, kv_heads: int, q_gamma, k_gamma, pos: int, theta_scale: float):
+    """(q_out, k rows, v rows), all fp32: the values a Q4_0 cache append quantises."""
+    qkv = _f32(qkv)
+    q_out = np.empty(q_heads * HEAD_DIM, dtype=np.float32)
+    k_f32 = np.empty(kv_heads * HEAD_DIM, dtype=np.float32)
+    qg, kg = _f32(q_gamma), _f32(k_gamma)
+    _check(lib().orc_qk_rope_append(_ptr(qkv), q_heads, kv_heads, _ptr(qg), _ptr(kg), pos, theta_scale,
+                                    _ptr(q_out), None, None, _ptr(k_f32)), "qk_rope_f32")
+    v = qkv[(q_heads + kv_heads) * HEAD_DIM:(q_heads + 2 * kv_heads) * HEAD_DIM].copy()
+    return q_out, k_f32, v
 
 
 def attention(q, k_cache: np.ndarray, v_cache: np.ndarray, n: int, q_heads: int, kv_heads: int,
@@ -329,6 +350,52 @@ def attention(q, k_cache: np.ndarray, v_cache: np.ndarray, n: int, q_heads: int,
     out = np.empty(q_heads * HEAD_DIM, dtype=np.float32)
     _check(lib().orc_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), ctx, n, q_heads, kv_heads, _ptr(out),
                                threads), "attention")
+    return out
+
+
+Q4_0_BLOCK_BYTES = 18
+
+
+def quantize_q4_0(x) -> np.ndarray:
+    """GGML Q4_0 blocks (18 bytes per 32 values) of fp32 x."""
+    x = _f32(x)
+    out = np.empty(x.size // 32 * Q4_0_BLOCK_BYTES, dtype=np.uint8)
+    _check(lib().orc_q4_0_quantize(_ptr(x), x.size, _ptr(out)), "q4_0_quantize")
+    return out
+
+
+def dequantize_q4_0(blocks: np.ndarray) -> np.ndarray:
+    """float64 values of Q4_0 blocks."""
+    blocks = np.ascontiguousarray(blocks, dtype=np.uint8).reshape(-1, Q4_0_BLOCK_BYTES)
+    out = np.empty(blocks.shape[0] * 32, dtype=np.float64)
+    for i in range(blocks.shape[0]):
+        lib().orc_q4_0_decode(_ptr(blocks[i]), _ptr(out[i * 32:]))
+    return out
+
+
+def kv_q4_0_rows(rows) -> tuple[np.ndarray, np.ndarray]:
+    """Q4_0 cache planes of fp32 rows [..., 128]: (nibbles [..., 64] uint8,
+    block scales [..., 4] fp16 bits), the split of GGML's 18-byte blocks."""
+    lead = np.shape(rows)[:-1]
+    assert np.shape(rows)[-1] == HEAD_DIM
+    blocks = quantize_q4_0(rows).reshape(-1, 4, Q4_0_BLOCK_BYTES)
+    d = np.ascontiguousarray(blocks[:, :, :2]).view(np.uint16).reshape(*lead, 4)
+    qs = np.ascontiguousarray(blocks[:, :, 2:]).reshape(*lead, 64)
+    return qs, d
+
+
+def attention_q4_0(q, k_qs: np.ndarray, v_qs: np.ndarray, kv_d: np.ndarray, n: int, q_heads: int, kv_heads: int,
+                   threads: int = 0) -> np.ndarray:
+    """attention over the Q4_0 cache planes: k_qs / v_qs uint8 [kv][ctx][64],
+    kv_d fp16 bits [kv][ctx][8] (K block scales, then V)."""
+    q = _f32(q)
+    assert k_qs.dtype == np.uint8 and v_qs.dtype == np.uint8 and kv_d.dtype == np.uint16
+    for a in (k_qs, v_qs, kv_d):
+        assert a.flags.c_contiguous
+    ctx = k_qs.shape[-2]
+    out = np.empty(q_heads * HEAD_DIM, dtype=np.float32)
+    _check(lib().orc_attention_q4_0(_ptr(q), _ptr(k_qs), _ptr(v_qs), _ptr(kv_d), ctx, n, q_heads, kv_heads,
+                                    _ptr(out), threads), "attention_q4_0")
     return out
 
 

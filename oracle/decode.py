@@ -5,7 +5,8 @@ Composes the oracle's per-op restatements (``oracle.c``) into the step that
 layer residual + RMSNorm -> Q8_1, the fused QKV matvec, q/k RMSNorm + IMROPE
 with the fp16 KV append, attention, the O matvec, residual + RMSNorm, the
 gate/up SwiGLU, Q8_1 of the product, the down matvec; final norm, Q6_K
-logits, first-maximum argmax.  Every value handed from one op to the next is
+logits, first-maximum argmax.  The KV cache is fp16 rows or the Q4_0 planes
+(GGML quantize_row_q4_0 of the fp32 K / V rows).  Every value handed from one op to the next is
 rounded to fp32 (fp16 in the cache, Q8_1 bytes for matvec inputs) exactly
 where the GPU rounds it, so the two agree bit for bit barring rounding ties.
 
@@ -20,8 +21,8 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from . import (argmax, attention, embed_q6k, q4k_gate_up, q4k_matvec, q6k_matvec, qk_rope_append,
-               quantize_q8_1, rmsnorm_q8_1)
+from . import (argmax, attention, attention_q4_0, embed_q6k, kv_q4_0_rows, q4k_gate_up, q4k_matvec, q6k_matvec,
+               qk_rope_append, qk_rope_f32, quantize_q8_1, rmsnorm_q8_1)
 
 ATOL = 1e-4
 RTOL = 1e-5
@@ -67,20 +68,29 @@ def host_model(weights) -> HostModel:
                      output=np_(weights.embedding))
 
 
-def reference_step(m: HostModel, k_cache: np.ndarray, v_cache: np.ndarray, token: int, pos: int,
-                   threads: int = 0) -> tuple[np.ndarray, int]:
+def reference_step(m: HostModel, k_cache: np.ndarray | None, v_cache: np.ndarray | None, token: int, pos: int,
+                   threads: int = 0, q4_0: tuple | None = None) -> tuple[np.ndarray, int]:
     """One decode step of `token` at `pos`.  k_cache / v_cache: fp16 bit
     patterns (uint16) [layers, kv_heads, ctx, 128], updated in place at row
-    `pos`.  Returns (fp32 logits, greedy next token)."""
+    `pos`; or, with q4_0 = (k_qs uint8 [layers, kv_heads, ctx, 64], v_qs,
+    d fp16 bits [layers, kv_heads, ctx, 8]), the Q4_0 cache planes, updated
+    in place.  Returns (fp32 logits, greedy next token)."""
     h = embed_q6k(m.output, m.hidden, token)
     delta = None
     for layer, lw in enumerate(m.layers):
         h, a = rmsnorm_q8_1(h, delta, lw.attn_norm, m.eps)
         qkv = q4k_matvec(lw.qkv, a, (m.q_heads + 2 * m.kv_heads) * 128, m.hidden, threads).astype(np.float32)
-        q, k_row, v_row = qk_rope_append(qkv, m.q_heads, m.kv_heads, lw.q_norm, lw.k_norm, pos, m.theta_scale)
-        k_cache[layer, :, pos, :] = k_row.reshape(m.kv_heads, 128)
-        v_cache[layer, :, pos, :] = v_row.reshape(m.kv_heads, 128)
-        att = attention(q, k_cache[layer], v_cache[layer], pos + 1, m.q_heads, m.kv_heads, threads)
+        if q4_0 is None:
+            q, k_row, v_row = qk_rope_append(qkv, m.q_heads, m.kv_heads, lw.q_norm, lw.k_norm, pos, m.theta_scale)
+            k_cache[layer, :, pos, :] = k_row.reshape(m.kv_heads, 128)
+            v_cache[layer, :, pos, :] = v_row.reshape(m.kv_heads, 128)
+            att = attention(q, k_cache[layer], v_cache[layer], pos + 1, m.q_heads, m.kv_heads, threads)
+        else:
+            k_qs, v_qs, kv_d = q4_0
+            q, k_f32, v_f32 = qk_rope_f32(qkv, m.q_heads, m.kv_heads, lw.q_norm, lw.k_norm, pos, m.theta_scale)
+            k_qs[layer, :, pos], kv_d[layer, :, pos, :4] = kv_q4_0_rows(k_f32.reshape(m.kv_heads, 128))
+            v_qs[layer, :, pos], kv_d[layer, :, pos, 4:] = kv_q4_0_rows(v_f32.reshape(m.kv_heads, 128))
+            att = attention_q4_0(q, k_qs[layer], v_qs[layer], kv_d[layer], pos + 1, m.q_heads, m.kv_heads, threads)
         o = q4k_matvec(lw.o, quantize_q8_1(att), m.hidden, m.q_heads * 128, threads).astype(np.float32)
         h, a = rmsnorm_q8_1(h, o, lw.ffn_norm, m.eps)
         _, _, prod = q4k_gate_up(lw.up, lw.gate, a, m.ffn, m.hidden, threads)

@@ -108,3 +108,64 @@ def test_gguf_loaded_stack_decodes_identically(tmp_path):
     b = D.Decoder(w2, k2, v2)
     assert a.generate(123, 4) == b.generate(123, 4)
     assert torch.equal(a.b.logits, b.b.logits)
+
+
+def run_q4_0_against_oracle(cfg, steps, token=17, graph=False, mode="quant_tail"):
+    """The same steps over the Q4_0 KV cache (the reference's KV type)."""
+    w = D.generate_weights(cfg, "cuda")
+    cache = D.generate_kv_cache_q4_0(cfg, "cuda")
+    host = OD.host_model(w)
+    planes = (cache.k_qs.cpu().numpy().copy(), cache.v_qs.cpu().numpy().copy(),
+              cache.d.cpu().numpy().view(np.uint16).copy())
+    stream = torch.cuda.Stream()
+    with torch.cuda.stream(stream):
+        dec = D.Decoder(w, cache, fused=mode == "fused", quant_tail=mode == "quant_tail")
+        assert dec.kv == "q4_0"
+        dec.reset(token)
+        if graph:
+            dec.capture()
+        pos = cfg.context
+        for _ in range(steps):
+            dec.replay() if graph else dec.step()
+            stream.synchronize()
+            got = dec.b.logits.cpu().numpy()
+            ref, ref_next = OD.reference_step(host, None, None, token, pos, q4_0=planes)
+            agree = OD.logit_agreement(ref, got)
+            assert agree["violations"] == 0, agree
+            assert agree["top_match"], agree
+            assert agree["bit_exact"] > 0.99 * agree["values"], agree
+            st = dec.read_state()
+            assert st["next_token"] == ref_next and st["pos"] == pos + 1
+            token, pos = ref_next, pos + 1
+    got_planes = (cache.k_qs.cpu().numpy(), cache.v_qs.cpu().numpy(), cache.d.cpu().numpy().view(np.uint16))
+    for got_p, ref_p in zip(got_planes, planes):
+        assert np.array_equal(got_p[:, :, :cfg.context], ref_p[:, :, :cfg.context])
+        assert (got_p[:, :, cfg.context:pos] == ref_p[:, :, cfg.context:pos]).mean() > 0.99
+    assert ops.device_error() == 0
+
+
+def test_q4_0_cache_holds_the_quantised_fp16_rows(orc):
+    """generate_kv_cache_q4_0 quantises the same seeded rows generate_kv_cache holds."""
+    cfg = D.DecodeConfig(layers=1, vocab=1000, context=40, new_tokens=2)
+    cache = D.generate_kv_cache_q4_0(cfg, "cuda")
+    k16, _ = D.generate_kv_cache(cfg, "cuda")
+    deq = orc.dequantize_q4_0(np.concatenate(
+        [cache.d[0, :, :cfg.context, :4].cpu().numpy().view(np.uint8).reshape(-1, 4, 2),
+         cache.k_qs[0, :, :cfg.context].cpu().numpy().reshape(-1, 4, 16)], axis=-1).reshape(-1))
+    k = k16[0, :, :cfg.context].float().cpu().numpy().reshape(-1)
+    assert np.abs(deq - k).max() < 0.5  # N(0, 1) rows: |d| <= ~0.6, error <= |d|
+
+
+@pytest.mark.parametrize("cfg", [SMALL, ODD], ids=["qwen-2layer", "odd-shapes"])
+@pytest.mark.parametrize("mode", ["quant_tail", "fused"])
+def test_decode_steps_q4_0_cache_match_oracle(orc, cfg, mode):
+    run_q4_0_against_oracle(cfg, steps=3, mode=mode)
+
+
+def test_graph_replay_q4_0_cache_matches_oracle(orc):
+    run_q4_0_against_oracle(SMALL, steps=3, graph=True)
+
+
+def test_full_size_decode_q4_0_cache_matches_oracle(orc):
+    """36 layers, 151936 vocabulary, context 4096, Q4_0 cache: two steps."""
+    run_q4_0_against_oracle(D.DecodeConfig(), steps=2)
