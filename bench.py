@@ -163,6 +163,22 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(samples)}
 
 
+def preroll(graph, seconds: float = 0.5) -> None:
+    """Replay `graph` for about `seconds` (untimed) so that the clock samples
+    taken around the timed region describe the same load.  For graphs with no
+    collectives (every rank may replay a different number of times)."""
+    import torch
+
+    t0 = time.perf_counter()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    n = max(1, int(seconds / max((time.perf_counter() - t0) / 3, 1e-6)))
+    for _ in range(n):
+        graph.replay()
+    torch.cuda.synchronize()
+
+
 # ----------------------------------------------------------------------------- inputs
 
 def host_weights(kind: str, rows: int, k: int, seed: int):
@@ -567,9 +583,7 @@ def run_prefill(args, rank: int, world: int):
     torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
+        preroll(graph)
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
@@ -644,6 +658,251 @@ def run_prefill(args, rank: int, world: int):
         print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- attention workload
+
+ATTN = dict(q_heads=32, kv_heads=8, extra_rows=128, profile="attn_split_ctx32k_f16_q4_0")
+
+
+def attention_describe(context: int, kv: str) -> str:
+    return (f"decode attention, {ATTN['q_heads']} q / {ATTN['kv_heads']} KV heads x 128, {context + 1} keys, "
+            f"{'fp16' if kv == 'f16' else 'Q4_0'} KV cache (fused q/k norm + IMROPE + append)")
+
+
+def attention_kv_bytes(context: int, kv: str) -> int:
+    """K and V bytes one call reads (the context rows and the appended one)."""
+    per_row = 512 if kv == "f16" else 144
+    return ATTN["kv_heads"] * (context + 1) * per_row
+
+
+def attention_host_cache(kv: str, capacity: int, seed: int):
+    """Seeded N(0, 1) K / V rows [kv_heads, capacity, 128] as the cache holds them."""
+    rng = np.random.default_rng(seed)
+    k = rng.standard_normal((ATTN["kv_heads"], capacity, 128), dtype=np.float32)
+    v = rng.standard_normal((ATTN["kv_heads"], capacity, 128), dtype=np.float32)
+    if kv == "f16":
+        return k.astype(np.float16), v.astype(np.float16)
+    return k, v
+
+
+def attention_cpu_reference(context: int, kv: str, target_s: float = 8.0):
+    """The oracle's attention (oracle/oracle.c, OpenMP over all host threads) on the same shapes."""
+    import oracle
+
+    hq, hkv = ATTN["q_heads"], ATTN["kv_heads"]
+    capacity = context + ATTN["extra_rows"]
+    k, v = attention_host_cache(kv, capacity, seed=1)
+    if kv == "q4_0":
+        kq, kd = oracle.kv_q4_0_rows(k)
+        vq, vd = oracle.kv_q4_0_rows(v)
+        d = np.ascontiguousarray(np.concatenate([kd, vd], axis=-1))
+    else:
+        k, v = k.view(np.uint16), v.view(np.uint16)
+    q = np.random.default_rng(2).standard_normal(hq * 128).astype(np.float32)
+    threads = os.cpu_count() or 1
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        if kv == "q4_0":
+            oracle.attention_q4_0(q, kq, vq, d, context + 1, hq, hkv, threads)
+        else:
+            oracle.attention(q, k, v, context + 1, hq, hkv, threads)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= target_s:
+            break
+    per = el / reps
+    return {"value": attention_kv_bytes(context, kv) / per / 1e9, "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{reps} attention calls over {context + 1} keys ({kv} cache) in {el:.1f} s "
+                      f"(oracle/oracle.c, OpenMP {threads} threads, float64)", "seconds_per_call": per}
+
+
+def run_attention_reference(args, rank: int, world: int):
+    if rank != 0:
+        return
+    ref = attention_cpu_reference(args.context, args.kv, target_s=max(3.0, min(20.0, 1.0 * args.steps)))
+    line = {"metric": f"{attention_describe(args.context, args.kv)} KV GB/s", "value": round(ref["value"], 4),
+            "unit": "GB/s", "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ref["seconds_per_call"] * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded N(0,1) K/V)",
+            "config": {"workload": attention_describe(args.context, args.kv)},
+            "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": round(ref["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def attention_profiled_traffic(context: int, kv: str):
+    """Per-launch DRAM bytes of the split kernel from the committed ncu summary (32768-key context only)."""
+    p = ROOT / "profiles" / f"{ATTN['profile']}.txt"
+    if context != 32768 or not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("traffic_bytes_per_launch:"):
+            for part in line.split(":", 1)[1].split(","):
+                name, _, val = part.strip().partition(" ")
+                if name == kv:
+                    try:
+                        return int(val.strip("() "))
+                    except ValueError:
+                        return None
+    return None
+
+
+def run_attention(args, rank: int, world: int):
+    """One step = `copies` fused attention calls (decode_attention_qkv[_q4_0]) over distinct caches
+    (> 2x L2 together), PDL-chained in one CUDA graph: q/k RMSNorm + IMROPE, the K/V append at
+    row `context`, attention over context + 1 keys, combine -> fp32 + Q8_1."""
+    import torch
+
+    from mojo_llm_lab_b200 import decode as D
+    from mojo_llm_lab_b200 import formats as F
+    from mojo_llm_lab_b200 import ops
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    hq, hkv, kv, context = ATTN["q_heads"], ATTN["kv_heads"], args.kv, args.context
+    capacity = context + ATTN["extra_rows"]
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    kh, vh = attention_host_cache(kv, capacity, seed=1)
+    per_copy = attention_kv_bytes(capacity - 1, kv)
+    copies = args.copies or max(2, -(-int(2.2 * L2_BYTES) // per_copy))
+
+    def make_cache():
+        if kv == "f16":
+            return torch.from_numpy(kh).to(device), torch.from_numpy(vh).to(device)
+        c = D.Q4_0Cache.zeros(1, hkv, capacity, device)
+        kq, vq, d = c.layer(0)
+        ops.kv_q4_0_store(torch.from_numpy(kh).to(device), torch.from_numpy(vh).to(device), kq, vq, d)
+        return kq, vq, d
+
+    caches = [make_cache()]
+    caches += [tuple(t.clone() for t in caches[0]) for _ in range(copies - 1)]
+    rng = np.random.default_rng(3)
+    qkv_host = (rng.standard_normal((hq + 2 * hkv) * 128) * 30).astype(np.float32)
+    qg = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kg = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    qkv, q_gamma, k_gamma = (torch.from_numpy(a).to(device) for a in (qkv_host, qg, kg))
+    state = torch.frombuffer(bytearray(D.state_bytes(0, context)), dtype=torch.uint8).to(device)
+    theta = F.theta_scale_f32()
+    out = torch.empty(hq * 128, dtype=torch.float32, device=device)
+    q8 = torch.empty(hq * 128 // 32 * 36, dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        scratch = torch.empty(int(ops.lib().mllb_decode_attention_scratch(hq, hkv, capacity)), dtype=torch.float64,
+                              device=device)
+
+    def call(i, pdl=True):
+        c = caches[i]
+        if kv == "f16":
+            ops.decode_attention_qkv(qkv, q_gamma, k_gamma, state, c[0], c[1], hq, theta, out, q8, scratch, pdl=pdl)
+        else:
+            ops.decode_attention_qkv_q4_0(qkv, q_gamma, k_gamma, state, c[0], c[1], c[2], hq, theta, out, q8,
+                                          scratch, pdl=pdl)
+
+    call(0, pdl=False)
+    torch.cuda.synchronize()
+    if not args.skip_check and rank == 0:
+        import oracle
+        got = out.cpu().numpy()
+        if kv == "f16":
+            q_ref, _, _ = oracle.qk_rope_append(qkv_host, hq, hkv, qg, kg, context, theta)
+            ref = oracle.attention(q_ref, caches[0][0].cpu().numpy().view(np.uint16),
+                                   caches[0][1].cpu().numpy().view(np.uint16), context + 1, hq, hkv)
+        else:
+            q_ref, _, _ = oracle.qk_rope_f32(qkv_host, hq, hkv, qg, kg, context, theta)
+            c = caches[0]
+            ref = oracle.attention_q4_0(q_ref, c[0].cpu().numpy(), c[1].cpu().numpy(),
+                                        np.ascontiguousarray(c[2].cpu().numpy().view(np.uint16)), context + 1, hq, hkv)
+        if not np.all(np.abs(got - ref) <= 1e-5 + 1e-5 * np.abs(ref)):
+            raise SystemExit("attention correctness gate failed against the oracle")
+
+    def step():
+        for i in range(copies):
+            call(i)
+
+    step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        preroll(graph)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    kv_bytes = attention_kv_bytes(context, kv)
+    us_call = ms * 1e3 / copies
+    gbs = kv_bytes / (us_call * 1e-6) / 1e9
+
+    # e2e through the public API with host buffers: the raw QKV projection from
+    # pinned host memory, the fused attention, its fp32 output back; graph-captured.
+    qkv_pin = torch.from_numpy(qkv_host).pin_memory()
+    out_pin = torch.empty(hq * 128, dtype=torch.float32).pin_memory()
+
+    def e2e_step():
+        qkv.copy_(qkv_pin, non_blocking=True)
+        call(0)
+        out_pin.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    e_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(e_graph, stream=stream):
+        e2e_step()
+    for _ in range(args.warmup):
+        e_graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        e_graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1) / args.steps
+    del graph, e_graph
+    if ops.device_error():
+        raise SystemExit("device error word set")
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        cpu = None
+        if not args.no_cpu_baseline and world == 1:
+            c = attention_cpu_reference(context, kv)
+            cpu = {kk: c[kk] for kk in ("value", "unit", "cores", "kind", "sample")}
+        line = {
+            "metric": f"{attention_describe(context, kv)} KV GB/s", "value": round(gbs * world, 2), "unit": "GB/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": ("fp16" if kv == "f16" else "Q4_0") + " cache, f64 scores / softmax / P.V",
+            "data": "synthetic (seeded N(0,1) K/V, N(0,30) QKV projection)",
+            "config": {"workload": attention_describe(context, kv), "context": context, "kv_cache": kv,
+                       "launches_per_step": 2 * copies, "us_per_call": round(us_call, 3),
+                       "kv_bytes_per_call": kv_bytes,
+                       "l2": f"{copies} cache copies ({copies * per_copy / 2**20:.0f} MiB) > 2x L2; no flush",
+                       "chain": "PDL-chained split + combine launches in one CUDA graph",
+                       "parallelism": "single GPU" if world == 1 else f"replicas x{world}"},
+            "e2e": {"value": round(kv_bytes / (e_ms * 1e-3) / 1e9 * world, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": qkv_host.nbytes, "d2h_bytes_per_step": hq * 128 * 4,
+                    "ms_per_step": round(e_ms, 6),
+                    "path": "ops.decode_attention_qkv[_q4_0] with pinned H2D of the QKV row and D2H of the output, "
+                            "graph-captured"},
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 5), "peak_source": peak_kind,
+                         "traffic": attention_profiled_traffic(context, kv),
+                         "kernel": "attn_split_kernel + attn_combine_kernel (timed together)",
+                         "us_per_launch": round(us_call, 3),
+                         "note": "issue-bound: fp64 arithmetic on converted cache values, not HBM"},
+            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies * 2,
+        }
+        print(json.dumps(line), flush=True)
+
+
 # ----------------------------------------------------------------------------- decode workload
 
 DECODE_TOKENS = 128
@@ -672,7 +931,7 @@ def decode_host_cache(cfg, kv: str, dev):
     return None, None, planes
 
 
-def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16"):
+def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16", context: int = 4096):
     """Time the oracle's decode step (oracle/decode.py over oracle/oracle.c, OpenMP over all
     host threads) on the 36-layer stack: whole tokens from the prefilled context."""
     import torch
@@ -680,7 +939,7 @@ def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16"):
     from mojo_llm_lab_b200 import decode as D
     from oracle import decode as OD
 
-    cfg = D.DecodeConfig()
+    cfg = D.DecodeConfig(context=context)
     # Data preparation only (torch's CPU generator takes ~30 s for 2.4 GB).
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     w = D.generate_weights(cfg, dev)
@@ -697,7 +956,7 @@ def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16"):
             break
     del torch
     return {"value": n / el, "unit": "tokens/s", "cores": threads, "kind": "port",
-            "sample": f"{n} greedy tokens of the 36-layer stack from context 4096 ({kv} KV) in {el:.1f} s "
+            "sample": f"{n} greedy tokens of the 36-layer stack from context {context} ({kv} KV) in {el:.1f} s "
                       f"(oracle/decode.py + oracle/oracle.c, OpenMP {threads} threads, float64)",
             "seconds_per_token": el / n}
 
@@ -705,12 +964,12 @@ def decode_cpu_reference(target_s: float = 15.0, kv: str = "f16"):
 def run_decode_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    ref = decode_cpu_reference(target_s=max(5.0, min(30.0, 2.0 * args.steps)), kv=args.kv)
+    ref = decode_cpu_reference(target_s=max(5.0, min(30.0, 2.0 * args.steps)), kv=args.kv, context=args.context)
     line = {"metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(ref["value"], 4),
             "unit": "tokens/s", "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ref["seconds_per_token"] * DECODE_TOKENS * 1e3, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded)",
-            "config": {"workload": "36-layer Qwen3-style decode, ctx 4096, 128 greedy tokens"
+            "config": {"workload": f"36-layer Qwen3-style decode, ctx {args.context}, 128 greedy tokens"
                                    + ("" if args.kv == "f16" else ", Q4_0 KV cache")},
             "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
             "e2e": {"value": round(ref["value"], 4), "unit": "tokens/s", "h2d_bytes_per_step": 0,
@@ -728,7 +987,7 @@ def run_decode(args, rank: int, world: int):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    cfg = D.DecodeConfig()
+    cfg = D.DecodeConfig(context=args.context)
     group = dist.group.WORLD if world > 1 else None
     weights = D.generate_weights(cfg, device, world=world, rank=rank)
     if args.kv == "q4_0":
@@ -841,7 +1100,8 @@ def run_decode(args, rank: int, world: int):
                       + cfg.kv_bytes_read(int(mean_keys), args.kv))
         us_per_token = ms * 1e3 / DECODE_TOKENS
         achieved = rank_bytes / (us_per_token * 1e-6) / 1e9
-        cpu = None if args.no_cpu_baseline or world > 1 else decode_cpu_reference(target_s=10.0, kv=args.kv)
+        cpu = None if args.no_cpu_baseline or world > 1 else decode_cpu_reference(target_s=10.0, kv=args.kv,
+                                                                                   context=args.context)
         line = {
             "metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
@@ -850,7 +1110,7 @@ def run_decode(args, rank: int, world: int):
                      + " KV, f64 attention",
             "data": "synthetic (seeded random weights, N(0,1) KV prefill)",
             "config": {"workload": "36-layer Qwen3-style decode (hidden 2560, 32/8 heads x 128, SwiGLU 9728, "
-                                   "vocab 151936), ctx 4096, 128 greedy tokens per step"
+                                   f"vocab 151936), ctx {args.context}, 128 greedy tokens per step"
                                    + ("" if args.kv == "f16" else ", Q4_0 KV cache"),
                        "kv_cache": args.kv,
                        "us_per_token": round(us_per_token, 3), "bytes_per_token_per_gpu": int(rank_bytes),
@@ -997,12 +1257,9 @@ def run_imrope(args, rank: int, world: int, batched: bool):
     torch.cuda.synchronize()
     serial_us = s0.elapsed_time(s1) / args.steps * 1e3 / copies
     del serial
-    t0 = time.perf_counter()
-    while time.perf_counter() - t0 < 0.3:  # load before the timed region (clock samples)
-        graph.replay()
-        torch.cuda.synchronize()
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
+        preroll(graph)  # load before the timed region (clock samples)
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
@@ -1086,9 +1343,11 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched", "prefill"],
+    ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched", "prefill",
+                                                               "attention"],
                     default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
+    ap.add_argument("--context", type=int, default=4096, help="decode: prefilled KV rows")
     ap.add_argument("--kv", choices=["f16", "q4_0"], default="f16",
                     help="decode: KV cache type (q4_0: GGML Q4_0, the reference's llama.cpp setting)")
     ap.add_argument("--copies", type=int, default=0)
@@ -1106,12 +1365,14 @@ def main():
             run_decode_reference(args, rank, world)
         elif args.workload == "prefill":
             run_prefill_reference(args, rank, world)
+        elif args.workload == "attention":
+            run_attention_reference(args, rank, world)
         elif args.workload.startswith("imrope"):
             run_imrope_reference(args, rank, world, batched=args.workload == "imrope_batched")
         else:
             run_reference(args, rank, world)
         return
-    runner = {"decode": run_decode, "prefill": run_prefill,
+    runner = {"decode": run_decode, "prefill": run_prefill, "attention": run_attention,
               "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
               "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True)}.get(args.workload, run_ours)
     if world > 1:

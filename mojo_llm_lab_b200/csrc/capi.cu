@@ -523,20 +523,66 @@ namespace {
 
 constexpr int64_t kAttnMaxSplits = 6144;  // combine weights: 48 KB of shared memory
 
-// Context chunks per KV head: enough CTAs to give every SM its resident
-// share, and chunks of at most the kernel's chunk size.
-int64_t attention_splits(int dev, int64_t q_heads, int64_t kv_heads, int64_t ctx) {
-  int per_sm = 1, max_chunk = 128;
-  switch (q_heads / kv_heads) {
-    case 1: per_sm = mllb::AttnConfig<1>::kCtasPerSm; max_chunk = mllb::AttnConfig<1>::kMaxChunk; break;
-    case 2: per_sm = mllb::AttnConfig<2>::kCtasPerSm; max_chunk = mllb::AttnConfig<2>::kMaxChunk; break;
-    case 4: per_sm = mllb::AttnConfig<4>::kCtasPerSm; max_chunk = mllb::AttnConfig<4>::kMaxChunk; break;
-    default: per_sm = mllb::AttnConfig<8>::kCtasPerSm; max_chunk = mllb::AttnConfig<8>::kMaxChunk; break;
-  }
-  int64_t base = static_cast<int64_t>(sm_count(dev)) * per_sm / kv_heads;
+// The long-context shape of the split kernel: LongShape<G>::kWarps warps
+// (at least G), chunks of MLLB_ATTN_LONG_CHUNK keys, as many resident CTAs
+// per SM as 128 registers a thread allow.  Only for 1 and 4 query heads per
+// KV head (2 and 8 need more than 128 registers a thread and keep the
+// default shape).  Build-time overridable for sweeps.
+#ifndef MLLB_ATTN_LONG_WARPS
+#define MLLB_ATTN_LONG_WARPS 8
+#endif
+#ifndef MLLB_ATTN_LONG_CHUNK
+#define MLLB_ATTN_LONG_CHUNK 128
+#endif
+#ifndef MLLB_ATTN_LONG_ALWAYS
+#define MLLB_ATTN_LONG_ALWAYS 0
+#endif
+
+template <int G>
+struct LongShape {
+  static constexpr int kWarps = G > MLLB_ATTN_LONG_WARPS ? G : MLLB_ATTN_LONG_WARPS;
+  static constexpr int kCtas = 512 / (kWarps * 32) > 0 ? 512 / (kWarps * 32) : 1;
+  template <int KV>
+  using Config = mllb::AttnConfig<G, KV, kWarps, MLLB_ATTN_LONG_CHUNK, kCtas>;
+};
+
+struct AttnPlan {
+  bool long_shape;
+  int64_t splits;
+};
+
+// Context chunks per KV head for one shape: enough CTAs to give every SM
+// its resident share, and chunks of at most the shape's chunk size.
+template <class C>
+int64_t shape_splits(int dev, int64_t kv_heads, int64_t ctx) {
+  int64_t base = static_cast<int64_t>(sm_count(dev)) * C::kCtasPerSm / kv_heads;
   if (base < 1) base = 1;
-  const int64_t need = (ctx + max_chunk - 1) / max_chunk;
+  const int64_t need = (ctx + C::kMaxChunk - 1) / C::kMaxChunk;
   return base > need ? base : need;
+}
+
+// The default shape (one CTA per SM, up to 256 keys) while its chunks fit in
+// one wave of CTAs; past that the long shape.
+template <int G>
+AttnPlan plan_for(int dev, int64_t kv_heads, int64_t ctx) {
+  using D = mllb::AttnConfig<G>;
+  const int64_t d = shape_splits<D>(dev, kv_heads, ctx);
+  if constexpr (G == 1 || G == 4) {
+    using L = typename LongShape<G>::template Config<mllb::kKvF16>;
+    const int64_t one_wave = static_cast<int64_t>(sm_count(dev)) * D::kCtasPerSm / kv_heads;
+    const int64_t l = shape_splits<L>(dev, kv_heads, ctx);
+    if ((MLLB_ATTN_LONG_ALWAYS || d > one_wave) && l <= kAttnMaxSplits) return {true, l};
+  }
+  return {false, d};
+}
+
+AttnPlan attention_plan(int dev, int64_t q_heads, int64_t kv_heads, int64_t ctx) {
+  switch (q_heads / kv_heads) {
+    case 1: return plan_for<1>(dev, kv_heads, ctx);
+    case 2: return plan_for<2>(dev, kv_heads, ctx);
+    case 4: return plan_for<4>(dev, kv_heads, ctx);
+    default: return plan_for<8>(dev, kv_heads, ctx);
+  }
 }
 
 int check_attention_shape(int64_t q_heads, int64_t kv_heads, int64_t ctx) {
@@ -563,17 +609,17 @@ struct AttentionArgs {
   uint8_t* v_cache;      // fp16 rows, or the Q4_0 V nibble plane
   uint8_t* kv_d;         // Q4_0 scale plane (nullptr for fp16)
   int kv;                // mllb::kKvF16 or mllb::kKvQ4_0
+  bool long_shape;       // AttnPlan::long_shape
   double* part_acc;
   double* part_ml;
   int64_t splits;
 };
 
-template <int G, int KV>
-int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
-  using C = mllb::AttnConfig<G, KV>;
+template <class C, int G, int KV, int W, int CH, int CTAS>
+int launch_shape(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
   int dev, rc, grid, per_sm;
   if ((rc = current_device(&dev))) return rc;
-  auto kernel = mllb::attn_split_kernel<G, KV>;
+  auto kernel = mllb::attn_split_kernel<G, KV, W, CH, CTAS>;
   if ((rc = stream_grid(kernel, C::kSmemBytes, C::kThreads, dev, 1, &grid, &per_sm))) return rc;
   return launched(launch(kernel, dim3(static_cast<unsigned>(a.splits), static_cast<unsigned>(a.kv_heads)),
                          dim3(C::kThreads), C::kSmemBytes, stream, pdl, a.q, a.qkv, a.q_gamma, a.k_gamma, a.theta,
@@ -581,6 +627,19 @@ int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
                          a.kv_d, a.part_acc, a.part_ml, static_cast<int>(a.ctx), static_cast<int>(a.splits),
                          1.0 / sqrt(128.0)),
                   "decode attention kernel");
+}
+
+template <int G, int KV>
+int launch_attention(const AttentionArgs& a, cudaStream_t stream, bool pdl) {
+  if constexpr (G == 1 || G == 4) {
+    if (a.long_shape) {
+      using S = LongShape<G>;
+      using C = typename S::template Config<KV>;
+      return launch_shape<C, G, KV, S::kWarps, MLLB_ATTN_LONG_CHUNK, S::kCtas>(a, stream, pdl);
+    }
+  }
+  using C = mllb::AttnConfig<G, KV>;
+  return launch_shape<C, G, KV, C::kWarps, C::kMaxChunk, C::kCtasPerSm>(a, stream, pdl);
 }
 
 // Split kernel + combine for both entry points.
@@ -599,7 +658,9 @@ int attention_impl(AttentionArgs a, double* scratch, int64_t scratch_doubles, fl
     return fail(MLLB_EALIGN, "q/qkv and caches need 16-byte, state/scratch 8-byte, others 4-byte alignment");
   int dev;
   if ((rc = current_device(&dev))) return rc;
-  a.splits = attention_splits(dev, a.q_heads, a.kv_heads, a.ctx);
+  const AttnPlan plan = attention_plan(dev, a.q_heads, a.kv_heads, a.ctx);
+  a.splits = plan.splits;
+  a.long_shape = plan.long_shape;
   const int64_t need = a.q_heads * a.splits * (128 + 2);
   if (scratch_doubles < need)
     return fail(MLLB_EINVAL, "scratch holds %lld doubles, %lld needed", static_cast<long long>(scratch_doubles),
@@ -745,7 +806,7 @@ int64_t mllb_decode_attention_scratch(int64_t q_heads, int64_t kv_heads, int64_t
   if (rc) return rc;
   int dev;
   if ((rc = current_device(&dev))) return rc;
-  return q_heads * attention_splits(dev, q_heads, kv_heads, ctx) * (128 + 2);
+  return q_heads * attention_plan(dev, q_heads, kv_heads, ctx).splits * (128 + 2);
 }
 
 int mllb_decode_attention(const float* q, const void* k_cache, const void* v_cache, const mllb_decode_state* state,

@@ -327,16 +327,20 @@ __device__ __forceinline__ double transpose_reduce32(double (&v)[32], int lane) 
 }
 
 // One CTA per (context chunk, KV head); G query heads share the KV head.
-// 16 warps where 128 registers a thread suffice (G = 4, the decode shape,
-// and G = 1), otherwise 8.  KV: kKvF16 (rows of 128 fp16) or kKvQ4_0 (the
-// three planes above; the scale rows travel with the K rows).
-template <int G, int KV = kKvF16>
+// Default shape: 16 warps where 128 registers a thread suffice (G = 4, the
+// decode shape, and G = 1), otherwise 8, one CTA per SM, chunks of up to 256
+// keys.  Long contexts (more chunks than one wave of SMs) take a smaller
+// shape with several CTAs per SM (WARPS warps, CHUNK keys), so that one CTA's
+// K/V copies and barriers overlap another's arithmetic.  KV: kKvF16 (rows of
+// 128 fp16) or kKvQ4_0 (the three planes above; the scale rows travel with
+// the K rows).
+template <int G, int KV = kKvF16, int WARPS = ((G == 4 || G == 1) ? 16 : 8), int CHUNK = 256, int CTAS = 1>
 struct AttnConfig {
-  static constexpr int kWarps = (G == 4 || G == 1) ? 16 : 8;
+  static constexpr int kWarps = WARPS;
   static constexpr int kThreads = kWarps * 32;
-  static constexpr int kCtasPerSm = 1;
-  static constexpr int kMaxChunk = 256;                   // keys per CTA
-  static constexpr int kSub = 64;                         // keys per staged sub-chunk
+  static constexpr int kCtasPerSm = CTAS;                 // resident CTAs per SM the launch bounds ask for
+  static constexpr int kMaxChunk = CHUNK;                 // keys per CTA
+  static constexpr int kSub = CHUNK < 64 ? CHUNK : 64;    // keys per staged sub-chunk
   static constexpr int kNumSub = kMaxChunk / kSub;
   static constexpr int kRowBytes = KV == kKvQ4_0 ? kQ4_0RowBytes : kHeadDim * 2;  // one K or V row
   static constexpr int kDRowBytes = KV == kKvQ4_0 ? kQ4_0DRowBytes : 0;
@@ -354,8 +358,10 @@ struct AttnConfig {
   static constexpr int kBarOffset = kRedOffset + 2 * kWarps * 8;            // 2 x kNumSub mbarriers
   static constexpr int kSmemBytes = kBarOffset + 2 * kNumSub * 8;
   static_assert(32 % G == 0 && G <= kWarps && kWarps % G == 0, "query heads per KV head");
-  static_assert(kSub % kKeysPerPass == 0, "score passes stay inside one sub-chunk");
+  static_assert(kSub % kKeysPerPass == 0 && kMaxChunk % kSub == 0, "score passes stay inside one sub-chunk");
+  static_assert(kMaxChunk % 16 == 0, "chunks are multiples of 16 keys");
   static_assert(KV == kKvF16 || KV == kKvQ4_0, "KV cache type");
+  static_assert(kSmemBytes * kCtasPerSm <= 227 * 1024, "resident CTAs fit in shared memory");
 };
 
 // 2^52 + n as a double (exact for 0 <= n < 2^32), minus 2^52 + 8: the
@@ -384,14 +390,15 @@ __device__ __forceinline__ double q4_0_value(uint32_t n) {
 // Q4_0 (KV == kKvQ4_0): k_cache / v_cache are the nibble planes and kv_d the
 // scale plane; cache values d * (q - 8) enter fp64 exactly (d through
 // half_bits_scaled, q - 8 through q4_0_value).
-template <int G, int KV>
-__global__ void __launch_bounds__(AttnConfig<G, KV>::kThreads, AttnConfig<G, KV>::kCtasPerSm)
+template <int G, int KV, int WARPS, int CHUNK, int CTAS>
+__global__ void __launch_bounds__(AttnConfig<G, KV, WARPS, CHUNK, CTAS>::kThreads,
+                                  AttnConfig<G, KV, WARPS, CHUNK, CTAS>::kCtasPerSm)
     attn_split_kernel(const float* __restrict__ q, const float* __restrict__ qkv, const float* __restrict__ q_gamma,
                       const float* __restrict__ k_gamma, double theta, int hq, int hkv,
                       const DecodeState* __restrict__ state, uint8_t* __restrict__ k_cache,
                       uint8_t* __restrict__ v_cache, uint8_t* __restrict__ kv_d, double* __restrict__ part_acc,
                       double* __restrict__ part_ml, int ctx, int splits, double scale) {
-  using C = AttnConfig<G, KV>;
+  using C = AttnConfig<G, KV, WARPS, CHUNK, CTAS>;
   constexpr int W = C::kWarps, KB = C::kKeysPerPass, WG = C::kWarpsPerHead;
   constexpr bool kQ4 = KV == kKvQ4_0;
   extern __shared__ __align__(128) uint8_t smem[];

@@ -162,7 +162,9 @@ def random_cache(hkv, ctx, seed, scale=1.0):
 @pytest.mark.parametrize("hq,hkv,ctx,pos", [
     (32, 8, 4224, 4096), (32, 8, 4224, 4223), (32, 8, 4224, 0), (32, 8, 4224, 15), (32, 8, 4224, 16),
     (32, 8, 4224, 287), (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 2047), (4, 4, 5000, 4999),
-    (16, 2, 64, 63)])
+    (16, 2, 64, 63),
+    # past one wave of the default shape: the long-context shape
+    (32, 8, 8192, 8000), (32, 8, 33000, 32999), (8, 8, 20000, 19999), (16, 4, 12000, 11999)])
 def test_attention_against_oracle(orc, hq, hkv, ctx, pos):
     k, v = random_cache(hkv, ctx, seed=ctx + pos)
     rng = np.random.default_rng(pos)
@@ -180,7 +182,8 @@ def test_attention_against_oracle(orc, hq, hkv, ctx, pos):
 
 @pytest.mark.parametrize("hq,hkv,ctx,pos", [
     (32, 8, 4224, 4096), (32, 8, 4224, 0), (32, 8, 4224, 63), (32, 8, 4224, 64), (32, 8, 4224, 4223),
-    (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 1000), (4, 4, 5000, 4999), (16, 2, 64, 63)])
+    (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 1000), (4, 4, 5000, 4999), (16, 2, 64, 63),
+    (32, 8, 8192, 8191), (32, 8, 33000, 20000), (32, 8, 33000, 64)])
 def test_fused_rope_append_attention(orc, hq, hkv, ctx, pos):
     """decode_attention_qkv == qk_rope_append + attention, cache rows included."""
     k, v = random_cache(hkv, ctx, seed=ctx * 3 + pos)

@@ -88,7 +88,9 @@ def test_store_rejects_bad_rows():
 @pytest.mark.parametrize("hq,hkv,ctx,pos", [
     (32, 8, 4224, 4096), (32, 8, 4224, 4223), (32, 8, 4224, 0), (32, 8, 4224, 15), (32, 8, 4224, 16),
     (32, 8, 4224, 287), (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 2047), (4, 4, 5000, 4999),
-    (16, 2, 64, 63)])
+    (16, 2, 64, 63),
+    # past one wave of the default shape: the long-context shape
+    (32, 8, 8192, 8000), (32, 8, 33000, 32999), (8, 8, 20000, 19999), (16, 4, 12000, 11999)])
 def test_attention_q4_0_against_oracle(orc, hq, hkv, ctx, pos):
     k, v = random_rows(hkv, ctx, seed=ctx + pos)
     kq, vq, d = host_planes(orc, k, v)
@@ -105,7 +107,8 @@ def test_attention_q4_0_against_oracle(orc, hq, hkv, ctx, pos):
 
 @pytest.mark.parametrize("hq,hkv,ctx,pos", [
     (32, 8, 4224, 4096), (32, 8, 4224, 0), (32, 8, 4224, 63), (32, 8, 4224, 64), (32, 8, 4224, 4223),
-    (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 1000), (4, 4, 5000, 4999), (16, 2, 64, 63)])
+    (8, 8, 300, 299), (8, 4, 1000, 517), (64, 8, 2048, 1000), (4, 4, 5000, 4999), (16, 2, 64, 63),
+    (32, 8, 8192, 8191), (32, 8, 33000, 20000), (32, 8, 33000, 64)])
 def test_fused_append_attention_q4_0(orc, hq, hkv, ctx, pos):
     """decode_attention_qkv_q4_0 == rope + Q4_0 append + attention_q4_0, cache planes included."""
     k, v = random_rows(hkv, ctx, seed=ctx * 3 + pos)
