@@ -65,9 +65,10 @@ const char *mllb_last_error(void);
  * its TMA pipeline (see csrc/common.cuh); bit 3 = decode next-token key out
  * of range; bit 4 = decode position outside the KV cache; bit 5 = decode
  * attention gave up waiting for its K/V copies; bit 6 = a peer all-gather
- * gave up waiting for another rank.  Copies the word of the
- * current device to *bits (synchronising), optionally clearing it.  0 in
- * normal runs.
+ * gave up waiting for another rank; bit 7 = a grid-wide epilogue
+ * (mllb_q4k_matvec_norm) gave up waiting for the other CTAs of its grid.
+ * Copies the word of the current device to *bits (synchronising),
+ * optionally clearing it.  0 in normal runs.
  */
 int mllb_device_error(uint32_t *bits, int clear);
 
@@ -249,6 +250,28 @@ int mllb_q6k_matvec_act(const void *weights, const mllb_act_f32 *act, float *out
 int64_t mllb_q4k_matmul_tokens_workspace(int64_t rows, int64_t k, int64_t tokens);
 int mllb_q4k_matmul_tokens(const void *weights, const void *q8, float *out, int64_t rows, int64_t k, int64_t tokens,
                            void *workspace, int64_t workspace_bytes, unsigned flags, void *stream);
+
+/*
+ * Q4_K matvec whose output is the delta of a residual stream, with the next
+ * RMSNorm + Q8_1 built in (no separate mllb_rmsnorm_q8_1 launch):
+ *   out[r] = sum_k W[r,k] a[k]             (fp32; out may be NULL)
+ *   h[r]   = x[r] + fp32(out[r])  -> x_out  (fp32; x_out may equal x)
+ *   q8_out = Q8_1(fp32(h * r * gamma)), r = 1 / sqrt(sum(h^2) / n + eps)  (fp64)
+ * i.e. mllb_q4k_matvec_ex followed by mllb_rmsnorm_q8_1(x, out, x_out, gamma,
+ * eps, q8_out, n, MLLB_Q8_1_S_D_SUMQ).  n % 32 == 0; K/256 in {8, 10, 16, 38}
+ * (others MLLB_EUNSUPPORTED).  workspace: at least
+ * mllb_q4k_matvec_norm_workspace(n, k) bytes, 16-byte aligned, its first 16
+ * bytes zero before the first call (every call leaves them zero); calls
+ * sharing a workspace must not overlap on the GPU.  The CTAs of the launch
+ * meet once (a bounded wait: device error bit 7 if the grid never gathers).
+ * The O projection and the FFN's down projection of the reference's decode
+ * graph, each followed by GGML's add + rms_norm + mul + quantize_q8_1 nodes
+ * (docs/decode-profile.md:5-11).
+ */
+int64_t mllb_q4k_matvec_norm_workspace(int64_t n, int64_t k);
+int mllb_q4k_matvec_norm(const void *weights, const void *q8, float *out, int64_t n, int64_t k, const float *x,
+                         float *x_out, const float *gamma, double eps, void *q8_out, void *workspace,
+                         int64_t workspace_bytes, unsigned flags, void *stream);
 
 /*
  * mllb_q4k_gate_up_q8: mllb_q4k_gate_up_ex that also writes the Q8_1 of prod

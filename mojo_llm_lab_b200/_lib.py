@@ -88,6 +88,8 @@ SIGNATURES = {
     "mllb_q4k_gate_up_act": (C.c_int, [_P, _P, _ACT, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q6k_matvec_act": (C.c_int, [_P, _ACT, _P, _I64, _I64, C.c_uint, _P]),
     "mllb_q4k_gate_up_q8": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _P, _I64, _I64, C.c_uint, _P]),
+    "mllb_q4k_matvec_norm_workspace": (_I64, [_I64, _I64]),
+    "mllb_q4k_matvec_norm": (C.c_int, [_P, _P, _P, _I64, _I64, _P, _P, _P, C.c_double, _P, _P, _I64, C.c_uint, _P]),
     "mllb_q4k_matmul_tokens_workspace": (C.c_int64, [_I64, _I64, _I64]),
     "mllb_q4k_matmul_tokens": (C.c_int, [_P, _P, _P, _I64, _I64, _I64, _P, _I64, C.c_uint, _P]),
 }

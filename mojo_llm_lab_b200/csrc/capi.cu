@@ -285,6 +285,31 @@ int q4k_gate_up_q8_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8,
   return fail(MLLB_EUNSUPPORTED, "no gate/up configuration for K=%lld", static_cast<long long>(k));
 }
 
+// Q4_K streaming launch with the residual + RMSNorm + Q8_1 epilogue
+// (kEpiResidualNorm; Q8_1 activation).
+int q4k_norm_team(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int64_t k, cudaStream_t stream,
+                  bool pdl, const mllb::Epilogue& epi) {
+  using F = mllb::Q4kFormat;
+  constexpr int E = mllb::kEpiResidualNorm;
+  const mllb::ActSource src = q8_source(q8);
+  const int rows = static_cast<int>(n);
+  switch (k / 256) {
+    case 8: return launch_team_kernel<F, 8, 1, MLLB_CFG_Q4K_8, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
+    case 10: {
+      using Small = mllb::TeamConfig<F, 10, 1, MLLB_CFG_Q4K_10_SMALL>;
+      int dev, rc;
+      if ((rc = current_device(&dev))) return rc;
+      if ((rows + Small::kT - 1) / Small::kT <= 2 * sm_count(dev))
+        return launch_team_kernel<F, 10, 1, MLLB_CFG_Q4K_10_SMALL, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
+      return launch_team_kernel<F, 10, 1, MLLB_CFG_Q4K_10, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
+    }
+    case 16: return launch_team_kernel<F, 16, 1, MLLB_CFG_Q4K_16, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
+    case 38: return launch_team_kernel<F, 38, 1, MLLB_CFG_Q4K_38, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
+    default: break;
+  }
+  return fail(MLLB_EUNSUPPORTED, "no streaming configuration for K=%lld", static_cast<long long>(k));
+}
+
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
                  int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
   const int rc = q4k_team(w0, w1, q8_source(q8), o0, o1, o2, n, k, stream, pdl);
@@ -987,6 +1012,48 @@ int mllb_q4k_gate_up_q8(const void* up_weights, const void* gate_weights, const 
   return q4k_gate_up_q8_team(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
                              static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
                              flags & MLLB_LAUNCH_PDL, epi);
+}
+
+int64_t mllb_q4k_matvec_norm_workspace(int64_t n, int64_t k) {
+  const int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  return 16 + 8 * ((n + 3) / 4);  // two counters (padded) + one double per CTA (at most one per 4-row tile)
+}
+
+int mllb_q4k_matvec_norm(const void* weights, const void* q8, float* out, int64_t n, int64_t k, const float* x,
+                         float* x_out, const float* gamma, double eps, void* q8_out, void* workspace,
+                         int64_t workspace_bytes, unsigned flags, void* stream) {
+  if (!weights || !q8 || !x || !x_out || !gamma || !q8_out || !workspace) return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (n % 32) return fail(MLLB_EINVAL, "the norm's Q8_1 needs a multiple of 32 rows");
+  if (!(eps >= 0.0)) return fail(MLLB_EINVAL, "eps must be >= 0");
+  if (!aligned(weights, 16) || !aligned(q8, 4) || !aligned(out, 4) || !aligned(x, 4) || !aligned(x_out, 4) ||
+      !aligned(gamma, 4) || !aligned(q8_out, 4) || !aligned(workspace, 16))
+    return fail(MLLB_EALIGN, "weights and workspace need 16-byte, the rest 4-byte alignment");
+  const int64_t need = mllb_q4k_matvec_norm_workspace(n, k);
+  if (workspace_bytes < need)
+    return fail(MLLB_EINVAL, "workspace holds %lld bytes, %lld needed", static_cast<long long>(workspace_bytes),
+                static_cast<long long>(need));
+  const auto overlaps = [](const void* p, int64_t pb, const void* q, int64_t qb) {
+    const char* a = static_cast<const char*>(p);
+    const char* b = static_cast<const char*>(q);
+    return a && b && a < b + qb && b < a + pb;
+  };
+  if ((x_out != x && overlaps(x_out, n * 4, x, n * 4)) || overlaps(x_out, n * 4, gamma, n * 4) ||
+      overlaps(out, n * 4, x, n * 4) || overlaps(out, n * 4, x_out, n * 4))
+    return fail(MLLB_EINVAL, "x_out may equal x but must not otherwise overlap x, gamma or out");
+  mllb::Epilogue epi = {};
+  epi.counters = static_cast<uint32_t*>(workspace);
+  epi.q8_out = static_cast<uint8_t*>(q8_out);
+  epi.x = x;
+  epi.x_out = x_out;
+  epi.gamma = gamma;
+  epi.partials = reinterpret_cast<double*>(static_cast<uint8_t*>(workspace) + 16);
+  epi.eps = eps;
+  return q4k_norm_team(static_cast<const uint8_t*>(weights), static_cast<const uint8_t*>(q8), out, n, k,
+                       static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, epi);
 }
 
 // ---------------------------------------------------------------- prefill

@@ -25,6 +25,7 @@ enum : uint32_t {
   kErrKvOverflow = 1u << 4,        // decode: position at or past the KV capacity (nothing written)
   kErrKvWaitTimeout = 1u << 5,     // decode attention gave up waiting for its K/V copies
   kErrPeerWaitTimeout = 1u << 6,   // peer all-gather gave up waiting for another rank's slice
+  kErrGridWaitTimeout = 1u << 7,   // a grid-wide epilogue gave up waiting for the grid's other CTAs
 };
 
 // Device-resident state of a decode loop; mirrors mllb_decode_state of the
@@ -170,6 +171,41 @@ __device__ __forceinline__ float ld_cg_f32(const float* p) {
   asm volatile("ld.global.cg.f32 %0, [%1];" : "=f"(v) : "l"(p));
   return v;
 }
+__device__ __forceinline__ double ld_cg_f64(const double* p) {
+  double v;
+  asm volatile("ld.global.cg.f64 %0, [%1];" : "=d"(v) : "l"(p));
+  return v;
+}
+
+// Arrival on a grid-wide counter: everything this thread wrote before (and,
+// through a preceding CTA barrier and fence, what its CTA wrote) is visible
+// to a thread that acquires the new value.
+__device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.add.release.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
+  return v;
+}
+
+// Wait until *count reaches target (the other CTAs of this grid arriving).
+// Only for grids whose CTAs are all resident at once.  Returns false (after
+// ~1 s) if it never does; the caller records the error.
+__device__ __forceinline__ bool wait_count_bounded(const uint32_t* count, uint32_t target) {
+  if (ld_acquire_gpu_u32(count) >= target) return true;
+  const uint64_t start = global_timer_ns();
+  for (uint32_t i = 0; i < kWaitMaxIters; ++i) {
+    if (ld_acquire_gpu_u32(count) >= target) return true;
+    if (i >= 1024) __nanosleep(64);  // spin first: the grid usually gathers within microseconds
+    if ((i & 63u) == 63u && global_timer_ns() - start > kWaitLimitNs) break;
+  }
+  return false;
+}
+
 __device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
 
 // Streaming 16-byte global load that does not allocate in L1.

@@ -66,13 +66,29 @@ struct ActSource {
 //    g; after its last tile each CTA arrives once per tile, and the CTA whose
 //    arrival completes a group quantises it (as q8_1_quantize: s = d * sum q)
 //    into q8_out and zeroes the counter.
+//  * kEpiResidualNorm (a single matrix whose n_rows outputs are the delta
+//    of a residual stream): h = x + out0 (fp32) -> x_out, then the Q8_1 of
+//    y = fp32(h * r * gamma), r = 1 / sqrt(sum(h^2) / n_rows + eps) (fp64),
+//    into q8_out -- the residual + RMSNorm + quantiser that otherwise runs
+//    as a separate launch.  Each CTA sums the squares of its rows (per team,
+//    in tile order), stores the sum to partials[blockIdx.x] and arrives on
+//    counters[0]; once all gridDim.x CTAs have arrived (every CTA of these
+//    grids is resident at once: one per SM at most), each sums the partials
+//    in index order -- the same r in every CTA, run after run -- and
+//    quantises the 32-row groups g = blockIdx.x, blockIdx.x + gridDim.x, ...
+//    On leaving, the last CTA to depart (counters[1]) zeroes both counters.
 // Counters must be zero before the first launch; every launch leaves them
 // zero.  Launches that share counters must not overlap on the GPU.
 struct Epilogue {
   uint32_t* counters;
   uint8_t* q8_out;
+  const float* x;      // kEpiResidualNorm: residual stream in
+  float* x_out;        //   h = x + out0 (may alias x)
+  const float* gamma;  //   RMSNorm weights [n_rows]
+  double* partials;    //   one per CTA of the grid
+  double eps;
 };
-enum : int { kEpiNone = 0, kEpiQuantProduct = 1 };
+enum : int { kEpiNone = 0, kEpiQuantProduct = 1, kEpiResidualNorm = 2 };
 
 // ============================================================== formats
 
@@ -419,6 +435,7 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
                        int pdl, const Epilogue epi) {
   using C = TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
   static_assert(EPI != kEpiQuantProduct || (MATS == 2 && 32 % C::kT == 0), "product groups of whole tiles");
+  static_assert(EPI != kEpiResidualNorm || MATS == 1, "the residual norm follows a single matrix");
   constexpr int W = C::kW, RG = C::kRG, T = C::kT, P = C::kP, ROWB = C::kRowBytes;
   constexpr int kFirstBatch = TEAMS > 2 ? TEAMS : 2;
   constexpr int DECB = Fmt::kDecBytes;
@@ -446,9 +463,11 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     *abort_flag = 0;
     fence_mbar_init();
   }
+  __shared__ double s_norm_ss[EPI == kEpiResidualNorm ? TEAMS : 1];  // kEpiResidualNorm: each team's sum of h^2
   {
     double* partials = reinterpret_cast<double*>(smem + C::kPartOffset);
     for (int i = threadIdx.x; i < TEAMS * C::kTeamPartials; i += blockDim.x) partials[i] = 0.0;
+    if (EPI == kEpiResidualNorm && threadIdx.x < TEAMS) s_norm_ss[threadIdx.x] = 0.0;
   }
   __syncthreads();
   MLLB_TRACE_POINT(0);
@@ -598,26 +617,83 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     }
     named_barrier(team_barrier, W * 32);
     if (*abort_flag) break;
-    if (twarp == 0 && lane < T) {
-      const int row = tile * T + lane;
-      double tot[MATS];
+    if (twarp == 0) {
+      double sq = 0.0;  // kEpiResidualNorm: h^2 of this lane's row
+      if (lane < T) {
+        const int row = tile * T + lane;
+        double tot[MATS];
 #pragma unroll
-      for (int m = 0; m < MATS; ++m) {
-        double acc = 0.0;
+        for (int m = 0; m < MATS; ++m) {
+          double acc = 0.0;
 #pragma unroll
-        for (int g = 0; g < C::kSegs; ++g) acc += part[(m * T + lane) * C::kSegs + g];
-        tot[m] = acc;
-      }
-      if (row < n_rows) {
-        if (out0) out0[row] = static_cast<float>(tot[0]);
-        if (MATS == 2) {
-          if (out1) out1[row] = static_cast<float>(tot[MATS - 1]);
-          if (out2) out2[row] = static_cast<float>(tot[0] * (tot[MATS - 1] / (1.0 + exp(-tot[MATS - 1]))));
+          for (int g = 0; g < C::kSegs; ++g) acc += part[(m * T + lane) * C::kSegs + g];
+          tot[m] = acc;
         }
+        if (row < n_rows) {
+          if (out0) out0[row] = static_cast<float>(tot[0]);
+          if (MATS == 2) {
+            if (out1) out1[row] = static_cast<float>(tot[MATS - 1]);
+            if (out2) out2[row] = static_cast<float>(tot[0] * (tot[MATS - 1] / (1.0 + exp(-tot[MATS - 1]))));
+          }
+          if constexpr (EPI == kEpiResidualNorm) {
+            const float h = epi.x[row] + static_cast<float>(tot[0]);
+            epi.x_out[row] = h;
+            sq = static_cast<double>(h) * static_cast<double>(h);
+          }
+        }
+      }
+      if constexpr (EPI == kEpiResidualNorm) {
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, off);
+        if (lane == 0) s_norm_ss[team] += sq;
       }
     }
   }
   MLLB_TRACE_POINT(7);
+  if constexpr (EPI == kEpiResidualNorm) {
+    __shared__ int s_all_arrived;
+    const int tid = threadIdx.x;
+    const int g0 = blockIdx.x;  // this CTA's first 32-row group
+    const bool has_group = g0 < n_rows / 32;
+    const float gamma0 = (tid < 32 && has_group) ? epi.gamma[g0 * 32 + lane] : 0.0f;
+    __threadfence();  // this CTA's x_out rows before its arrival
+    named_barrier(1, C::kConsumers);
+    if (tid == 0) {
+      double cta = 0.0;
+#pragma unroll
+      for (int t = 0; t < TEAMS; ++t) cta += s_norm_ss[t];
+      epi.partials[blockIdx.x] = cta;
+      __threadfence();
+      atom_add_release_gpu(&epi.counters[0], 1u);
+      const bool ok = wait_count_bounded(&epi.counters[0], gridDim.x);
+      if (!ok) record_error(kErrGridWaitTimeout);
+      s_all_arrived = ok;
+    }
+    named_barrier(1, C::kConsumers);
+    if (s_all_arrived && tid < 32) {
+      // The first group's h is loaded with the partials: one L2 round trip.
+      const float h0 = has_group ? ld_cg_f32(epi.x_out + g0 * 32 + lane) : 0.0f;
+      double ss = 0.0;
+      for (int i = lane; i < static_cast<int>(gridDim.x); i += 32) ss += ld_cg_f64(epi.partials + i);
+#pragma unroll
+      for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      const double r = 1.0 / sqrt(ss / static_cast<double>(n_rows) + epi.eps);
+      for (int g = g0; g < n_rows / 32; g += gridDim.x) {
+        const int i = g * 32 + lane;
+        const float h = g == g0 ? h0 : ld_cg_f32(epi.x_out + i);
+        const float gm = g == g0 ? gamma0 : epi.gamma[i];
+        const float y = static_cast<float>(static_cast<double>(h) * r * static_cast<double>(gm));
+        uint32_t d16, s16;
+        const int q = q8_1_quantize_lane(y, kQ8SumDTimesSumQ, &d16, &s16);
+        q8_1_store_block(epi.q8_out + static_cast<size_t>(g) * kQ8BlockBytes, q, d16, s16, lane);
+      }
+    }
+    // Every CTA has passed the wait once the last one departs: it resets both.
+    if (tid == 0 && atomicAdd(&epi.counters[1], 1u) == gridDim.x - 1) {
+      epi.counters[0] = 0u;
+      epi.counters[1] = 0u;
+    }
+  }
   if constexpr (EPI == kEpiQuantProduct) {
     // One arrival per stored tile, then the groups this CTA completed.
     __shared__ uint32_t s_done[32];

@@ -337,7 +337,8 @@ class Decoder:
     """
 
     def __init__(self, weights: DecodeWeights, k_cache, v_cache: torch.Tensor | None = None, *, pdl: bool = True,
-                 fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False, quant_tail: bool = True):
+                 fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False, quant_tail: bool = True,
+                 norm_tail: bool = False):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
@@ -400,6 +401,24 @@ class Decoder:
                            and ffn_local % 32 == 0)
         if self.quant_tail:
             self.b.extra["prod_counters"] = torch.zeros(ffn_local // 32, dtype=torch.int32, device=dev)
+        # norm_tail: the O and down projections (hidden rows each) also do the
+        # residual add + RMSNorm + Q8_1 that follows them (mllb_q4k_matvec_norm)
+        # where a streaming configuration exists for their K: two launches
+        # fewer per layer, but the grid-wide meeting in that epilogue costs
+        # more than the separate 10-CTA norm launch, which the PDL chain
+        # largely hides (36-layer A/B: 1779 vs 1680 us/token), so it is off by
+        # default.  The first layer's norm and the final norm (which advances
+        # the state) stay separate launches either way.
+        team_k = (8, 10, 16, 38)
+        self.norm_tail_o = norm_tail and not self.fused and cfg.attn_width // 256 in team_k
+        self.norm_tail_down = norm_tail and not self.fused and cfg.ffn // 256 in team_k
+        for name, on, k in (("norm_ws_o", self.norm_tail_o, cfg.attn_width),
+                            ("norm_ws_down", self.norm_tail_down, cfg.ffn)):
+            if on:
+                need = int(lib().mllb_q4k_matvec_norm_workspace(cfg.hidden, k))
+                if need < 0:
+                    raise ValueError(f"norm epilogue rejected: {lib().mllb_last_error().decode()}")
+                self.b.extra[name] = torch.zeros(need, dtype=torch.uint8, device=dev)
         self.graph = None
 
     # -- state ------------------------------------------------------------
@@ -517,16 +536,29 @@ class Decoder:
             if out is not None:
                 cur = 1 - cur
 
+        def matvec_norm(weights, q8_in, k, gamma, ws, what):
+            # h[cur] + W a -> h[1 - cur]; the Q8_1 of its norm -> q8_hidden.
+            nonlocal cur
+            check(L.mllb_q4k_matvec_norm(P(weights), q8_in, None, cfg.hidden, k, h[cur], h[1 - cur], P(gamma),
+                                         cfg.eps, P(b.q8_hidden), P(ws), ws.numel(), fl, s), what)
+            cur = 1 - cur
+
         ffn_local = w.ffn_shard.local_rows
         self._prefetch_layer(0)
+        norm_pending = True  # this layer's attention norm still needs its own launch
         for layer, lw in enumerate(w.layers):
             self._prefetch_layer(layer + 1)
-            norm(None if layer == 0 else P(b.down_out), lw.attn_norm, "attn_norm")
+            if norm_pending:
+                norm(None if layer == 0 else P(b.down_out), lw.attn_norm, "attn_norm")
             check(L.mllb_q4k_matvec_ex(P(lw.qkv), P(b.q8_hidden), P(b.qkv), cfg.qkv_rows, cfg.hidden, fl, s),
                   "qkv")
             self._attention(layer, lw, state, fl, s)
-            check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s), "o")
-            norm(P(b.o_out), lw.ffn_norm, "ffn_norm")
+            if self.norm_tail_o:
+                matvec_norm(lw.o, P(b.q8_attn), cfg.attn_width, lw.ffn_norm, b.extra["norm_ws_o"], "o + ffn_norm")
+            else:
+                check(L.mllb_q4k_matvec_ex(P(lw.o), P(b.q8_attn), P(b.o_out), cfg.hidden, cfg.attn_width, fl, s),
+                      "o")
+                norm(P(b.o_out), lw.ffn_norm, "ffn_norm")
             if self.quant_tail:
                 check(L.mllb_q4k_gate_up_q8(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod),
                                             P(b.q8_prod), P(b.extra["prod_counters"]), ffn_local, cfg.hidden, fl, s),
@@ -540,7 +572,13 @@ class Decoder:
                     q8_prod = P(b.q8_prod)
                 else:
                     q8_prod = self._gather_prod(s, fl, layer)
-            check(L.mllb_q4k_matvec_ex(P(lw.down), q8_prod, P(b.down_out), cfg.hidden, cfg.ffn, fl, s), "down")
+            if self.norm_tail_down and layer + 1 < cfg.layers:
+                matvec_norm(lw.down, q8_prod, cfg.ffn, w.layers[layer + 1].attn_norm, b.extra["norm_ws_down"],
+                            "down + attn_norm")
+                norm_pending = False
+            else:
+                check(L.mllb_q4k_matvec_ex(P(lw.down), q8_prod, P(b.down_out), cfg.hidden, cfg.ffn, fl, s), "down")
+                norm_pending = True
         check(L.mllb_decode_final_norm(h[cur], P(b.down_out), h[1 - cur], P(w.out_norm), cfg.eps,
                                        P(b.q8_hidden), cfg.hidden, state, fl, s), "final_norm")
         check(L.mllb_q6k_matvec_ex(P(w.output), P(b.q8_hidden), P(b.logits), w.vocab_shard.local_rows, cfg.hidden,
@@ -556,9 +594,12 @@ class Decoder:
         # embedding; per layer (fused) QKV, attention split + combine, O,
         # gate/up, down or (unfused) those plus two norms and the quantiser;
         # final norm (unfused) and logits; argmax.
+        L = self.cfg.layers
         if self.fused:
-            return 1 + self.cfg.layers * 6 + 1 + 1
-        return 1 + self.cfg.layers * (8 if self.quant_tail else 9) + 2 + 1
+            return 1 + L * 6 + 1 + 1
+        per_layer = 6 if self.quant_tail else 7           # QKV, attention x 2, O, gate/up (+ quantiser), down
+        norms = (0 if self.norm_tail_o else L) + (1 if self.norm_tail_down else L)
+        return 1 + L * per_layer + norms + 1 + 1 + 1       # embed, ..., final norm, logits, argmax
 
     # -- sharded pieces -----------------------------------------------------
     def _setup_peer_gather(self):

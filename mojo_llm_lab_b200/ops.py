@@ -30,7 +30,8 @@ __all__ = [
     "fused_q_imrope_runtime_fastpow", "rmsnorm_imrope_q", "q4k_subdots", "stream_read", "device_error",
     "rmsnorm_q8_1", "decode_embed", "decode_final_norm", "decode_qk_rope_append", "decode_attention",
     "decode_attention_qkv", "kv_q4_0_store", "decode_attention_q4_0", "decode_attention_qkv_q4_0",
-    "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32", "q5_k_q8_1_matvec",
+    "q4k_matvec_act", "q4k_gate_up_act", "q6k_matvec_act", "act_f32", "q5_k_q8_1_matvec", "q4k_matvec_norm",
+    "q4k_matvec_norm_workspace",
     "argmax_key", "token_key", "key_token", "S_D_SUMQ", "S_SUM_X",
 ]
 
@@ -588,6 +589,50 @@ def q4k_gate_up_q8(up_weights: torch.Tensor, gate_weights: torch.Tensor, activat
                                     _ptr(up), _ptr(gate), prod.data_ptr(), q8_out.data_ptr(), counters.data_ptr(),
                                     rows, k, _flags(pdl), _stream(up_weights)), "q4k_gate_up_q8")
     return q8_out
+
+
+def q4k_matvec_norm_workspace(rows: int, k: int, device) -> torch.Tensor:
+    """Zeroed workspace for q4k_matvec_norm (reusable by calls that do not overlap on the GPU)."""
+    need = int(lib().mllb_q4k_matvec_norm_workspace(rows, k))
+    if need < 0:
+        check(need, "q4k_matvec_norm_workspace")
+    return torch.zeros(need, dtype=torch.uint8, device=device)
+
+
+def q4k_matvec_norm(weights: torch.Tensor, activations: torch.Tensor, x: torch.Tensor, gamma: torch.Tensor,
+                    eps: float = 1e-6, x_out: torch.Tensor | None = None, q8_out: torch.Tensor | None = None,
+                    out: torch.Tensor | None = None, workspace: torch.Tensor | None = None, pdl: bool = False):
+    """Q4_K matvec whose output is a residual delta, with the next RMSNorm + Q8_1 built in:
+    h = x + W a -> x_out, q8_out = Q8_1(rmsnorm(h) * gamma).  Returns (x_out, q8_out, out)."""
+    _need(weights, "weights", torch.uint8)
+    _need(activations, "activations", torch.uint8)
+    k = _k_from_q8(activations)
+    rows = _rows(weights, F.q4k_row_bytes(k), "Q4_K")
+    _need(x, "x", torch.float32)
+    _need(gamma, "gamma", torch.float32)
+    if x.numel() != rows or gamma.numel() != rows:
+        raise ValueError("x and gamma need one value per row")
+    if x_out is None:
+        x_out = torch.empty_like(x)
+    if q8_out is None:
+        q8_out = torch.empty(F.q8_1_bytes(rows), dtype=torch.uint8, device=x.device)
+    if workspace is None:
+        workspace = q4k_matvec_norm_workspace(rows, k, x.device)
+    for name, t in (("x_out", x_out), ("out", out)):
+        if t is not None:
+            _need(t, name, torch.float32)
+            if t.numel() != rows:
+                raise ValueError(f"{name} has the wrong size")
+    _need(q8_out, "q8_out", torch.uint8)
+    if q8_out.numel() != F.q8_1_bytes(rows):
+        raise ValueError("q8_out has the wrong size")
+    _need(workspace, "workspace", torch.uint8)
+    _same_device(weights, activations, x, gamma, x_out, q8_out, out, workspace)
+    check(lib().mllb_q4k_matvec_norm(weights.data_ptr(), activations.data_ptr(), _ptr(out), rows, k, x.data_ptr(),
+                                     x_out.data_ptr(), gamma.data_ptr(), float(eps), q8_out.data_ptr(),
+                                     workspace.data_ptr(), workspace.numel(), _flags(pdl), _stream(weights)),
+          "q4k_matvec_norm")
+    return x_out, q8_out, out
 
 
 # ------------------------------------------------------- batched tokens (prefill)

@@ -32,14 +32,20 @@ def host_cache(t):
 
 
 def run_against_oracle(cfg, steps, token=17, graph=False, mode="quant_tail"):
+    """mode: "quant_tail" (the default Decoder), "separate" (a separate Q8_1
+    launch after gate/up), "norm_tail" (the default plus the residual norms
+    built into the O and down projections) or "fused"."""
     w, k, v = build(cfg)
     host = OD.host_model(w)
     kh, vh = host_cache(k), host_cache(v)
     stream = torch.cuda.Stream()
     with torch.cuda.stream(stream):
-        dec = D.Decoder(w, k, v, fused=mode == "fused", quant_tail=mode == "quant_tail")
+        dec = D.Decoder(w, k, v, fused=mode == "fused", quant_tail=mode in ("quant_tail", "norm_tail"),
+                        norm_tail=mode == "norm_tail")
         assert dec.fused == (mode == "fused")
-        assert dec.quant_tail == (mode == "quant_tail")
+        assert dec.quant_tail == (mode in ("quant_tail", "norm_tail"))
+        if mode == "norm_tail":
+            assert dec.norm_tail_down and dec.norm_tail_o == (cfg.attn_width // 256 in (8, 10, 16, 38))
         dec.reset(token)
         if graph:
             dec.capture()
@@ -64,7 +70,7 @@ def run_against_oracle(cfg, steps, token=17, graph=False, mode="quant_tail"):
 
 
 @pytest.mark.parametrize("cfg", [SMALL, ODD], ids=["qwen-2layer", "odd-shapes"])
-@pytest.mark.parametrize("mode", ["quant_tail", "separate", "fused"])
+@pytest.mark.parametrize("mode", ["quant_tail", "separate", "norm_tail", "fused"])
 def test_decode_steps_match_oracle(orc, cfg, mode):
     run_against_oracle(cfg, steps=3, mode=mode)
 

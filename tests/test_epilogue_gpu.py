@@ -54,3 +54,72 @@ def test_gate_up_q8_rejects_bad_shapes():
                                  q8.data_ptr(), None, 32, k, 0, None) != 0
     torch.cuda.synchronize()
     assert not counters.cpu().numpy().any()
+
+
+# ------------------------------------------------ residual + RMSNorm epilogue
+
+@pytest.mark.parametrize("rows,k", [(2560, 4096), (2560, 9728), (2560, 2560), (4096, 2560), (2048, 2048),
+                                    (1024, 4096)])
+def test_matvec_norm_equals_matvec_then_norm(orc, rows, k):
+    """mllb_q4k_matvec_norm == mllb_q4k_matvec_ex + the oracle's residual +
+    RMSNorm + Q8_1, twice in a row (the grid counters come back to zero)."""
+    w = dev(fx.seeded_q4k_matrix(rows, k, seed=31))
+    a = ops.quantize_q8_1(dev(fx.seeded_activation(k, seed=32)))
+    rng = np.random.default_rng(rows + k)
+    x = (rng.standard_normal(rows) * 3).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, rows).astype(np.float32)
+    delta = ops.q4_k_q8_1_matvec(w, a).cpu().numpy()
+    h_ref, q8_ref = orc.rmsnorm_q8_1(x, delta, gamma, 1e-6)
+    ws = ops.q4k_matvec_norm_workspace(rows, k, "cuda")
+    for call in range(2):
+        x_out = torch.full((rows,), 7.0, device="cuda")
+        out = torch.full((rows,), 5.0, device="cuda")
+        q8 = torch.zeros(F.q8_1_bytes(rows), dtype=torch.uint8, device="cuda")
+        ops.q4k_matvec_norm(w, a, dev(x), dev(gamma), 1e-6, x_out=x_out, q8_out=q8, out=out, workspace=ws,
+                            pdl=call == 1)
+        torch.cuda.synchronize()
+        assert np.array_equal(out.cpu().numpy().view(np.uint32), delta.view(np.uint32)), f"call {call}: delta"
+        assert np.array_equal(x_out.cpu().numpy(), h_ref), f"call {call}: residual"
+        assert np.array_equal(q8.cpu().numpy(), q8_ref), f"call {call}: Q8_1 of the norm"
+        assert not ws[:16].cpu().numpy().any()
+    assert ops.device_error() == 0
+
+
+def test_matvec_norm_in_place_and_without_delta(orc):
+    rows, k = 2560, 4096
+    w = dev(fx.seeded_q4k_matrix(rows, k, seed=41))
+    a = ops.quantize_q8_1(dev(fx.seeded_activation(k, seed=42)))
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(rows).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, rows).astype(np.float32)
+    delta = ops.q4_k_q8_1_matvec(w, a).cpu().numpy()
+    h_ref, q8_ref = orc.rmsnorm_q8_1(x, delta, gamma, 1e-6)
+    xd = dev(x)
+    _, q8, _ = ops.q4k_matvec_norm(w, a, xd, dev(gamma), 1e-6, x_out=xd)
+    assert np.array_equal(xd.cpu().numpy(), h_ref)
+    assert np.array_equal(q8.cpu().numpy(), q8_ref)
+
+
+def test_matvec_norm_rejects_bad_arguments():
+    from mojo_llm_lab_b200._lib import lib
+    k, rows = 2560, 48
+    w = torch.zeros(64 * F.q4k_row_bytes(k), dtype=torch.uint8, device="cuda")
+    a = torch.zeros(F.q8_1_bytes(k), dtype=torch.uint8, device="cuda")
+    x = torch.zeros(64, device="cuda")
+    q8 = torch.zeros(F.q8_1_bytes(64), dtype=torch.uint8, device="cuda")
+    ws = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    L = lib()
+    P = lambda t: t.data_ptr()  # noqa: E731
+    # 48 rows: not whole Q8_1 groups
+    assert L.mllb_q4k_matvec_norm(P(w), P(a), None, rows, k, P(x), P(x), P(x), 1e-6, P(q8), P(ws), ws.numel(), 0,
+                                  None) != 0
+    # workspace too small
+    assert L.mllb_q4k_matvec_norm(P(w), P(a), None, 64, k, P(x), P(x), P(x), 1e-6, P(q8), P(ws), 8, 0, None) != 0
+    # x_out overlapping x off by one element
+    assert L.mllb_q4k_matvec_norm(P(w), P(a), None, 32, k, P(x), P(x) + 4, P(q8), 1e-6, P(q8), P(ws), ws.numel(),
+                                  0, None) != 0
+    # K with no streaming configuration
+    assert L.mllb_q4k_matvec_norm(P(w), P(a), None, 32, 768, P(x), P(x), P(x), 1e-6, P(q8), P(ws), ws.numel(), 0,
+                                  None) != 0
+    torch.cuda.synchronize()
+    assert not ws.cpu().numpy().any()
