@@ -36,6 +36,10 @@
 #ifndef MLLB_CFG_Q4K_10_SMALL
 #define MLLB_CFG_Q4K_10_SMALL 8, 2, 2
 #endif
+// Row tiles per SM up to which K = 2560 takes the small configuration.
+#ifndef MLLB_Q4K_10_SMALL_TILES_PER_SM
+#define MLLB_Q4K_10_SMALL_TILES_PER_SM 2
+#endif
 #ifndef MLLB_CFG_Q4K_16
 #define MLLB_CFG_Q4K_16 8, 4, 3
 #endif
@@ -248,7 +252,7 @@ int q4k_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, f
         using Small = mllb::TeamConfig<F, 10, 1, MLLB_CFG_Q4K_10_SMALL>;
         int dev, rc;
         if ((rc = current_device(&dev))) return rc;
-        if ((rows + Small::kT - 1) / Small::kT <= 2 * sm_count(dev))
+        if ((rows + Small::kT - 1) / Small::kT <= MLLB_Q4K_10_SMALL_TILES_PER_SM * sm_count(dev))
           return launch_team<F, 10, 1, MLLB_CFG_Q4K_10_SMALL>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
         return launch_team<F, 10, 1, MLLB_CFG_Q4K_10>(w0, w1, src, o0, o1, o2, rows, stream, pdl);
       }
@@ -299,7 +303,7 @@ int q4k_norm_team(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, in
       using Small = mllb::TeamConfig<F, 10, 1, MLLB_CFG_Q4K_10_SMALL>;
       int dev, rc;
       if ((rc = current_device(&dev))) return rc;
-      if ((rows + Small::kT - 1) / Small::kT <= 2 * sm_count(dev))
+      if ((rows + Small::kT - 1) / Small::kT <= MLLB_Q4K_10_SMALL_TILES_PER_SM * sm_count(dev))
         return launch_team_kernel<F, 10, 1, MLLB_CFG_Q4K_10_SMALL, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
       return launch_team_kernel<F, 10, 1, MLLB_CFG_Q4K_10, false, E>(w, nullptr, src, out, nullptr, nullptr, rows, stream, pdl, epi);
     }
@@ -1223,7 +1227,7 @@ extern "C" int mllb_q5k_matvec_ex(const void* weights, const void* q8, float* ou
       using Small = mllb::TeamConfig<F, 10, 1, MLLB_CFG_Q5K_10_SMALL>;
       int dev;
       if ((rc = current_device(&dev))) return rc;
-      if ((rows + Small::kT - 1) / Small::kT <= 2 * sm_count(dev))
+      if ((rows + Small::kT - 1) / Small::kT <= MLLB_Q4K_10_SMALL_TILES_PER_SM * sm_count(dev))
         return launch_team<F, 10, 1, MLLB_CFG_Q5K_10_SMALL>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
       return launch_team<F, 10, 1, MLLB_CFG_Q5K_10>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
     }
