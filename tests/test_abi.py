@@ -29,6 +29,13 @@ def test_abi_version_and_error_string():
     lambda L: L.mllb_rmsnorm_imrope_q(None, None, None, None, None, 32, None),
     lambda L: L.mllb_q4k_subdots(None, None, None, None, 1, 256, None),
     lambda L: L.mllb_stream_read(None, 16, None, 0, None),
+    lambda L: L.mllb_kv_q4_0_store(None, None, None, None, None, 8, 64, 0, 1, 0, None),
+    lambda L: L.mllb_decode_attention_q4_0(None, 16, 16, 16, 16, 16, 1 << 20, 16, 16, 32, 8, 64, 0, None),
+    lambda L: L.mllb_decode_attention_qkv_q4_0(None, None, None, 0.5, 16, 16, 16, 16, 16, 1 << 20, 16, 16, 32, 8,
+                                               64, 0, None),
+    lambda L: L.mllb_q4k_matvec_norm(None, None, None, 2560, 4096, None, None, None, 1e-6, None, None, 4096, 0,
+                                     None),
+    lambda L: L.mllb_q4k_gate_up_q8(None, None, None, None, None, None, None, None, 32, 2560, 0, None),
 ])
 def test_null_pointers_rejected_without_cuda(call):
     assert call(_lib.lib()) == _lib.MLLB_EINVAL
@@ -45,6 +52,22 @@ def test_shape_and_alignment_rejections():
     assert L.mllb_q4k_matvec(8, 16, 16, 4, 2560, None) == _lib.MLLB_EALIGN
     assert L.mllb_q6k_matvec(8, 16, 16, 4, 2560, None) == _lib.MLLB_EALIGN
     assert L.mllb_q4k_gate_up(16, 16, 16, None, None, None, 4, 2560, None) == _lib.MLLB_EINVAL
+
+
+def test_new_entry_rejections_without_cuda():
+    L = _lib.lib()
+    # residual-norm matvec: rows not whole Q8_1 groups, workspace too small,
+    # negative eps; its workspace size is pure arithmetic.
+    assert L.mllb_q4k_matvec_norm(16, 16, None, 48, 2560, 16, 16, 16, 1e-6, 16, 16, 4096, 0, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 16, 16, 16, 1e-6, 16, 16, 8, 0, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 16, 16, 16, -1.0, 16, 16, 4096, 0, None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm_workspace(2560, 4096) == 16 + 8 * 640
+    # Q4_0 cache store: rows past the cache, misaligned scale plane for the attention
+    assert L.mllb_kv_q4_0_store(16, 16, 16, 16, 16, 2, 10, 7, 4, 0, None) == _lib.MLLB_EINVAL
+    assert L.mllb_decode_attention_q4_0(16, 16, 16, 18, 16, 16, 1 << 20, 16, 16, 32, 8, 64, 0,
+                                        None) == _lib.MLLB_EALIGN
+    assert L.mllb_decode_attention_q4_0(16, 16, 16, None, 16, 16, 1 << 20, 16, 16, 32, 8, 64, 0,
+                                        None) == _lib.MLLB_EINVAL
 
 
 def test_compat_cubin_built_for_sm100a():
