@@ -1,0 +1,50 @@
+"""bench.py's reference arm on the CPU: `--impl reference` times the oracle
+(the reference's CPU algorithm restated) and prints one JSON line carrying the
+same metric and unit as the GPU arm, with its cpu_baseline and e2e; under a
+multi-rank launch only rank 0 runs and prints."""
+import json
+import os
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parents[1]
+
+
+def run_bench(args, env_extra=None):
+    env = dict(os.environ)
+    env.update(env_extra or {})
+    proc = subprocess.run([sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1",
+                           "--warmup", "3", *args], capture_output=True, text=True, cwd=ROOT, env=env, timeout=300)
+    assert proc.returncode == 0, proc.stderr[-2000:]
+    return [json.loads(line) for line in proc.stdout.splitlines() if line.startswith("{")]
+
+
+@pytest.mark.parametrize("args,unit", [
+    ([], "GB/s"),
+    (["--workload", "attention"], "GB/s"),
+    (["--workload", "attention", "--kv", "q4_0"], "GB/s"),
+    (["--workload", "imrope"], "us/op"),
+    (["--workload", "prefill"], "int8 TOP/s"),
+])
+def test_reference_arm_prints_the_contract_line(args, unit):
+    lines = run_bench(args)
+    assert len(lines) == 1
+    line = lines[0]
+    assert line["impl"] == "reference"
+    assert line["unit"] == unit and line["value"] > 0
+    assert line["n_gpus"] == 1 and line["steps"] == 1 and line["warmup"] == 3
+    cpu = line["cpu_baseline"]
+    assert cpu["kind"] in ("port", "reference") and cpu["cores"] >= 1 and cpu["sample"]
+    assert cpu["value"] == pytest.approx(line["value"], rel=1e-3)
+    e2e = line["e2e"]
+    assert e2e["unit"] == unit and e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+    assert "workload" in line["config"]
+    if "--kv" in args:
+        assert "Q4_0" in line["metric"]
+
+
+def test_reference_arm_prints_on_rank_zero_only():
+    assert run_bench(["--workload", "attention"], {"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
