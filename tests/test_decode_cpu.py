@@ -115,3 +115,43 @@ def test_logit_agreement_criterion():
     bad = OD.logit_agreement(ref, np.array([1.0, 100.0, -2.99], dtype=np.float32))
     assert bad["violations"] == 1
     assert not OD.logit_agreement(ref, np.array([200.0, 100.0, -3.0], dtype=np.float32))["top_match"]
+
+
+def test_kv_bytes_of_both_cache_types():
+    cfg = D.DecodeConfig()
+    assert cfg.kv_bytes_read(4096, "f16") == 603_979_776
+    assert cfg.kv_bytes_read(4096, "q4_0") == 36 * 8 * 4096 * 144
+    assert cfg.bytes_per_token(4096, "q4_0") == cfg.q4k_bytes() + cfg.q6k_bytes() + 36 * 8 * 4096 * 144
+
+
+def test_oracle_step_over_a_q4_0_cache(orc):
+    """The whole-step oracle with a Q4_0 cache (tiny stack, CPU): it appends
+    the token's K / V rows to the planes by the GGML rule, leaves the other
+    rows alone, and its logits stay close to the fp16-cache step over the
+    same rows (the cache's 4-bit error is the only difference)."""
+    cfg = D.DecodeConfig(layers=2, hidden=256, q_heads=2, kv_heads=1, ffn=256, vocab=64, context=40,
+                         new_tokens=2, seed=5)
+    w = D.generate_weights(cfg, "cpu")
+    host = OD.host_model(w)
+    k16, v16 = D.generate_kv_cache(cfg, "cpu")
+    kh, vh = k16.numpy().view(np.uint16).copy(), v16.numpy().view(np.uint16).copy()
+    qs = (cfg.layers, cfg.kv_heads, cfg.ctx_capacity, 64)
+    planes = (np.zeros(qs, np.uint8), np.zeros(qs, np.uint8), np.zeros(qs[:3] + (8,), np.uint16))
+    for layer in range(cfg.layers):
+        for slot, p, lo in ((9, planes[0], 0), (10, planes[1], 4)):
+            rows = D._kv_values(cfg, layer, slot, "cpu").numpy()
+            p[layer, :, :cfg.context], planes[2][layer, :, :cfg.context, lo:lo + 4] = orc.kv_q4_0_rows(rows)
+    before = [p.copy() for p in planes]
+    ref16, tok16 = OD.reference_step(host, kh, vh, 7, cfg.context)
+    ref4, tok4 = OD.reference_step(host, None, None, 7, cfg.context, q4_0=planes)
+    assert np.all(np.isfinite(ref4))
+    for b, p in zip(before, planes):
+        assert np.array_equal(b[:, :, :cfg.context], p[:, :, :cfg.context])   # prefilled rows untouched
+        assert np.array_equal(b[:, :, cfg.context + 1:], p[:, :, cfg.context + 1:])
+        assert p[:, :, cfg.context].any()                                     # the token's row appended
+    # 4-bit K / V (about 1/16 of each block's range per value) over random
+    # weights move these logits by ~12 % (relative L2); a wrong row or plane
+    # would decorrelate them entirely.
+    rel = np.linalg.norm(ref4.astype(np.float64) - ref16) / np.linalg.norm(ref16.astype(np.float64))
+    assert rel < 0.25, rel
+    assert np.corrcoef(ref4, ref16)[0, 1] > 0.95
