@@ -1048,6 +1048,12 @@ int mllb_q4k_matvec_norm(const void* weights, const void* q8, float* out, int64_
   if ((x_out != x && overlaps(x_out, n * 4, x, n * 4)) || overlaps(x_out, n * 4, gamma, n * 4) ||
       overlaps(out, n * 4, x, n * 4) || overlaps(out, n * 4, x_out, n * 4))
     return fail(MLLB_EINVAL, "x_out may equal x but must not otherwise overlap x, gamma or out");
+  const int64_t q8_bytes = n / 32 * 36;
+  if (overlaps(q8_out, q8_bytes, x, n * 4) || overlaps(q8_out, q8_bytes, x_out, n * 4) ||
+      overlaps(q8_out, q8_bytes, gamma, n * 4) || overlaps(q8_out, q8_bytes, out, n * 4) ||
+      overlaps(q8_out, q8_bytes, workspace, need) || overlaps(workspace, need, x_out, n * 4) ||
+      overlaps(workspace, need, out, n * 4))
+    return fail(MLLB_EINVAL, "q8_out and workspace must not overlap each other or the fp32 buffers");
   mllb::Epilogue epi = {};
   epi.counters = static_cast<uint32_t*>(workspace);
   epi.q8_out = static_cast<uint8_t*>(q8_out);

@@ -62,6 +62,11 @@ def test_new_entry_rejections_without_cuda():
     assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 16, 16, 16, 1e-6, 16, 16, 8, 0, None) == _lib.MLLB_EINVAL
     assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 16, 16, 16, -1.0, 16, 16, 4096, 0, None) == _lib.MLLB_EINVAL
     assert L.mllb_q4k_matvec_norm_workspace(2560, 4096) == 16 + 8 * 640
+    # q8_out inside x_out, workspace inside q8_out
+    assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 8192 + 64, 1 << 20, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 32768, 32768 + 16, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
     # Q4_0 cache store: rows past the cache, misaligned scale plane for the attention
     assert L.mllb_kv_q4_0_store(16, 16, 16, 16, 16, 2, 10, 7, 4, 0, None) == _lib.MLLB_EINVAL
     assert L.mllb_decode_attention_q4_0(16, 16, 16, 18, 16, 16, 1 << 20, 16, 16, 32, 8, 64, 0,
