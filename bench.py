@@ -570,6 +570,7 @@ def run_prefill_reference(args, rank: int, world: int):
 def run_prefill(args, rank: int, world: int):
     """One step = `copies` batched launches over distinct weight and activation copies (> 2x L2)."""
     import torch
+    import torch.distributed as dist
 
     from mojo_llm_lab_b200 import fixtures as fx
     from mojo_llm_lab_b200 import ops
@@ -617,12 +618,19 @@ def run_prefill(args, rank: int, world: int):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         preroll(graph)
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
         stop.record(stream)
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop) / args.steps
+    if world > 1:  # the slowest rank's time
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     ops_per_launch = 2.0 * rows * k * tokens
     value = copies * ops_per_launch / (ms * 1e-3) / 1e12
 
@@ -647,6 +655,9 @@ def run_prefill(args, rank: int, world: int):
     for _ in range(args.warmup):
         e_graph.replay()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -654,6 +665,10 @@ def run_prefill(args, rank: int, world: int):
     e1.record(stream)
     torch.cuda.synchronize()
     e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
     del graph, e_graph
     if ops.device_error():
         raise SystemExit("device error word set")
@@ -785,6 +800,7 @@ def run_attention(args, rank: int, world: int):
     (> 2x L2 together), PDL-chained in one CUDA graph: q/k RMSNorm + IMROPE, the K/V append at
     row `context`, attention over context + 1 keys, combine -> fp32 + Q8_1."""
     import torch
+    import torch.distributed as dist
 
     from mojo_llm_lab_b200 import decode as D
     from mojo_llm_lab_b200 import formats as F
@@ -864,12 +880,19 @@ def run_attention(args, rank: int, world: int):
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
         preroll(graph)
+        if world > 1:
+            dist.barrier()
+            torch.cuda.synchronize()
         start.record(stream)
         for _ in range(args.steps):
             graph.replay()
         stop.record(stream)
         torch.cuda.synchronize()
     ms = start.elapsed_time(stop) / args.steps
+    if world > 1:  # the slowest rank's time
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
     kv_bytes = attention_kv_bytes(context, kv)
     us_call = ms * 1e3 / copies
     gbs = kv_bytes / (us_call * 1e-6) / 1e9
@@ -892,6 +915,9 @@ def run_attention(args, rank: int, world: int):
     for _ in range(args.warmup):
         e_graph.replay()
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(args.steps):
@@ -899,6 +925,10 @@ def run_attention(args, rank: int, world: int):
     e1.record(stream)
     torch.cuda.synchronize()
     e_ms = e0.elapsed_time(e1) / args.steps
+    if world > 1:
+        t = torch.tensor([e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e_ms = float(t.item())
     del graph, e_graph
     if ops.device_error():
         raise SystemExit("device error word set")
