@@ -61,7 +61,7 @@ int mllb_abi_version(void);
 const char *mllb_last_error(void);
 
 /*
- * Device error word: bit 0/1/2 = a kernel gave up a bounded (~1 s) wait on
+ * Device error word (bit n = mask 1 << n): bit 0/1/2 = a kernel gave up a bounded (~1 s) wait on
  * its TMA pipeline (see csrc/common.cuh); bit 3 = decode next-token key out
  * of range; bit 4 = decode position outside the KV cache; bit 5 = decode
  * attention gave up waiting for its K/V copies; bit 6 = a peer all-gather
@@ -299,7 +299,7 @@ int mllb_q4k_gate_up_q8(const void *up_weights, const void *gate_weights, const 
  * (peer mappings, e.g. symmetric memory); count: this rank's gather counter
  * (one uint32, zero before the first gather).  Every rank must issue the
  * same sequence of gathers with the same k, each on its own GPU.  A rank
- * that does not arrive within ~1 s sets device error bit 64.  Replaces the
+ * that does not arrive within ~1 s sets device error bit 6 (mask 0x40).  Replaces the
  * NCCL all-gather of the sharded SwiGLU product.  world <= 8.
  */
 typedef struct mllb_peer_gather {
@@ -333,7 +333,7 @@ int64_t mllb_key_token(int64_t key);
  * rows x k (the output projection, tied to the token embedding), token taken
  * from state->next_token_key.  Records state->token and, when tokens is not
  * NULL, tokens[state->steps] (if steps < capacity).  An out-of-range key
- * sets device error bit 8 and embeds row 0.  GGML get_rows on the token
+ * sets device error bit 3 (mask 0x08) and embeds row 0.  GGML get_rows on the token
  * embedding (no reference kernel).
  */
 int mllb_decode_embed(const void *q6k_weights, int64_t vocab, int64_t k, mllb_decode_state *state, int32_t *tokens,
@@ -366,7 +366,7 @@ int mllb_decode_final_norm(const float *x, const float *delta, float *x_out, con
  * IMROPE axis positions (pos, pos, pos, 0), theta scale theta_scale (host
  * double; the reference's runtime value is the fp32 0x3f492c27).
  * Caches: fp16 [kv_heads][ctx][128].  pos outside [0, ctx) sets device error
- * bit 16 and appends nothing.  The q part is the reference's
+ * bit 4 (mask 0x10) and appends nothing.  The q part is the reference's
  * kernels/fused_q_imrope_runtime_fastpow.mojo:8-36 per head.
  */
 int mllb_decode_qk_rope_append(const float *qkv, const float *q_gamma, const float *k_gamma,
@@ -397,7 +397,7 @@ int mllb_decode_attention(const float *q, const void *k_cache, const void *v_cac
  * + q_gamma + IMROPE itself, appends the K row (RMSNorm + k_gamma + IMROPE,
  * fp16) and the V row (fp16) at state->pos, and attends as
  * mllb_decode_attention -- one launch fewer, the same numbers.  pos outside
- * [0, ctx) sets device error bit 16 and appends nothing.
+ * [0, ctx) sets device error bit 4 (mask 0x10) and appends nothing.
  */
 int mllb_decode_attention_qkv(const float *qkv, const float *q_gamma, const float *k_gamma, double theta_scale,
                               const mllb_decode_state *state, void *k_cache, void *v_cache, double *scratch,

@@ -1052,8 +1052,10 @@ int mllb_q4k_matvec_norm(const void* weights, const void* q8, float* out, int64_
   if (overlaps(q8_out, q8_bytes, x, n * 4) || overlaps(q8_out, q8_bytes, x_out, n * 4) ||
       overlaps(q8_out, q8_bytes, gamma, n * 4) || overlaps(q8_out, q8_bytes, out, n * 4) ||
       overlaps(q8_out, q8_bytes, workspace, need) || overlaps(workspace, need, x_out, n * 4) ||
-      overlaps(workspace, need, out, n * 4))
-    return fail(MLLB_EINVAL, "q8_out and workspace must not overlap each other or the fp32 buffers");
+      overlaps(workspace, need, out, n * 4) || overlaps(workspace, need, x, n * 4) ||
+      overlaps(workspace, need, gamma, n * 4) || overlaps(workspace, need, q8, k / 32 * 36) ||
+      overlaps(q8_out, q8_bytes, q8, k / 32 * 36))
+    return fail(MLLB_EINVAL, "q8_out and workspace must not overlap each other, the Q8_1 input or the fp32 buffers");
   mllb::Epilogue epi = {};
   epi.counters = static_cast<uint32_t*>(workspace);
   epi.q8_out = static_cast<uint8_t*>(q8_out);

@@ -1,8 +1,8 @@
 """Generate tests/golden/golden.json by running the REFERENCE's own Python code.
 
-Run in a container where the reference checkout is mounted (read-only):
+Run where a checkout of the reference is available (it is only read):
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 It imports the reference's oracles (tests/q4_reference.py, tests/reference_math.py)
 and fixture generators (tools/generate_fixtures.py,
@@ -16,8 +16,9 @@ tools/generate_q4_matvec_fixtures.py) and records:
   activation was quantised by this repository's oracle (the reference has no
   quantiser of its own; its dot is what is pinned here).
 
-The JSON is read by tests/test_oracle_golden.py and tests/test_fixtures_golden.py;
-nothing at test time touches the reference checkout.
+The JSON is read by tests/test_oracle_golden.py (the oracle against it) and by
+the GPU parity tests (test_q4k_gpu.py, test_imrope_gpu.py, test_q8_1_gpu.py,
+test_compat_gpu.py); nothing at test time touches the reference checkout.
 """
 from __future__ import annotations
 
@@ -41,7 +42,7 @@ def sha(data: bytes) -> str:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="path of the reference checkout (read only)")
     args = ap.parse_args()
     ref = Path(args.reference)
     sys.dont_write_bytecode = True  # the checkout is read-only

@@ -67,6 +67,15 @@ def test_new_entry_rejections_without_cuda():
                                   None) == _lib.MLLB_EINVAL
     assert L.mllb_q4k_matvec_norm(16, 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 32768, 32768 + 16, 4096, 0,
                                   None) == _lib.MLLB_EINVAL
+    # workspace over x, over gamma, over the Q8_1 input; q8_out over the Q8_1 input
+    assert L.mllb_q4k_matvec_norm(16, 1 << 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 32768, 4096, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 1 << 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 32768, 16384, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 1 << 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 32768, 1 << 16, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
+    assert L.mllb_q4k_matvec_norm(16, 1 << 16, None, 64, 2560, 4096, 8192, 16384, 1e-6, 1 << 16, 1 << 20, 4096, 0,
+                                  None) == _lib.MLLB_EINVAL
     # Q4_0 cache store: rows past the cache, misaligned scale plane for the attention
     assert L.mllb_kv_q4_0_store(16, 16, 16, 16, 16, 2, 10, 7, 4, 0, None) == _lib.MLLB_EINVAL
     assert L.mllb_decode_attention_q4_0(16, 16, 16, 18, 16, 16, 1 << 20, 16, 16, 32, 8, 64, 0,

@@ -12,6 +12,7 @@ import torch
 from gpu_util import assert_within_tolerance, canaries_intact, dev, dev_bytes, with_canaries
 from mojo_llm_lab_b200 import build
 from mojo_llm_lab_b200 import fixtures as fx
+import ref_fixtures as rfx
 from mojo_llm_lab_b200 import formats as F
 
 pytestmark = pytest.mark.gpu
@@ -55,7 +56,7 @@ def drv():
 def test_plain_matvec_entries(drv, golden, entry, block):
     # q4_comparison_worker.py: 64-row fixture tiled x152 to 9728 rows, grid rows x block 32
     g = golden["q4_reference_fixtures"]["default"]
-    files = fx.q4_matvec_fixtures()
+    files = rfx.q4_matvec_fixtures()
     w = dev_bytes(fx.tile_rows(files["weights.bin"], 1440, 9728))
     act = dev_bytes(files["activations.bin"])
     buf, out = with_canaries(9728)
@@ -67,7 +68,7 @@ def test_plain_matvec_entries(drv, golden, entry, block):
 
 def test_gate_order_entry(drv, orc, golden):
     g = golden["q4_reference_fixtures"]["varied_activations"]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     w, gw, act = (dev_bytes(files[n]) for n in ("weights.bin", "gate.bin", "activations.bin"))
     buf, out = with_canaries(64)
     drv.launch("q4_k_q8_1_gate_order", 64, 128, w, gw, act, out)
@@ -78,7 +79,7 @@ def test_gate_order_entry(drv, orc, golden):
 
 def test_gate_order_2b_entry(drv, orc, golden):
     g = golden["q4_reference_fixtures"]["width2048"]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     w, gw, act = (dev_bytes(files[n]) for n in ("weights.bin", "gate.bin", "activations.bin"))
     out = torch.empty(64, dtype=torch.float32, device="cuda")
     drv.launch("q4_k_q8_1_gate_order_2b", 64, 128, w, gw, act, out)
@@ -88,7 +89,7 @@ def test_gate_order_2b_entry(drv, orc, golden):
 
 def test_imrope_entry(drv, orc):
     # benchmark/bench.c: grid 32 x block 128, theta bits 0x3f492c27, canaries
-    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(fx.imrope_reference_inputs(fx.IMROPE_CASES["long_position"])))
+    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(rfx.imrope_reference_inputs(rfx.IMROPE_CASES["long_position"])))
     theta = torch.tensor([F.THETA_SCALE_BITS], dtype=torch.int64).to(torch.int32).view(torch.float32).cuda()
     buf, out = with_canaries(4096, guard=1, fill=float("nan"))
     drv.launch("fused_q_imrope_runtime_fastpow", 32, 128, dev(q), dev(gamma), dev(pos), out, theta)

@@ -15,6 +15,7 @@ import torch
 
 from gpu_util import assert_within_tolerance, dev
 from mojo_llm_lab_b200 import fixtures as fx
+import ref_fixtures as rfx
 from mojo_llm_lab_b200 import formats as F
 from mojo_llm_lab_b200 import ops
 
@@ -28,9 +29,9 @@ def _run_ref_abi(q, gamma, pos):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("name", list(fx.IMROPE_CASES))
+@pytest.mark.parametrize("name", list(rfx.IMROPE_CASES))
 def test_reference_fixtures_at_runtime_theta(orc, name):
-    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(fx.imrope_reference_inputs(fx.IMROPE_CASES[name])))
+    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(rfx.imrope_reference_inputs(rfx.IMROPE_CASES[name])))
     got = _run_ref_abi(q, gamma, pos)
     ref = orc.imrope(q, gamma, pos, orc.runtime_theta_scale())
     assert_within_tolerance(got.reshape(-1), ref.reshape(-1), name)
@@ -44,10 +45,10 @@ def test_seeded_inputs_at_runtime_theta(orc, name):
     assert_within_tolerance(got.reshape(-1), ref.reshape(-1), name)
 
 
-@pytest.mark.parametrize("name", list(fx.IMROPE_CASES))
+@pytest.mark.parametrize("name", list(rfx.IMROPE_CASES))
 def test_reference_goldens_at_exact_theta(golden, name):
     g = golden["imrope_reference_fixtures"][name]
-    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(fx.imrope_reference_inputs(g["positions"])))
+    q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"])))
     out = ops.rmsnorm_imrope_q(dev(q), dev(gamma), dev(pos), theta_scale=golden["reference_theta_scale"])
     got = out.cpu().numpy()
     assert_within_tolerance(got[0], g["head0"], name + " head0")
@@ -59,7 +60,7 @@ def test_reference_goldens_need_float64_theta_only_at_long_positions(golden, orc
     # exact-base reference; long_position does not (documented input effect).
     for name in ("distinct_axes", "fallback_only"):
         g = golden["imrope_reference_fixtures"][name]
-        q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(fx.imrope_reference_inputs(g["positions"])))
+        q, gamma, pos = fx.parse_imrope(fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"])))
         got = _run_ref_abi(q, gamma, pos)
         assert_within_tolerance(got[0], g["head0"], name)
 
@@ -84,5 +85,5 @@ def test_zero_input_gives_zero():
 
 def test_input_fixture_hashes_unchanged(golden):
     for name, g in golden["imrope_reference_fixtures"].items():
-        payload = fx.serialize_imrope(fx.imrope_reference_inputs(g["positions"]))
+        payload = fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"]))
         assert hashlib.sha256(payload).hexdigest() == g["input_sha256"]

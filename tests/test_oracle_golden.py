@@ -11,6 +11,7 @@ import numpy as np
 import pytest
 
 from mojo_llm_lab_b200 import fixtures as fx
+import ref_fixtures as rfx
 
 
 def sha(b: bytes) -> str:
@@ -33,7 +34,7 @@ def test_reference_theta_scale_bits(orc, golden):
 @pytest.mark.parametrize("name", ["distinct_axes", "long_position", "fallback_only"])
 def test_imrope_reference_fixtures_bit_exact(orc, golden, name):
     g = golden["imrope_reference_fixtures"][name]
-    payload = fx.serialize_imrope(fx.imrope_reference_inputs(g["positions"]))
+    payload = fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"]))
     assert sha(payload) == g["input_sha256"]
     q, gamma, positions = fx.parse_imrope(payload)
     out = orc.imrope(q, gamma, positions, orc.reference_theta_scale())
@@ -70,7 +71,7 @@ def test_imrope_contract_cases(orc):
                                   "default_activation_scales", "width2048"])
 def test_q4_dot_bit_exact_on_reference_fixtures(orc, golden, case):
     g = golden["q4_reference_fixtures"][case]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     assert {k: sha(v) for k, v in files.items()} == g["sha256"]
     width = g["options"].get("input_width", 2560)
     for key in ("weights", "gate"):
@@ -143,7 +144,7 @@ def test_q4_decoder_all_six_bit_values(orc):
     for value in range(64):
         scales = [(value + j * 7) % 64 for j in range(8)]
         minima = [(63 - value + j * 11) % 64 for j in range(8)]
-        got = orc.decode_block(F.q4k_block(scales, minima, 0.5, 0.25, fx.DEMO_QUANTS))
+        got = orc.decode_block(F.q4k_block(scales, minima, 0.5, 0.25, rfx.DEMO_QUANTS))
         want = [0.5 * scales[g] * (lane % 16 if g % 2 == 0 else 15 - lane % 16) - 0.25 * minima[g]
                 for g in range(8) for lane in range(32)]
         assert got == want
@@ -152,10 +153,10 @@ def test_q4_decoder_all_six_bit_values(orc):
 def test_q4_dot_reference_contract_cases(orc):
     # tests/test_q4_dot.py:13-23 restated
     from mojo_llm_lab_b200 import formats as F
-    weights = F.q4k_block([1] * 8, [0] * 8, 1, 0, fx.DEMO_QUANTS) * 10
+    weights = F.q4k_block([1] * 8, [0] * 8, 1, 0, rfx.DEMO_QUANTS) * 10
     groups = [struct.pack("<ee32b", (g + 1) / 8, 0, *([1] * 32)) for g in range(8)]
     assert orc.dot_q4_q8(weights, b"".join(groups) * 10) == 10 * 240 * sum((g + 1) / 8 for g in range(8))
-    weights = F.q4k_block([0] * 8, [1] * 8, 0, 0.5, fx.DEMO_QUANTS)
+    weights = F.q4k_block([0] * 8, [1] * 8, 0, 0.5, rfx.DEMO_QUANTS)
     assert orc.dot_q4_q8(weights, struct.pack("<ee32b", 1, 0, *([1, -1] * 16)) * 8) == 0
     assert orc.dot_q4_q8(weights, struct.pack("<ee32b", 1, 32, *([1] * 32)) * 8) == -128
     for w, a in [(b"", b""), (bytes(144), bytes(36)), (bytes(145), bytes(288))]:

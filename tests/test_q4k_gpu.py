@@ -9,6 +9,7 @@ import torch
 
 from gpu_util import assert_within_tolerance, canaries_intact, dev, dev_bytes, with_canaries
 from mojo_llm_lab_b200 import fixtures as fx
+import ref_fixtures as rfx
 from mojo_llm_lab_b200 import ops
 
 pytestmark = pytest.mark.gpu
@@ -20,7 +21,7 @@ REF_CASES = ["default", "random_quants", "gate_up", "gate_up_rows128", "varied_f
 @pytest.mark.parametrize("case", REF_CASES)
 def test_reference_fixtures_match_golden(golden, case):
     g = golden["q4_reference_fixtures"][case]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     act = dev_bytes(files["activations.bin"])
     for key in ("weights", "gate"):
         if "dot_" + key not in g:
@@ -40,7 +41,7 @@ def test_reference_fixtures_match_golden(golden, case):
 @pytest.mark.parametrize("case", ["gate_up", "varied_factors", "varied_activations", "width2048"])
 def test_reference_gate_up_fixtures(orc, golden, case):
     g = golden["q4_reference_fixtures"][case]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     k = g["options"].get("input_width", 2560)
     rows = len(g["dot_weights"])
     up_w, gate_w, act = (dev_bytes(files[n]) for n in ("weights.bin", "gate.bin", "activations.bin"))
@@ -58,7 +59,7 @@ def test_reference_gate_up_fixtures(orc, golden, case):
 def test_reference_fixture_tiled_to_9728_rows(golden):
     # benchmark/q4_compare.c:148-163 tiles the 64-row file to ROWS=9728
     g = golden["q4_reference_fixtures"]["varied_activations"]
-    files = fx.q4_matvec_fixtures(**g["options"])
+    files = rfx.q4_matvec_fixtures(**g["options"])
     w = dev_bytes(fx.tile_rows(files["weights.bin"], 1440, 9728))
     gw = dev_bytes(fx.tile_rows(files["gate.bin"], 1440, 9728))
     act = dev_bytes(files["activations.bin"])
