@@ -111,7 +111,7 @@ def profiled_traffic(name: str):
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples (every 100 ms) around the timed region.
+    """nvidia-smi clock / throttle-reason samples (every 20 ms) around the timed region.
 
     Started under load shortly before the timed region and stopped right after
     it (the recipe's `nvidia-smi ... -lms` line)."""
@@ -128,7 +128,7 @@ class ClockSampler:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
@@ -160,10 +160,12 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for s in samples for i in range(4) if s[5 + i] == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
-                "reasons": reasons, "samples": len(samples)}
+                "reasons": reasons, "samples": len(samples),
+                "window": "every 20 ms over ~1 s of the same graph replayed just before the timed region, "
+                          "and the timed region"}
 
 
-def preroll(graph, seconds: float = 0.5) -> None:
+def preroll(graph, seconds: float = 1.0) -> None:
     """Replay `graph` for about `seconds` (untimed) so that the clock samples
     taken around the timed region describe the same load.  For graphs with no
     collectives (every rank may replay a different number of times)."""
@@ -205,15 +207,16 @@ def oracle_outputs(kind: str, ws, act: bytes, rows: int, k: int, threads: int = 
 
 # ----------------------------------------------------------------------------- reference arm
 
-def cpu_reference(workload: str, target_s: float = 10.0):
-    """Time the oracle (CPU restatement of the reference's path) with all host threads
-    on a bounded sample: whole operations of the workload, repeated for ~target_s."""
+def cpu_reference(workload: str, target_s: float = 10.0, threads: int = 0):
+    """Time the oracle (CPU restatement of the reference's path) on a bounded
+    sample: whole operations of the workload, repeated for ~target_s.
+    threads = 0: all host threads (OpenMP over rows)."""
     import oracle
     from mojo_llm_lab_b200 import fixtures as fx
 
     wl = WORKLOADS[workload]
     kind, rows, k = wl["kind"], wl["rows"], wl["k"]
-    threads = os.cpu_count() or 1
+    threads = threads or os.cpu_count() or 1
     ws = host_weights(kind, rows, k, seed=1)
     act = oracle.quantize_q8_1(fx.seeded_activation(k, seed=2))
     t0 = time.perf_counter()
@@ -234,17 +237,98 @@ def cpu_reference(workload: str, target_s: float = 10.0):
             "seconds_per_op": el / reps}
 
 
+def cpu_python_reference(workload: str, target_s: float = 6.0):
+    """The reference's own CPU path, pure Python on one core (oracle/pyport.py,
+    the same float64 arithmetic as tests/q4_reference.py:36-47): whole rows for
+    ~target_s, scaled to the workload's rows.  None for formats the reference's
+    Python has no code for (Q5_K, Q6_K)."""
+    import math
+
+    import oracle
+    from oracle import pyport
+    from mojo_llm_lab_b200 import fixtures as fx
+
+    wl = WORKLOADS[workload]
+    kind, rows, k = wl["kind"], wl["rows"], wl["k"]
+    if kind not in ("q4k", "gate_up"):
+        return None
+    sample_rows = min(rows, 512)
+    mats = [w.tobytes() for w in host_weights(kind, sample_rows, k, seed=1)]
+    act = oracle.quantize_q8_1(fx.seeded_activation(k, seed=2))
+    row_bytes = k // 256 * 144
+    done, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < target_s and done < sample_rows:
+        r = slice(done * row_bytes, (done + 1) * row_bytes)
+        vals = [pyport.dot_q4_q8(m[r], act) for m in mats]
+        if kind == "gate_up":
+            up, gate = vals
+            vals.append(up * (gate / (1.0 + math.exp(-gate))))
+        done += 1
+    el = time.perf_counter() - t0
+    per_op_s = el / done * rows
+    return {"value": algorithmic_bytes(kind, rows, k) / per_op_s / 1e9, "unit": "GB/s", "cores": 1,
+            "kind": "port", "seconds_per_op": per_op_s,
+            "sample": f"{done} of {rows} rows in {el:.1f} s, scaled to all rows (oracle/pyport.py: the "
+                      f"reference's pure-Python dot_q4_q8 arithmetic, 1 thread)"}
+
+
+def cpu_baselines(workload: str, target_s: float = 10.0) -> dict:
+    """The contract's cpu_baseline (the C port on all host threads) with the
+    other CPU arms beside it: the C port on 1 thread and the reference's own
+    pure-Python path on 1 thread."""
+    main = cpu_reference(workload, target_s=target_s)
+    line = {kk: main[kk] for kk in ("value", "unit", "cores", "kind", "sample")}
+    others = []
+    one = cpu_reference(workload, target_s=min(4.0, target_s), threads=1)
+    others.append({kk: one[kk] for kk in ("value", "unit", "cores", "kind", "sample")})
+    py = cpu_python_reference(workload)
+    if py is not None:
+        others.append({kk: py[kk] for kk in ("value", "unit", "cores", "kind", "sample")})
+    line["others"] = others
+    line["host"] = host_cpu()
+    return line
+
+
+def host_cpu() -> str:
+    try:
+        for ln in Path("/proc/cpuinfo").read_text().splitlines():
+            if ln.startswith("model name"):
+                return f"{ln.split(':', 1)[1].strip()} ({os.cpu_count()} threads)"
+    except OSError:
+        pass
+    return f"{os.cpu_count()} threads"
+
+
+def matvec_config(workload: str, world: int, pdl: bool, copies: int = 0) -> dict:
+    """The config dict of a matvec workload, the same in both arms."""
+    wl = WORKLOADS[workload]
+    kind, rows, k = wl["kind"], wl["rows"], wl["k"]
+    sharded = kind in ("gate_up", "q6k") and world > 1
+    my_rows = rows // world if sharded else rows
+    wbytes = weight_bytes(kind, my_rows, k)
+    copies = copies or max(2, -(-int(2.2 * L2_BYTES) // wbytes))
+    return {"workload": describe(workload), "rows": rows, "k": k, "launches_per_step": copies,
+            "bytes_per_op": algorithmic_bytes(kind, rows, k),
+            "l2": f"{copies} distinct weight copies ({copies * wbytes / 2**20:.0f} MiB per GPU) > 2x L2 per step; "
+                  f"no flush",
+            "parallelism": (f"rows/{world} per rank + NCCL all-gather" if sharded else
+                            (f"replicas x{world}" if world > 1 else "single GPU")),
+            "pdl": pdl}
+
+
 def run_reference(args, rank: int, world: int):
     if rank != 0:
         return
-    wl = WORKLOADS[args.workload]
     ref = cpu_reference(args.workload, target_s=max(3.0, min(30.0, 1.5 * args.steps)))
+    base = cpu_baselines(args.workload, target_s=3.0)
+    base.update({kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")})
     line = {"metric": f"{describe(args.workload)} HBM GB/s", "value": round(ref["value"], 4), "unit": "GB/s",
             "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": ref["seconds_per_op"] * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "int8 dot / f64 sum", "data": "synthetic (seeded)",
-            "config": {"workload": describe(args.workload), "rows": wl["rows"], "k": wl["k"]},
-            "cpu_baseline": {kk: ref[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "vs_baseline": None, "dtype": "u8/s8 dp4a, f64 accumulate",
+            "data": "synthetic (seeded; the reference benchmark's value distributions)",
+            "config": matvec_config(args.workload, world, not args.no_pdl, args.copies),
+            "cpu_baseline": base,
             "e2e": {"value": round(ref["value"], 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -353,14 +437,14 @@ def run_ours(args, rank: int, world: int):
     torch.cuda.synchronize()
 
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    # ~0.5 s of the same load before the timed region (untimed) so that the
+    # ~1 s of the same load before the timed region (untimed) so that the
     # clock samples describe it; every rank replays the same number of times
     # (the graph may hold collectives).
     t0 = time.perf_counter()
     for _ in range(3):
         graph.replay()
     torch.cuda.synchronize()
-    n_load = max(1, int(0.5 / max((time.perf_counter() - t0) / 3, 1e-6)))
+    n_load = max(1, int(1.0 / max((time.perf_counter() - t0) / 3, 1e-6)))
     if world > 1:
         t = torch.tensor([n_load], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -493,20 +577,15 @@ def run_ours(args, rank: int, world: int):
 
     if rank == 0:
         peak, peak_kind = measured_peak()
-        cpu = None if args.no_cpu_baseline or world > 1 else cpu_reference(args.workload, target_s=10.0)
+        cpu = None if args.no_cpu_baseline or world > 1 else cpu_baselines(args.workload, target_s=10.0)
         clk = clocks.summary()
         line = {
             "metric": f"{describe(args.workload)} HBM GB/s", "value": round(value, 2), "unit": "GB/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6),
             "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
             "dtype": "u8/s8 dp4a, f64 accumulate", "data": "synthetic (seeded; the reference benchmark's value distributions)",
-            "config": {"workload": describe(args.workload), "rows": rows, "k": k, "launches_per_step": copies,
-                       "bytes_per_op": per_op, "us_per_op": round(ms * 1e3 / copies, 4),
-                       "l2": f"{copies} distinct weight copies ({copies * wbytes / 2**20:.0f} MiB per GPU) "
-                             f"> 2x L2 per step; no flush",
-                       "parallelism": (f"rows/{world} per rank + NCCL all-gather" if sharded else
-                                       (f"replicas x{world}" if world > 1 else "single GPU")),
-                       "pdl": pdl},
+            "config": matvec_config(args.workload, world, pdl, args.copies),
+            "us_per_op": round(ms * 1e3 / copies, 4),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": copies * k * 4,
                     "d2h_bytes_per_step": int(result.numel() * 4), "ms_per_step": round(e_ms, 6),
                     "path": "ops.quantize_q8_1 over a chunk's activations, then ops.<matvec> per launch "
@@ -516,7 +595,7 @@ def run_ours(args, rank: int, world: int):
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
                          "traffic": profiled_traffic(wl["profile"]), "kernel": wl["kernel"],
                          "us_per_launch": round(launch_ms * 1e3, 4)},
-            "cpu_baseline": None if cpu is None else {kk: cpu[kk] for kk in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": cpu,
             "clocks": clk,
             "gpu_launches": args.steps * copies,
         }
@@ -1400,6 +1479,178 @@ def run_imrope(args, rank: int, world: int, batched: bool):
     print(json.dumps(line), flush=True)
 
 
+# ----------------------------------------------------------------------------- Q8_1 quantiser workloads
+
+Q8_1_TOKENS_BATCHED = 4096
+
+
+def q8_1_bytes_per_op(k: int, tokens: int = 1) -> int:
+    """fp32 read + Q8_1 write (36 bytes per 32 values)."""
+    return tokens * (k * 4 + k // 32 * 36)
+
+
+def q8_1_cpu_reference(k: int, target_s: float = 3.0):
+    import oracle
+    from mojo_llm_lab_b200 import fixtures as fx
+
+    x = fx.seeded_activation(k, seed=3)
+    reps, t0 = 0, time.perf_counter()
+    while time.perf_counter() - t0 < target_s:
+        oracle.quantize_q8_1(x)
+        reps += 1
+    el = time.perf_counter() - t0
+    return {"per_op_s": el / reps, "cores": 1, "kind": "port",
+            "sample": f"{reps} x quantise fp32[{k}] in {el:.1f} s (oracle/oracle.c orc_q8_1_quantize, 1 thread)"}
+
+
+def q8_1_describe(batched: bool, k: int) -> str:
+    return (f"Q8_1 quantiser {Q8_1_TOKENS_BATCHED} tokens x {k}" if batched else f"Q8_1 quantiser fp32[{k}]")
+
+
+def run_q8_1_reference(args, rank: int, world: int, batched: bool):
+    if rank != 0:
+        return
+    k = args.k
+    c = q8_1_cpu_reference(k, target_s=max(3.0, min(20.0, args.steps)))
+    if batched:
+        value, unit, hib = q8_1_bytes_per_op(k) / c["per_op_s"] / 1e9, "GB/s", True
+    else:
+        value, unit, hib = c["per_op_s"] * 1e6, "us/op", False
+    line = {"metric": f"{q8_1_describe(batched, k)} {unit}", "value": round(value, 4), "unit": unit,
+            "impl": "reference", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": c["per_op_s"] * 1e3, "higher_is_better": hib, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32 -> s8 + f16", "data": "synthetic (seeded N(0,1))",
+            "config": q8_1_config(batched, k, world),
+            "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": 1, "kind": "port",
+                             "sample": c["sample"]},
+            "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def q8_1_config(batched: bool, k: int, world: int) -> dict:
+    tokens = Q8_1_TOKENS_BATCHED if batched else 1
+    copies = 6 if batched else 128
+    return {"workload": q8_1_describe(batched, k), "k": k, "tokens": tokens, "launches_per_step": copies,
+            "bytes_per_op": q8_1_bytes_per_op(k, tokens),
+            "l2": (f"{copies} inputs x {tokens * k * 4 / 2**20:.0f} MiB > 2x L2; no flush" if batched else
+                   f"{copies} distinct {k * 4 // 1024} KB inputs (L2-resident, as a decode step's activations)"),
+            "chain": "PDL-chained launches in one CUDA graph",
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
+
+def run_q8_1(args, rank: int, world: int, batched: bool):
+    """The activation quantiser alone: one fp32 vector of k (latency: us/op over
+    128 PDL-chained launches on distinct inputs) or 4096 such vectors in one
+    launch (HBM throughput mode)."""
+    import torch
+    import torch.distributed as dist
+
+    import ctypes as C
+    from mojo_llm_lab_b200 import ops
+    from mojo_llm_lab_b200._lib import LAUNCH_PDL, S_D_SUMQ, check, lib
+
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    k = args.k
+    tokens = Q8_1_TOKENS_BATCHED if batched else 1
+    cfg = q8_1_config(batched, k, world)
+    copies = cfg["launches_per_step"]
+    stream = torch.cuda.Stream(device)
+    torch.cuda.set_stream(stream)
+    gen = torch.Generator(device=device)
+    gen.manual_seed(7)
+    xs = torch.randn(copies, tokens * k, generator=gen, device=device)
+    outs = torch.empty(copies, tokens * k // 32 * 36, dtype=torch.uint8, device=device)
+    lib_ = lib()
+
+    def launch(i, pdl=True):
+        check(lib_.mllb_q8_1_quantize_ex(xs[i].data_ptr(), outs[i].data_ptr(), tokens * k, S_D_SUMQ,
+                                         LAUNCH_PDL if pdl else 0, C.c_void_p(stream.cuda_stream)), "q8_1")
+
+    if not args.skip_check:
+        import oracle
+        launch(0, pdl=False)
+        torch.cuda.synchronize()
+        x0 = xs[0][: min(tokens * k, 1 << 20)].cpu().numpy()
+        if outs[0][: x0.size // 32 * 36].cpu().numpy().tobytes() != oracle.quantize_q8_1(x0):
+            raise SystemExit("Q8_1 correctness gate failed: bytes differ from the oracle")
+    for i in range(copies):
+        launch(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(copies):
+            launch(i)
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        preroll(graph)
+        start.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        stop.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(stop) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    us_op = ms * 1e3 / copies
+    per_op = q8_1_bytes_per_op(k, tokens)
+    gbs = per_op / (us_op * 1e-6) / 1e9
+
+    # e2e through the public API with host buffers: pinned H2D of x, the
+    # quantiser, D2H of the Q8_1 bytes, one op per step, eager.
+    x_pin = xs[0].cpu().pin_memory()
+    o_pin = torch.empty(outs.shape[1], dtype=torch.uint8).pin_memory()
+    x_stage = torch.empty_like(xs[0])
+    e_times = []
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t1 = time.perf_counter()
+        x_stage.copy_(x_pin, non_blocking=True)
+        ops.quantize_q8_1(x_stage, outs[0])
+        o_pin.copy_(outs[0], non_blocking=True)
+        torch.cuda.synchronize()
+        if i >= args.warmup:
+            e_times.append(time.perf_counter() - t1)
+    e_us = statistics.median(e_times) * 1e6
+    if ops.device_error():
+        raise SystemExit("device error word set")
+    del graph
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    cpu = None
+    if not args.no_cpu_baseline and world == 1:
+        c = q8_1_cpu_reference(k)
+        cpu = ({"value": round(q8_1_bytes_per_op(k) / c["per_op_s"] / 1e9, 4), "unit": "GB/s", "cores": 1,
+                "kind": "port", "sample": c["sample"]} if batched else
+               {"value": round(c["per_op_s"] * 1e6, 3), "unit": "us/op", "cores": 1, "kind": "port",
+                "sample": c["sample"]})
+    if batched:
+        value, unit, hib = round(gbs, 2), "GB/s", True
+        e2e = {"value": round(per_op / (e_us * 1e-6) / 1e9, 2), "unit": "GB/s"}
+    else:
+        value, unit, hib = round(us_op, 4), "us/op", False
+        e2e = {"value": round(e_us, 3), "unit": "us/op"}
+    e2e.update({"h2d_bytes_per_step": tokens * k * 4, "d2h_bytes_per_step": tokens * k // 32 * 36,
+                "path": "ops.quantize_q8_1 with pinned H2D/D2H, eager, one op per step"})
+    cfg["us_per_op"] = round(us_op, 4)
+    line = {"metric": f"{q8_1_describe(batched, k)} {unit}", "value": value, "unit": unit, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32 -> s8 + f16", "data": "synthetic (seeded N(0,1))",
+            "config": cfg, "e2e": e2e,
+            "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
+                         "frac": round(gbs / peak, 5), "peak_source": peak_kind, "traffic": None,
+                         "kernel": "q8_1_quantize_kernel", "us_per_launch": round(us_op, 4)},
+            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -1407,13 +1658,14 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS) + ["decode", "imrope", "imrope_batched", "prefill",
-                                                               "attention"],
+                                                               "attention", "q8_1", "q8_1_batched"],
                     default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
     ap.add_argument("--context", type=int, default=4096, help="decode: prefilled KV rows")
     ap.add_argument("--kv", choices=["f16", "q4_0"], default="f16",
                     help="decode: KV cache type (q4_0: GGML Q4_0, the reference's llama.cpp setting)")
     ap.add_argument("--copies", type=int, default=0)
+    ap.add_argument("--k", type=int, default=2560, help="q8_1 workloads: values per activation vector")
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1432,12 +1684,16 @@ def main():
             run_attention_reference(args, rank, world)
         elif args.workload.startswith("imrope"):
             run_imrope_reference(args, rank, world, batched=args.workload == "imrope_batched")
+        elif args.workload.startswith("q8_1"):
+            run_q8_1_reference(args, rank, world, batched=args.workload == "q8_1_batched")
         else:
             run_reference(args, rank, world)
         return
     runner = {"decode": run_decode, "prefill": run_prefill, "attention": run_attention,
               "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
-              "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True)}.get(args.workload, run_ours)
+              "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True),
+              "q8_1": lambda a, r, w: run_q8_1(a, r, w, batched=False),
+              "q8_1_batched": lambda a, r, w: run_q8_1(a, r, w, batched=True)}.get(args.workload, run_ours)
     if world > 1:
         import datetime
 

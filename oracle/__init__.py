@@ -17,14 +17,19 @@ wrappers whose names follow the reference:
 * ``position_axis``                    tests/reference_math.py:11-19
 * ``quantize_q8_1``                    GGML quantize_q8_1 semantics captured at
                                        benchmark/q4_compare.c:328-357
-* ``q6k_matvec``                       public GGML Q6_K layout (parity unpinned:
-                                       the reference has no Q6_K oracle)
-* ``q5k_matvec``                       public GGML Q5_K layout (parity unpinned:
-                                       the reference has no Q5_K code)
+* ``q6k_matvec``                       public GGML Q6_K layout (the reference has
+                                       no Q6_K oracle; pinned to llama.cpp's
+                                       gguf-py 0.19.0 Q6_K.dequantize_blocks in
+                                       tests/test_gguf_pin_cpu.py)
+* ``q5k_matvec``                       public GGML Q5_K layout (no reference
+                                       code; pinned to gguf-py Q5_K likewise)
 * ``quantize_q4_0`` / ``kv_q4_0_rows`` GGML quantize_row_q4_0 for the Q4_0 KV
                                        cache the reference's contexts use
                                        (integration/resident_decode.cpp:70);
-                                       parity unpinned (no reference Q4_0 code)
+                                       pinned to gguf-py Q4_0.quantize_blocks
+* ``pyport``                           pure-Python restatement of the reference's
+                                       Python oracles, for the single-thread
+                                       Python CPU baseline only
 * ``attention`` / ``attention_q4_0``   float64 softmax attention over an fp16 or
                                        a Q4_0 cache
 """

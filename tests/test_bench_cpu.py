@@ -28,6 +28,8 @@ def run_bench(args, env_extra=None):
     (["--workload", "attention", "--kv", "q4_0"], "GB/s"),
     (["--workload", "imrope"], "us/op"),
     (["--workload", "prefill"], "int8 TOP/s"),
+    (["--workload", "q8_1"], "us/op"),
+    (["--workload", "q8_1_batched"], "GB/s"),
 ])
 def test_reference_arm_prints_the_contract_line(args, unit):
     lines = run_bench(args)
@@ -48,3 +50,16 @@ def test_reference_arm_prints_the_contract_line(args, unit):
 
 def test_reference_arm_prints_on_rank_zero_only():
     assert run_bench(["--workload", "attention"], {"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"}) == []
+
+
+def test_reference_arm_reports_every_cpu_arm_and_the_gpu_arms_config():
+    """Default workload: the C port on all threads (the contract's value), the
+    C port on 1 thread and the pure-Python path on 1 thread beside it; the
+    config dict is the one the GPU arm prints."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    line = run_bench([])[0]
+    others = line["cpu_baseline"]["others"]
+    assert [o["cores"] for o in others] == [1, 1]
+    assert "pyport" in others[1]["sample"] and all(o["value"] > 0 for o in others)
+    assert line["config"] == bench.matvec_config("q4k_matvec", 1, True)

@@ -180,3 +180,30 @@ def test_q6k_decoder_layout(orc):
     assert v[96] == 0.5 * 7 * ((4 | 48) - 32)
     assert v[16] == 0.5 * 2 * (0 - 32)   # second sub-block scale for l >= 16
     assert v[128] == 0.5 * 9 * (0 - 32)  # second half uses scales 8..15
+
+
+# ------------------------------------------------ pure-Python port (CPU baseline)
+
+def test_python_port_dot_bit_exact_on_golden(golden):
+    from oracle import pyport
+    g = golden["q4_reference_fixtures"]["varied_factors"]
+    files = rfx.q4_matvec_fixtures(**g["options"])
+    w, a = files["weights.bin"], files["activations.bin"]
+    row = 10 * 144
+    got = [pyport.dot_q4_q8(w[r * row:(r + 1) * row], a) for r in range(8)]
+    assert got == g["dot_weights"][:8]
+    s = golden["q4_seeded"]
+    w = fx.seeded_q4k_matrix(s["rows"], s["k"], seed=s["weight_seed"])
+    import oracle
+    a = oracle.quantize_q8_1(fx.seeded_activation(s["k"], seed=s["activation_seed"]))
+    row = s["k"] // 256 * 144
+    assert [pyport.dot_q4_q8(w[r * row:(r + 1) * row].tobytes(), a) for r in range(4)] == s["dot"][:4]
+
+
+def test_python_port_head_bit_exact_on_golden(golden):
+    from oracle import pyport
+    g = golden["imrope_reference_fixtures"]["long_position"]
+    q, gamma, positions = fx.parse_imrope(fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"])))
+    q64, g64 = q.astype(np.float64), gamma.astype(np.float64).tolist()
+    assert pyport.reference_head(q64[0].tolist(), g64, positions.tolist()) == g["head0"]
+    assert pyport.reference_head(q64[31].tolist(), g64, positions.tolist()) == g["head31"]
