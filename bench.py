@@ -252,7 +252,7 @@ def cpu_python_reference(workload: str, target_s: float = 6.0):
     kind, rows, k = wl["kind"], wl["rows"], wl["k"]
     if kind not in ("q4k", "gate_up"):
         return None
-    sample_rows = min(rows, 512)
+    sample_rows = rows
     mats = [w.tobytes() for w in host_weights(kind, sample_rows, k, seed=1)]
     act = oracle.quantize_q8_1(fx.seeded_activation(k, seed=2))
     row_bytes = k // 256 * 144
@@ -599,7 +599,7 @@ def run_ours(args, rank: int, world: int):
             "clocks": clk,
             "gpu_launches": args.steps * copies,
         }
-        print(json.dumps(line), flush=True)
+        return line
 
 
 # ----------------------------------------------------------------------------- prefill workload
@@ -782,7 +782,7 @@ def run_prefill(args, rank: int, world: int):
             "clocks": clocks.summary(),
             "gpu_launches": args.steps * copies,
         }
-        print(json.dumps(line), flush=True)
+        return line
 
 
 # ----------------------------------------------------------------------------- attention workload
@@ -1042,7 +1042,7 @@ def run_attention(args, rank: int, world: int):
                          "note": "issue-bound: fp64 arithmetic on converted cache values, not HBM"},
             "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies * 2,
         }
-        print(json.dumps(line), flush=True)
+        return line
 
 
 # ----------------------------------------------------------------------------- decode workload
@@ -1271,7 +1271,7 @@ def run_decode(args, rank: int, world: int):
             "clocks": clocks.summary(),
             "gpu_launches": args.steps * DECODE_TOKENS * launches,
         }
-        print(json.dumps(line), flush=True)
+        return line
 
 
 # ----------------------------------------------------------------------------- IMROPE workloads
@@ -1348,9 +1348,12 @@ def run_imrope(args, rank: int, world: int, batched: bool):
 
     def launch(i, pdl=True):
         # PDL-chained through the batched entry (theta from device memory, as
-        # the reference ABI passes it); pdl=False is the reference entry.
+        # the reference ABI passes it; gamma / positions / theta, which no
+        # kernel of the chain writes, read before the dependency wait);
+        # pdl=False is the reference entry.
         if batched or pdl:
-            ops.rmsnorm_imrope_q(qs[i], gamma, pos, theta, out=outs[i], heads_per_token=heads, pdl=pdl)
+            ops.rmsnorm_imrope_q(qs[i], gamma, pos, theta, out=outs[i], heads_per_token=heads, pdl=pdl,
+                                 const_aux=pdl)
         else:
             ops.fused_q_imrope_runtime_fastpow(qs[i], gamma, pos, outs[i], theta)
 
@@ -1473,10 +1476,11 @@ def run_imrope(args, rank: int, world: int, batched: bool):
                        "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
             "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 5), "peak_source": peak_kind, "traffic": None,
+                         "frac": round(gbs / peak, 5), "peak_source": peak_kind,
+                         "traffic": profiled_traffic("imrope_q_32x128_and_4096_tokens") if batched else None,
                          "kernel": "imrope_q_kernel", "us_per_launch": round(us_op, 4)},
             "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 # ----------------------------------------------------------------------------- Q8_1 quantiser workloads
@@ -1645,10 +1649,11 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 -> s8 + f16", "data": "synthetic (seeded N(0,1))",
             "config": cfg, "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(gbs / peak, 5), "peak_source": peak_kind, "traffic": None,
-                         "kernel": "q8_1_quantize_kernel", "us_per_launch": round(us_op, 4)},
+                         "frac": round(gbs / peak, 5), "peak_source": peak_kind,
+                         "traffic": profiled_traffic("q8_1_quantize_k2560_and_4096x2560") if batched else None,
+                         "kernel": "q8_1_quantize_x4_kernel", "us_per_launch": round(us_op, 4)},
             "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def main():
@@ -1669,6 +1674,8 @@ def main():
     ap.add_argument("--no-pdl", action="store_true")
     ap.add_argument("--skip-check", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--headline-only", action="store_true",
+                    help="default workload: skip the other configurations measured after the headline")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -1703,11 +1710,47 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         try:
-            runner(args, rank, world)
+            line = runner(args, rank, world)
         finally:
             dist.destroy_process_group()
     else:
-        runner(args, rank, world)
+        line = runner(args, rank, world)
+        if line is not None and args.workload == "q4k_matvec" and not args.headline_only:
+            line["other_configs"] = other_configs(args, rank, world)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+
+
+# The other benchmark configurations, measured in the same run as the headline
+# (one GPU): each entry is that workload's own line, trimmed.
+OTHER_CONFIGS = (("imrope", {}), ("imrope_batched", {}), ("q8_1", {}), ("gate_up", {}), ("q6k_vocab", {}),
+                 ("decode", {"steps": 3, "warmup": 3}))
+
+
+def other_configs(args, rank: int, world: int) -> dict:
+    import gc
+
+    import torch
+    runners = {"decode": run_decode, "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
+               "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True),
+               "q8_1": lambda a, r, w: run_q8_1(a, r, w, batched=False)}
+    keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "vs_baseline", "dtype",
+            "config", "e2e", "roofline", "clocks", "gpu_launches", "us_per_op")
+    out = {}
+    for name, over in OTHER_CONFIGS:
+        sub = argparse.Namespace(**vars(args))
+        sub.workload, sub.no_cpu_baseline, sub.copies = name, True, 0
+        sub.steps, sub.warmup = over.get("steps", args.steps), over.get("warmup", args.warmup)
+        t0 = time.perf_counter()
+        try:
+            line = runners.get(name, run_ours)(sub, rank, world)
+            out[name] = {kk: line[kk] for kk in keep if kk in line}
+        except SystemExit as e:  # a failed correctness gate: recorded, the headline stands
+            out[name] = {"error": str(e)}
+        out[name]["wall_s"] = round(time.perf_counter() - t0, 1)
+        gc.collect()
+        torch.cuda.empty_cache()
+    return out
 
 
 if __name__ == "__main__":

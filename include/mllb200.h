@@ -51,6 +51,15 @@ extern "C" {
  */
 #define MLLB_LAUNCH_PDL 1u
 
+/*
+ * MLLB_LAUNCH_CONST_AUX (IMROPE entries, with MLLB_LAUNCH_PDL): gamma, the
+ * positions and the theta scale are not written by the preceding kernel (they
+ * are set by the host or by an earlier, finished kernel), so the kernel reads
+ * them and builds its 64 fp64 rotations before the dependency wait; only q is
+ * read after it.  The weights rule of MLLB_LAUNCH_PDL, for these operands.
+ */
+#define MLLB_LAUNCH_CONST_AUX 2u
+
 /* Q8_1 `s` field convention (the dot products never read s). */
 #define MLLB_Q8_1_S_D_SUMQ 0 /* s = fp16(fp16(d) * sum(q)): tools/generate_q4_matvec_fixtures.py:59 */
 #define MLLB_Q8_1_S_SUM_X 1  /* s = fp16(sum(x)): GGML quantize_q8_1 */
@@ -153,7 +162,8 @@ int mllb_rmsnorm_imrope_q_batched(const float *q, const float *gamma, const int3
                                   const float *theta_scale, double theta_value, float *out, int64_t tokens,
                                   int64_t heads_per_token, void *stream);
 /* Same, with launch flags (MLLB_LAUNCH_PDL: the kernel may start while the
- * preceding kernel runs; it waits for it before reading anything). */
+ * preceding kernel runs; it waits for it before reading anything, or, with
+ * MLLB_LAUNCH_CONST_AUX too, before reading q). */
 int mllb_rmsnorm_imrope_q_batched_ex(const float *q, const float *gamma, const int32_t *positions,
                                      const float *theta_scale, double theta_value, float *out, int64_t tokens,
                                      int64_t heads_per_token, unsigned flags, void *stream);
@@ -311,6 +321,25 @@ typedef struct mllb_peer_gather {
 
 int mllb_q8_1_quantize_allgather(const float *x, int64_t k, const mllb_peer_gather *peers, unsigned flags,
                                  void *stream);
+
+/*
+ * mllb_q4k_gate_up_q8 for one rank of a row-sharded gate/up (n = this rank's
+ * rows, a multiple of 32) with the all-gather built in: each completed
+ * 32-row group's Q8_1 block of the product goes straight into every rank's
+ * buffer (peers->buffers[r] + (rank * n / 32 + group) * 36, NVLink stores),
+ * each CTA then arrives on every rank's counter for this rank, and the launch
+ * completes only when every rank's blocks are in this GPU's buffer (a rank
+ * that does not arrive within ~1 s sets device error bit 6, mask 0x40).  So
+ * the down projection, launched next, reads the whole product's Q8_1 from
+ * peers->buffers[rank].  counters: n / 32 zeroed uint32, left zero.  peers as
+ * for mllb_q8_1_quantize_allgather; every rank issues the same sequence of
+ * these launches with the same n and k.  One launch in place of the gate/up
+ * launch plus mllb_q8_1_quantize_allgather.  No reference counterpart (the
+ * reference runs on one GPU).
+ */
+int mllb_q4k_gate_up_q8_gather(const void *up_weights, const void *gate_weights, const void *q8, float *up,
+                               float *gate, float *prod, uint32_t *counters, int64_t n, int64_t k,
+                               const mllb_peer_gather *peers, unsigned flags, void *stream);
 
 /*
  * Bring bytes [data, data + bytes) into L2 ahead of their use, marked

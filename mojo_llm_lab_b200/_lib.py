@@ -22,6 +22,7 @@ MLLB_ECUDA = -3
 MLLB_EUNSUPPORTED = -4
 
 LAUNCH_PDL = 1
+LAUNCH_CONST_AUX = 2  # IMROPE: gamma / positions / theta not written by the preceding kernel
 
 S_D_SUMQ = 0
 S_SUM_X = 1
@@ -81,6 +82,8 @@ SIGNATURES = {
                                                  _I64, _I64, C.c_uint, _P]),
     "mllb_argmax_f32": (C.c_int, [_P, _I64, _I64, _P, C.c_uint, _P]),
     "mllb_q8_1_quantize_allgather": (C.c_int, [_P, _I64, C.POINTER(PeerGather), C.c_uint, _P]),
+    "mllb_q4k_gate_up_q8_gather": (C.c_int, [_P, _P, _P, _P, _P, _P, _P, _I64, _I64, C.POINTER(PeerGather),
+                                             C.c_uint, _P]),
     "mllb_prefetch_l2": (C.c_int, [_P, _I64, _P]),
     "mllb_q5k_matvec": (C.c_int, [_P, _P, _P, _I64, _I64, _P]),
     "mllb_q5k_matvec_ex": (C.c_int, [_P, _P, _P, _I64, _I64, C.c_uint, _P]),

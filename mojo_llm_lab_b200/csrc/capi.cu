@@ -19,6 +19,7 @@
 #include "stream.cuh"
 #include "decode.cuh"
 #include "prefill.cuh"
+#include "resident.cuh"
 
 // Streaming-kernel configurations: V (row groups per tile), S (stages),
 // TEAMS (consumer teams per CTA) per format, matrices and K/256.  Each can
@@ -124,6 +125,9 @@ int launched(cudaError_t e, const char* what) {
 }
 
 bool known_flags(unsigned flags) { return (flags & ~static_cast<unsigned>(MLLB_LAUNCH_PDL)) == 0; }
+bool known_flags_aux(unsigned flags) {
+  return (flags & ~static_cast<unsigned>(MLLB_LAUNCH_PDL | MLLB_LAUNCH_CONST_AUX)) == 0;
+}
 
 bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) & (a - 1)) == 0; }
 
@@ -274,10 +278,10 @@ int q4k_team(const uint8_t* w0, const uint8_t* w1, const mllb::ActSource& src, f
 
 // Q4_K gate/up streaming launch with the Q8_1 of the product fused in
 // (Q8_1 activation).
+template <int E = mllb::kEpiQuantProduct>
 int q4k_gate_up_q8_team(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
                         int64_t n, int64_t k, cudaStream_t stream, bool pdl, const mllb::Epilogue& epi) {
   using F = mllb::Q4kFormat;
-  constexpr int E = mllb::kEpiQuantProduct;
   const mllb::ActSource src = q8_source(q8);
   const int rows = static_cast<int>(n);
   switch (k / 256) {
@@ -314,8 +318,56 @@ int q4k_norm_team(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, in
   return fail(MLLB_EUNSUPPORTED, "no streaming configuration for K=%lld", static_cast<long long>(k));
 }
 
+// Resident-weights path (csrc/resident.cuh): a plain Q4_K matvec of at most
+// 32 rows per SM with K = 2560 or 4096 runs with all its weights in shared
+// memory, brought in before the dependency wait.  MLLB_EUNSUPPORTED (nothing
+// launched) for other shapes.  MLLB_Q4K_RESIDENT=0 turns it off (the
+// streaming kernels then take every shape).
+template <int NB>
+int launch_resident(int dev, const uint8_t* w, const uint8_t* q8, float* out, int rows, int per_cta,
+                    cudaStream_t stream, bool pdl) {
+  auto kernel = mllb::resident_q4k_kernel<NB>;
+  static std::once_flag once[kMaxDevices];
+  static cudaError_t attr_err[kMaxDevices];
+  std::call_once(once[dev], [&] {
+    attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         mllb::kResidentMaxRowsPerCta * NB * mllb::kQ4kBlockBytes);
+  });
+  if (attr_err[dev] != cudaSuccess)
+    return fail(MLLB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err[dev]));
+  const int grid = (rows + per_cta - 1) / per_cta;
+  const int threads = 32 * ((per_cta + 1) / 2);
+  const size_t smem = static_cast<size_t>(per_cta) * NB * mllb::kQ4kBlockBytes;
+  return launched(launch(kernel, dim3(grid), dim3(threads), smem, stream, pdl, w, q8, out, rows, per_cta),
+                  "resident Q4_K matvec kernel");
+}
+
+int q4k_resident(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int64_t k, cudaStream_t stream,
+                 bool pdl) {
+  static const bool enabled = [] {
+    const char* env = getenv("MLLB_Q4K_RESIDENT");
+    return !(env && env[0] == '0');
+  }();
+  if (!enabled) return MLLB_EUNSUPPORTED;
+  int dev, rc;
+  if ((rc = current_device(&dev))) return rc;
+  const int sms = sm_count(dev);
+  if (n > static_cast<int64_t>(sms) * mllb::kResidentMaxRowsPerCta) return MLLB_EUNSUPPORTED;
+  const int rows = static_cast<int>(n);
+  const int per_cta = (rows + sms - 1) / sms;
+  switch (k / 256) {
+    case 10: return launch_resident<10>(dev, w, q8, out, rows, per_cta, stream, pdl);
+    case 16: return launch_resident<16>(dev, w, q8, out, rows, per_cta, stream, pdl);
+    default: return MLLB_EUNSUPPORTED;
+  }
+}
+
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
                  int64_t n, int64_t k, cudaStream_t stream, bool pdl) {
+  if (w1 == nullptr) {
+    const int rr = q4k_resident(w0, q8, o0, n, k, stream, pdl);
+    if (rr != MLLB_EUNSUPPORTED) return rr;
+  }
   const int rc = q4k_team(w0, w1, q8_source(q8), o0, o1, o2, n, k, stream, pdl);
   if (rc != MLLB_EUNSUPPORTED) return rc;
   // The row kernel reads its weights only after the preceding kernel is done,
@@ -401,6 +453,14 @@ int mllb_q8_1_quantize_ex(const float* x, void* q8, int64_t k, int s_mode, unsig
   if (s_mode != MLLB_Q8_1_S_D_SUMQ && s_mode != MLLB_Q8_1_S_SUM_X) return fail(MLLB_EINVAL, "unknown s_mode %d", s_mode);
   if (!aligned(x, 4) || !aligned(q8, 4)) return fail(MLLB_EALIGN, "x and q8 must be 4-byte aligned");
   const int64_t blocks = k / 32;
+  if (aligned(x, 16)) {  // four values per lane (one 16-byte load each)
+    int64_t grid = (blocks + 31) / 32;
+    if (grid > 65535) grid = 65535;
+    return launched(launch(mllb::q8_1_quantize_x4_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
+                           static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, x, static_cast<uint8_t*>(q8),
+                           blocks, s_mode),
+                    "q8_1 quantize kernel");
+  }
   int64_t grid = (blocks + 7) / 8;
   if (grid > 65535) grid = 65535;
   return launched(launch(mllb::q8_1_quantize_kernel, dim3(static_cast<unsigned>(grid)), dim3(256), 0,
@@ -493,7 +553,7 @@ int mllb_rmsnorm_imrope_q_batched_ex(const float* q, const float* gamma, const i
                                      const float* theta_scale, double theta_value, float* out, int64_t tokens,
                                      int64_t heads_per_token, unsigned flags, void* stream) {
   if (!q || !gamma || !positions || !out) return fail(MLLB_EINVAL, "null pointer");
-  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  if (!known_flags_aux(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
   if (tokens <= 0 || heads_per_token <= 0) return fail(MLLB_EINVAL, "empty shape");
   if (!aligned(q, 4) || !aligned(gamma, 4) || !aligned(positions, 4) || !aligned(out, 4) ||
       (theta_scale && !aligned(theta_scale, 4)))
@@ -503,7 +563,8 @@ int mllb_rmsnorm_imrope_q_batched_ex(const float* q, const float* gamma, const i
   if (grid > 0x7fffffff) return fail(MLLB_EUNSUPPORTED, "too many heads");
   return launched(launch(mllb::imrope_q_kernel, dim3(static_cast<unsigned>(grid)), dim3(static_cast<unsigned>(per_cta * 32)),
                          0, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, q, gamma, positions,
-                         theta_scale, theta_value, out, tokens, heads_per_token),
+                         theta_scale, theta_value, out, tokens, heads_per_token,
+                         (flags & MLLB_LAUNCH_CONST_AUX) ? 1 : 0),
                   "imrope kernel");
 }
 
@@ -1016,6 +1077,38 @@ int mllb_q4k_gate_up_q8(const void* up_weights, const void* gate_weights, const 
   return q4k_gate_up_q8_team(static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
                              static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
                              flags & MLLB_LAUNCH_PDL, epi);
+}
+
+int mllb_q4k_gate_up_q8_gather(const void* up_weights, const void* gate_weights, const void* q8, float* up,
+                               float* gate, float* prod, uint32_t* counters, int64_t n, int64_t k,
+                               const mllb_peer_gather* peers, unsigned flags, void* stream) {
+  if (!up_weights || !gate_weights || !q8 || !prod || !counters || !peers || !peers->count)
+    return fail(MLLB_EINVAL, "null pointer");
+  if (!known_flags(flags)) return fail(MLLB_EINVAL, "unknown flags %#x", flags);
+  int rc = check_rows(n, k, 1 << 30);
+  if (rc) return rc;
+  if (n % 32) return fail(MLLB_EINVAL, "the product's Q8_1 needs a multiple of 32 rows");
+  if (peers->world < 1 || peers->world > mllb::kMaxPeers || peers->rank < 0 || peers->rank >= peers->world)
+    return fail(MLLB_EINVAL, "rank %d / world %d out of range", peers->rank, peers->world);
+  if (!aligned(up_weights, 16) || !aligned(gate_weights, 16) || !aligned(q8, 4) || !aligned(up, 4) ||
+      !aligned(gate, 4) || !aligned(prod, 4) || !aligned(counters, 4) || !aligned(peers->count, 4))
+    return fail(MLLB_EALIGN, "weights need 16-byte, the rest 4-byte alignment");
+  mllb::Epilogue epi = {};
+  epi.counters = counters;
+  epi.peer.rank = peers->rank;
+  epi.peer.world = peers->world;
+  for (int r = 0; r < peers->world; ++r) {
+    if (!peers->buffers[r] || !peers->flags[r]) return fail(MLLB_EINVAL, "null peer pointer for rank %d", r);
+    if (!aligned(peers->buffers[r], 4) || !aligned(peers->flags[r], 4))
+      return fail(MLLB_EALIGN, "peer buffers and counters must be 4-byte aligned");
+    epi.peer.buffers[r] = static_cast<uint8_t*>(peers->buffers[r]);
+    epi.peer.flags[r] = peers->flags[r];
+  }
+  epi.peer.count = peers->count;
+  return q4k_gate_up_q8_team<mllb::kEpiQuantProductPeer>(
+      static_cast<const uint8_t*>(up_weights), static_cast<const uint8_t*>(gate_weights),
+      static_cast<const uint8_t*>(q8), up, gate, prod, n, k, static_cast<cudaStream_t>(stream),
+      flags & MLLB_LAUNCH_PDL, epi);
 }
 
 int64_t mllb_q4k_matvec_norm_workspace(int64_t n, int64_t k) {

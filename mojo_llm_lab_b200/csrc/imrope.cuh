@@ -107,41 +107,52 @@ __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, co
   out[lane + 96] = static_cast<float>(o[3]);
 }
 
-// One CTA per (token, group of up to 32 heads), one warp per head (the
-// launcher sizes the CTA to min(heads per token, 32) warps).  Every head of a
-// token shares its 4 positions, so the CTA first builds the 64 rotations (one
-// fp64 pow + sincos per thread) and the warps then only normalise and rotate:
-// the fp64 table is built once per token, not once per few heads.  Head h belongs to token h / heads_per_token and
-// uses that token's 4 positions.  The theta scale comes from device memory
-// (fp32, the reference ABI) unless theta_ptr is null, in which case
-// theta_value is used.
-constexpr int kImropeMaxHeadsPerCta = 32;
+// One CTA per (token, group of up to 8 heads), one warp per head (the
+// launcher sizes the CTA to min(heads per token, 8) warps: small CTAs, so that
+// several per SM overlap their latency chains in the many-token form).  Every
+// head of a token shares its 4 positions, so the CTA first builds the 64
+// rotations (one fp64 pow + sincos per thread) and the warps then only
+// normalise and rotate.  Head h belongs to token h / heads_per_token and uses
+// that token's 4 positions.  The theta scale comes from device memory (fp32,
+// the reference ABI) unless theta_ptr is null, in which case theta_value is
+// used.  early_aux (MLLB_LAUNCH_CONST_AUX): positions, theta and gamma are not
+// written by the preceding kernel, so the rotation table (the pow / sincos
+// chain) and gamma are built and loaded before the dependency wait; only q
+// waits for the preceding kernel.
+constexpr int kImropeMaxHeadsPerCta = 8;
 
 __global__ void __launch_bounds__(kImropeMaxHeadsPerCta * 32) imrope_q_kernel(
     const float* __restrict__ q, const float* __restrict__ gamma, const int32_t* __restrict__ positions,
     const float* __restrict__ theta_ptr, double theta_value, float* __restrict__ out, int64_t tokens,
-    int64_t heads_per_token) {
+    int64_t heads_per_token, int early_aux) {
   __shared__ double2 rot[kHeadDim / 2];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads_per_cta = static_cast<int>(blockDim.x >> 5);
   const int64_t ctas_per_token = (heads_per_token + heads_per_cta - 1) / heads_per_cta;
   const int64_t token = blockIdx.x / ctas_per_token;
   const int64_t h = (blockIdx.x % ctas_per_token) * heads_per_cta + warp;
+  const bool active = token < tokens && h < heads_per_token;
+  const size_t head = static_cast<size_t>(token * heads_per_token + (active ? h : 0));
+  float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
+  auto build_table = [&] {
+    if (token < tokens) {
+      g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
+      for (int p = threadIdx.x; p < kHeadDim / 2; p += blockDim.x) {
+        const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
+        const int32_t* pos = positions + 4 * token;
+        rot[p] = imrope_rotation(p, pos[0], pos[1], pos[2], pos[3], theta);
+      }
+    }
+  };
+  if (early_aux) build_table();
   pdl_wait_prerequisite();
   pdl_launch_dependents();
   if (token >= tokens) return;
   // The head's values are loaded first, so their latency overlaps the
-  // rotation table's pow / sincos.
-  const bool active = h < heads_per_token;
-  const size_t head = static_cast<size_t>(token * heads_per_token + (active ? h : 0));
+  // rotation table's pow / sincos when that is built after the wait.
   const float* x = q + head * kHeadDim;
   const float x0 = x[lane], x1 = x[lane + 32], x2 = x[lane + 64], x3 = x[lane + 96];
-  const float g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
-  for (int p = threadIdx.x; p < kHeadDim / 2; p += blockDim.x) {
-    const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
-    const int32_t* pos = positions + 4 * token;
-    rot[p] = imrope_rotation(p, pos[0], pos[1], pos[2], pos[3], theta);
-  }
+  if (!early_aux) build_table();
   __syncthreads();
   if (!active) return;
   double o[4];

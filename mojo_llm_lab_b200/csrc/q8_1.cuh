@@ -79,6 +79,75 @@ __global__ void __launch_bounds__(256) q8_1_quantize_kernel(const float* __restr
   }
 }
 
+// Four values per lane: eight lanes per 32-value block, four blocks per warp
+// (one 16-byte load per lane; x must be 16-byte aligned).  The same
+// arithmetic as q8_1_quantize_lane -- max |x| with its NaN rule, IEEE
+// d = amax / 127 and x / d, roundf, fp16 RNE, s by either convention with
+// sum(x) in the same xor-butterfly association -- so the bytes are identical,
+// with the per-block work (the d division, the reductions, the packing)
+// shared by four values instead of repeated in every lane.
+__global__ void __launch_bounds__(256) q8_1_quantize_x4_kernel(const float* __restrict__ x, uint8_t* __restrict__ out,
+                                                               int64_t blocks, int s_mode) {
+  const int lane = threadIdx.x & 31, sub = lane & 7;
+  pdl_wait_prerequisite();
+  pdl_launch_dependents();
+  const int64_t step = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5) * 4;
+  for (int64_t g0 = (static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5)) * 4; g0 < blocks;
+       g0 += step) {
+    const int64_t g = g0 + (lane >> 3);
+    const bool live = g < blocks;
+    const float4 v4 = live ? reinterpret_cast<const float4*>(x)[g * 8 + sub] : make_float4(0.f, 0.f, 0.f, 0.f);
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+    uint32_t mbits = 0u;
+    bool all_nan = true;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float a = fabsf(v[i]);
+      const bool nan = a != a;
+      mbits = max(mbits, nan ? 0u : __float_as_uint(a));
+      all_nan = all_nan && nan;
+    }
+    uint32_t every_nan = all_nan ? 1u : 0u;
+#pragma unroll
+    for (int off = 4; off >= 1; off >>= 1) {
+      mbits = max(mbits, __shfl_xor_sync(0xffffffffu, mbits, off));
+      every_nan &= __shfl_xor_sync(0xffffffffu, every_nan, off);
+    }
+    const float amax = every_nan ? fabsf(v[0]) : __uint_as_float(mbits);
+    const float d = __fdiv_rn(amax, 127.0f);
+    int q[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) q[i] = amax == 0.0f ? 0 : static_cast<int>(roundf(__fdiv_rn(v[i], d)));
+    const __half dh = __float2half_rn(d);
+    float s;
+    if (s_mode == kQ8SumX) {
+      // xor-butterfly over the block's 32 values (offsets 16, 8, 4 across
+      // lanes, then 2, 1 inside the lane), as warp_sum_float_butterfly.
+      float t[4] = {v[0], v[1], v[2], v[3]};
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) t[i] += __shfl_xor_sync(0xffffffffu, t[i], off);
+      const float u0 = t[0] + t[2], u1 = t[1] + t[3];
+      s = u0 + u1;
+    } else {
+      int sum = q[0] + q[1] + q[2] + q[3];
+#pragma unroll
+      for (int off = 4; off >= 1; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      s = __half2float(dh) * static_cast<float>(sum);  // exact product
+    }
+    if (live) {
+      uint8_t* blk = out + g * 36;
+      *reinterpret_cast<uint32_t*>(blk + 4 + 4 * sub) =
+          (static_cast<uint32_t>(q[0]) & 0xffu) | ((static_cast<uint32_t>(q[1]) & 0xffu) << 8) |
+          ((static_cast<uint32_t>(q[2]) & 0xffu) << 16) | ((static_cast<uint32_t>(q[3]) & 0xffu) << 24);
+      if (sub == 0)
+        *reinterpret_cast<uint32_t*>(blk) =
+            static_cast<uint32_t>(__half_as_ushort(dh)) | (static_cast<uint32_t>(__half_as_ushort(__float2half_rn(s))) << 16);
+    }
+  }
+}
+
 // Peer all-gather of a Q8_1 activation: every rank quantises its slice and
 // stores the blocks into every rank's buffer (NVLink stores), then (after one
 // system-scope fence per CTA) counts one arrival per CTA into every rank's

@@ -1,0 +1,181 @@
+// Resident-weights Q4_K x Q8_1 matvec for matrices that fit in the SMs' shared
+// memory (a decode step's Q / K / V / O projections: N <= 32 rows per SM).
+//
+// A matvec launched right after the kernel that produces its activation is
+// latency-bound, not bandwidth-bound: one 5.9 MB matrix streams in ~0.9 us,
+// while a launch's dependent chain (wait for the producer, read the
+// activation, compute, reduce, store) takes longer.  So this kernel moves
+// everything that depends only on the weights ahead of the dependency wait:
+//
+// * One CTA per SM takes a contiguous run of R <= 32 rows (R = ceil(N / SMs)).
+//   Before griddepcontrol.wait, one thread brings the run into shared memory
+//   with a single cp.async.bulk (R x NB x 144 bytes, L2 evict-first), and
+//   every lane decodes the 6-bit (scale, min) pair of the groups it
+//   finalises into exact fp32 products d*sc and dmin*m (11 + 6 significant
+//   bits) and (NB = 10) loads its weight nibbles into registers.  The CTA triggers
+//   launch_dependents at once, so the next launch of a chain starts its own
+//   prefetch on the SM's second CTA slot while this one waits and computes.
+// * After the wait only activation-dependent work remains: one thread per
+//   Q8_1 group re-lays the activation into shared memory (its 32 quants at a
+//   bank-spread 16-byte-aligned slot, then fp32 delta and the exact int sum
+//   of its quants), one CTA barrier, and each lane reads per unit two 16-byte
+//   quant vectors and one (delta, sum) pair, forms 8 dp4a, swaps one partial
+//   dot with its partner lane, adds its terms in fp64, and the half-warp
+//   reduces by xor-shuffles; lane 0 stores the row.
+//
+// Layout: a half-warp per row (warp w: rows 2w, 2w+1), 16 lanes x NB/2 units
+// of 16 nibble bytes.  Lane l16 (h = l16 & 1, m = l16 >> 1) takes the units
+// of group pairs q = m + 8i (i < NB/2): block b = q >> 2, pair j = q & 3,
+// bytes [16 + 32j + 16h, +16) -- groups 2j (low nibbles) and 2j+1 (high
+// nibbles), elements [16h, 16h + 16) of each.  Lanes 2m and 2m+1 hold the two
+// halves of both groups; after one exchange lane h finalises group s = 2j+h.
+//
+// Numerics as the streaming kernels (csrc/stream.cuh): integer sub-block dots
+// exact; d*sc*dot and dmin*m*sum(q) exact in fp64; one rounding for their
+// difference, one for the Q8_1 scale, then a fixed-order fp64 sum per row and
+// one rounding to fp32.
+//
+// Trace points (-DMLLB_TRACE builds): 0 start, 1 weights landed, 2 dependency
+// wait returned, 3 activation staged, 7 row stored.
+#pragma once
+
+#include "common.cuh"
+#include "q4k.cuh"
+
+namespace mllb {
+
+constexpr int kResidentMaxRowsPerCta = 32;
+constexpr int kResidentThreads = 32 * (kResidentMaxRowsPerCta / 2);
+
+// Shared-memory slot of Q8_1 group G's 32 quants: 32 bytes per group plus 32
+// bytes of padding after every 4 groups, so that the 8 lanes of a quarter-warp
+// (groups 2m and 2m + 1, halves h) read 8 disjoint 4-bank runs.
+__host__ __device__ constexpr int resident_act_slot(int g) { return 32 * (g + (g >> 2)); }
+
+template <int NB>
+struct ResidentAct {
+  static constexpr int kGroups = NB * 8;
+  static constexpr int kQuantBytes = resident_act_slot(kGroups);
+  static constexpr int kBytes = kQuantBytes + kGroups * 8;  // + (fp32 delta, int32 sum q) per group
+};
+
+template <int NB>
+__global__ void __launch_bounds__(kResidentThreads, 2)
+    resident_q4k_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8, float* __restrict__ out,
+                        int n_rows, int rows_per_cta) {
+  static_assert(NB % 2 == 0, "two units per group pair: NB must be even");
+  constexpr int UPL = NB / 2;  // units per lane
+  constexpr int ROWB = NB * kQ4kBlockBytes;
+  constexpr int G = NB * 8;
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ uint64_t bar;
+  __shared__ __align__(16) uint8_t act[ResidentAct<NB>::kBytes];
+  float2* act_ds = reinterpret_cast<float2*>(act + ResidentAct<NB>::kQuantBytes);  // (delta, sum q as int bits)
+
+  MLLB_TRACE_POINT(0);
+  const int row0 = blockIdx.x * rows_per_cta;
+  const int rows = min(rows_per_cta, n_rows - row0);  // >= 1 by the host's grid
+  const uint32_t bytes = static_cast<uint32_t>(rows * ROWB);
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&bar, bytes);
+    bulk_copy_g2s(smem, w + static_cast<size_t>(row0) * ROWB, bytes, &bar, l2_evict_first_policy());
+  }
+  pdl_launch_dependents();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = 2 * warp + (lane >> 4);
+  const int l16 = lane & 15, h = l16 & 1, m = l16 >> 1;
+  __syncthreads();  // the barrier's initialisation before anyone waits on it
+  const bool landed = __syncthreads_and(mbar_wait_bounded(&bar, 0));
+  if (!landed) {
+    if (threadIdx.x == 0) {
+      record_error(kErrFullWaitTimeout);
+      if (!mbar_wait_bounded(&bar, 0)) record_error(kErrDrainTimeout);  // never leave with the copy in flight
+    }
+    return;
+  }
+  MLLB_TRACE_POINT(1);
+
+  // ---- weights only: before the dependency wait
+  const uint8_t* row = smem + (r < rows ? r : rows - 1) * ROWB;
+  // Nibbles in registers before the wait when they fit the 64-register
+  // budget (NB = 10); wider rows re-read them from shared memory after it.
+  constexpr bool kWeightsInRegs = UPL <= 5;
+  uint4 wq[kWeightsInRegs ? UPL : 1];
+  float dsc[UPL], dmn[UPL];
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+    const int q = m + 8 * i, b = q >> 2, j = q & 3, s = 2 * j + h;
+    const uint8_t* blk = row + b * kQ4kBlockBytes;
+    if constexpr (kWeightsInRegs) wq[i] = lds128(blk + 16 + 32 * j + 16 * h);
+    const uint32_t dd = lds32(blk);
+    const uint8_t* sm = blk + 4;
+    int sc, mn;
+    if (s < 4) {
+      sc = sm[s] & 63;
+      mn = sm[s + 4] & 63;
+    } else {
+      sc = (sm[s + 4] & 15) | ((sm[s - 4] >> 6) << 4);
+      mn = (sm[s + 4] >> 4) | ((sm[s] >> 6) << 4);
+    }
+    // fp16 d (11 significant bits) x 6-bit scale: exact in fp32.
+    dsc[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu))) * static_cast<float>(sc);
+    dmn[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16))) * static_cast<float>(mn);
+  }
+
+  pdl_wait_prerequisite();  // the activation may come from the preceding kernel
+  MLLB_TRACE_POINT(2);
+
+  // ---- activation-dependent work: stage, then compute
+  for (int g = threadIdx.x; g < G; g += blockDim.x) {  // blockDim can be below G for small row counts
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(q8 + g * kQ8BlockBytes);
+    uint32_t v[9];
+#pragma unroll
+    for (int t = 0; t < 9; ++t) v[t] = __ldg(src + t);
+    int sum = 0;
+#pragma unroll
+    for (int t = 1; t < 9; ++t) sum = byte_sum_s8(v[t], sum);
+    uint4* dst = reinterpret_cast<uint4*>(act + resident_act_slot(g));
+    dst[0] = make_uint4(v[1], v[2], v[3], v[4]);
+    dst[1] = make_uint4(v[5], v[6], v[7], v[8]);
+    act_ds[g] = make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(v[0] & 0xffffu))),
+                            __int_as_float(sum));
+  }
+  __syncthreads();
+  MLLB_TRACE_POINT(3);
+  double acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < UPL; ++i) {
+    const int q = m + 8 * i;  // group pair: groups 2q (low nibbles) and 2q + 1 (high nibbles)
+    const uint4 al = lds128(act + resident_act_slot(2 * q) + 16 * h);
+    const uint4 ah = lds128(act + resident_act_slot(2 * q + 1) + 16 * h);
+    const float2 ds = act_ds[2 * q + h];
+    uint4 wv;
+    if constexpr (kWeightsInRegs) wv = wq[i];
+    else wv = lds128(row + (q >> 2) * kQ4kBlockBytes + 16 + 32 * (q & 3) + 16 * h);
+    // Low nibbles x group 2q; high nibbles (unshifted, 16x) x group 2q + 1.
+    int dlo = dp4a_us(wv.x & 0x0f0f0f0fu, al.x, 0);
+    int dhi = dp4a_us(wv.x & 0xf0f0f0f0u, ah.x, 0);
+    dlo = dp4a_us(wv.y & 0x0f0f0f0fu, al.y, dlo);
+    dhi = dp4a_us(wv.y & 0xf0f0f0f0u, ah.y, dhi);
+    dlo = dp4a_us(wv.z & 0x0f0f0f0fu, al.z, dlo);
+    dhi = dp4a_us(wv.z & 0xf0f0f0f0u, ah.z, dhi);
+    dlo = dp4a_us(wv.w & 0x0f0f0f0fu, al.w, dlo);
+    dhi = dp4a_us(wv.w & 0xf0f0f0f0u, ah.w, dhi);
+    // Lane h keeps group 2q+h and takes the partner's half of it.
+    const int dot = (h ? dhi : dlo) + __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
+    const int sum = __float_as_int(ds.y);
+    // h = 1: the dot is 16x (high nibbles unshifted); scale the sum and the delta to match.
+    const double delta = static_cast<double>(ds.x) * (h ? 0.0625 : 1.0);
+    const double t = fma(static_cast<double>(dsc[i]), i2d_exact(dot),
+                         -static_cast<double>(dmn[i]) * i2d_exact(sum << (4 * h)));
+    acc = fma(delta, t, acc);
+  }
+#pragma unroll
+  for (int off = 8; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (l16 == 0 && r < rows) out[row0 + r] = static_cast<float>(acc);
+  MLLB_TRACE_POINT(7);
+}
+
+}  // namespace mllb

@@ -77,6 +77,18 @@ struct ActSource {
 //    in index order -- the same r in every CTA, run after run -- and
 //    quantises the 32-row groups g = blockIdx.x, blockIdx.x + gridDim.x, ...
 //    On leaving, the last CTA to depart (counters[1]) zeroes both counters.
+//  * kEpiQuantProductPeer (row-sharded fused gate/up over `world` GPUs): as
+//    kEpiQuantProduct, but each completed group's Q8_1 block is stored into
+//    EVERY rank's buffer (peer.buffers[r], at this rank's slice: rank x
+//    n_rows/32 blocks, then the group) over NVLink.  After its groups each
+//    CTA fences at system scope and arrives once on every rank's counter for
+//    this rank (peer.flags[r][rank]); CTA 0 then waits (bounded, ~1 s, then
+//    kErrPeerWaitTimeout) until every rank's CTAs have arrived for this
+//    gather ((gathers so far + 1) x gridDim.x, counters cumulative) and
+//    counts the gather -- so the launch completes only when the whole
+//    product's Q8_1 is in this GPU's buffer, and the next kernel's
+//    dependency wait covers it.  Every rank launches the same sequence with
+//    the same shapes (the same grid); plain peer stores, no multicast.
 // Counters must be zero before the first launch; every launch leaves them
 // zero.  Launches that share counters must not overlap on the GPU.
 struct Epilogue {
@@ -87,8 +99,9 @@ struct Epilogue {
   const float* gamma;  //   RMSNorm weights [n_rows]
   double* partials;    //   one per CTA of the grid
   double eps;
+  PeerGather peer;     // kEpiQuantProductPeer
 };
-enum : int { kEpiNone = 0, kEpiQuantProduct = 1, kEpiResidualNorm = 2 };
+enum : int { kEpiNone = 0, kEpiQuantProduct = 1, kEpiResidualNorm = 2, kEpiQuantProductPeer = 3 };
 
 // ============================================================== formats
 
@@ -434,7 +447,8 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
                        float* __restrict__ out0, float* __restrict__ out1, float* __restrict__ out2, int n_rows,
                        int pdl, const Epilogue epi) {
   using C = TeamConfig<Fmt, NB, MATS, V, S, TEAMS>;
-  static_assert(EPI != kEpiQuantProduct || (MATS == 2 && 32 % C::kT == 0), "product groups of whole tiles");
+  constexpr bool kQuantTail = EPI == kEpiQuantProduct || EPI == kEpiQuantProductPeer;
+  static_assert(!kQuantTail || (MATS == 2 && 32 % C::kT == 0), "product groups of whole tiles");
   static_assert(EPI != kEpiResidualNorm || MATS == 1, "the residual norm follows a single matrix");
   constexpr int W = C::kW, RG = C::kRG, T = C::kT, P = C::kP, ROWB = C::kRowBytes;
   constexpr int kFirstBatch = TEAMS > 2 ? TEAMS : 2;
@@ -694,7 +708,7 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
       epi.counters[1] = 0u;
     }
   }
-  if constexpr (EPI == kEpiQuantProduct) {
+  if constexpr (kQuantTail) {
     // One arrival per stored tile, then the groups this CTA completed.
     __shared__ uint32_t s_done[32];
     __shared__ int s_ndone;
@@ -716,13 +730,45 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
           const int g = s_done[i];
           uint32_t d16, s16;
           const int q = q8_1_quantize_lane(ld_cg_f32(out2 + g * 32 + lane), kQ8SumDTimesSumQ, &d16, &s16);
-          q8_1_store_block(epi.q8_out + static_cast<size_t>(g) * kQ8BlockBytes, q, d16, s16, lane);
+          if constexpr (EPI == kEpiQuantProductPeer) {
+            const size_t off = (static_cast<size_t>(epi.peer.rank) * (n_rows / 32) + g) * kQ8BlockBytes;
+            for (int r = 0; r < epi.peer.world; ++r) q8_1_store_block(epi.peer.buffers[r] + off, q, d16, s16, lane);
+          } else {
+            q8_1_store_block(epi.q8_out + static_cast<size_t>(g) * kQ8BlockBytes, q, d16, s16, lane);
+          }
           if (lane == 0) epi.counters[g] = 0;
         }
       }
       named_barrier(1, C::kConsumers);
       if (tid == 0) s_ndone = 0;
       named_barrier(1, C::kConsumers);
+    }
+    if constexpr (EPI == kEpiQuantProductPeer) {
+      // The barrier above orders this CTA's peer stores before thread 0's
+      // system-scope fence and arrivals.
+      if (tid == 0) {
+        const PeerGather& pg = epi.peer;
+        fence_sys();
+        for (int r = 0; r < pg.world; ++r) red_relaxed_sys_add(pg.flags[r] + pg.rank, 1u);
+        if (blockIdx.x == 0) {
+          const uint32_t target = (*pg.count + 1u) * gridDim.x;
+          const uint32_t* mine = pg.flags[pg.rank];
+          const uint64_t start = global_timer_ns();
+          bool ok = true;
+          for (int src = 0; src < pg.world && ok; ++src) {
+            for (uint32_t i = 0;; ++i) {
+              if (static_cast<int32_t>(ld_volatile_u32(mine + src) - target) >= 0) break;
+              if (((i & 255u) == 255u && global_timer_ns() - start > kWaitLimitNs) || i >= kWaitMaxIters) {
+                ok = false;
+                break;
+              }
+            }
+          }
+          fence_sys();  // the peers' blocks are visible before this launch completes
+          if (!ok) record_error(kErrPeerWaitTimeout);
+          *pg.count += 1u;
+        }
+      }
     }
   }
 }

@@ -338,7 +338,7 @@ class Decoder:
 
     def __init__(self, weights: DecodeWeights, k_cache, v_cache: torch.Tensor | None = None, *, pdl: bool = True,
                  fused: bool = False, group=None, gather: str = "peer", prefetch: bool = False, quant_tail: bool = True,
-                 norm_tail: bool = False):
+                 norm_tail: bool = False, gather_tail: bool = True):
         cfg = weights.cfg
         cfg.validate()
         self.cfg, self.w, self.k_cache, self.v_cache = cfg, weights, k_cache, v_cache
@@ -399,7 +399,13 @@ class Decoder:
         # separate quantiser launch: 8 launches per layer instead of 9.
         self.quant_tail = (quant_tail and not self.fused and self.world == 1 and nb_h in (8, 10, 16)
                            and ffn_local % 32 == 0)
-        if self.quant_tail:
+        # Sharded over GPUs with peer mappings: the gate/up launch also stores
+        # the Q8_1 of its product slice into every rank's buffer and completes
+        # once all ranks' slices have arrived (mllb_q4k_gate_up_q8_gather), in
+        # place of the separate all-gather launch.
+        self.gather_tail = (gather_tail and self.peer is not None and not self.fused and nb_h in (8, 10, 16)
+                            and ffn_local % 32 == 0)
+        if self.quant_tail or self.gather_tail:
             self.b.extra["prod_counters"] = torch.zeros(ffn_local // 32, dtype=torch.int32, device=dev)
         # norm_tail: the O and down projections (hidden rows each) also do the
         # residual add + RMSNorm + Q8_1 that follows them (mllb_q4k_matvec_norm)
@@ -564,6 +570,12 @@ class Decoder:
                                             P(b.q8_prod), P(b.extra["prod_counters"]), ffn_local, cfg.hidden, fl, s),
                       "gate_up + Q8_1")
                 q8_prod = P(b.q8_prod)
+            elif self.gather_tail:
+                half = layer % 2
+                check(L.mllb_q4k_gate_up_q8_gather(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod),
+                                                   P(b.extra["prod_counters"]), ffn_local, cfg.hidden,
+                                                   self.peer["tables"][half], fl, s), "gate_up + Q8_1 gather")
+                q8_prod = self.peer["buf"].data_ptr() + half * self.peer["half"]
             else:
                 check(L.mllb_q4k_gate_up_ex(P(lw.up), P(lw.gate), P(b.q8_hidden), None, None, P(b.prod), ffn_local,
                                             cfg.hidden, fl, s), "gate_up")
@@ -597,7 +609,7 @@ class Decoder:
         L = self.cfg.layers
         if self.fused:
             return 1 + L * 6 + 1 + 1
-        per_layer = 6 if self.quant_tail else 7           # QKV, attention x 2, O, gate/up (+ quantiser), down
+        per_layer = 6 if (self.quant_tail or self.gather_tail) else 7  # QKV, attention x 2, O, gate/up (+ quantiser / gather), down
         norms = (0 if self.norm_tail_o else L) + (1 if self.norm_tail_down else L)
         return 1 + L * per_layer + norms + 1 + 1 + 1       # embed, ..., final norm, logits, argmax
 

@@ -23,7 +23,7 @@ from __future__ import annotations
 import torch
 
 from . import formats as F
-from ._lib import LAUNCH_PDL, S_D_SUMQ, S_SUM_X, ActF32, check, device_error, lib  # noqa: F401
+from ._lib import LAUNCH_CONST_AUX, LAUNCH_PDL, S_D_SUMQ, S_SUM_X, ActF32, check, device_error, lib  # noqa: F401
 
 __all__ = [
     "quantize_q8_1", "q4_k_q8_1_matvec", "q4_k_q8_1_gate_order", "q4k_gate_up", "q6_k_q8_1_matvec",
@@ -198,11 +198,15 @@ def fused_q_imrope_runtime_fastpow(q: torch.Tensor, gamma: torch.Tensor, positio
 
 def rmsnorm_imrope_q(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tensor,
                      theta_scale: torch.Tensor | float | None = None, out: torch.Tensor | None = None,
-                     heads_per_token: int | None = None, pdl: bool = False) -> torch.Tensor:
+                     heads_per_token: int | None = None, pdl: bool = False,
+                     const_aux: bool = False) -> torch.Tensor:
     """Batched form: q[tokens*heads_per_token, 128], positions int32[tokens, 4].
 
     theta_scale: a device fp32[1] tensor (reference ABI), a Python float used
     as the exact float64 scale, or None for pow(5e6, -2/128) in float64.
+    pdl: programmatic dependent launch; with const_aux too, gamma, positions
+    and theta_scale (not written by the preceding kernel) are read and the
+    rotation table built before waiting for it (MLLB_LAUNCH_CONST_AUX).
     """
     _need(q, "q", torch.float32)
     _need(gamma, "gamma", torch.float32)
@@ -228,7 +232,8 @@ def rmsnorm_imrope_q(q: torch.Tensor, gamma: torch.Tensor, positions: torch.Tens
         value = float(theta_scale)
     _same_device(q, gamma, positions, out)
     check(lib().mllb_rmsnorm_imrope_q_batched_ex(q.data_ptr(), gamma.data_ptr(), positions.data_ptr(), ptr, value,
-                                                 out.data_ptr(), tokens, heads_per_token, LAUNCH_PDL if pdl else 0,
+                                                 out.data_ptr(), tokens, heads_per_token,
+                                                 (LAUNCH_PDL if pdl else 0) | (LAUNCH_CONST_AUX if const_aux else 0),
                                                  _stream(q)),
           "rmsnorm_imrope_q")
     return out

@@ -87,3 +87,28 @@ def test_input_fixture_hashes_unchanged(golden):
     for name, g in golden["imrope_reference_fixtures"].items():
         payload = fx.serialize_imrope(rfx.imrope_reference_inputs(g["positions"]))
         assert hashlib.sha256(payload).hexdigest() == g["input_sha256"]
+
+
+@pytest.mark.parametrize("const_aux", [False, True])
+@pytest.mark.parametrize("tokens", [1, 5])
+def test_pdl_chain_feeds_each_output_into_the_next(orc, const_aux, tokens):
+    """out_i = IMROPE(out_{i-1}), every launch PDL-chained on the previous one.
+    With const_aux the rotation table is built before the dependency wait;
+    q (the previous launch's output) must still be read after it."""
+    rng = np.random.default_rng(31 + tokens)
+    q0 = rng.standard_normal((tokens * 32, 128)).astype(np.float32)
+    gamma = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    pos = rng.integers(0, 40000, (tokens, 4)).astype(np.int32)
+    theta = torch.tensor([F.theta_scale_f32()], dtype=torch.float32, device="cuda")
+    g_d, p_d = dev(gamma), dev(pos)
+    bufs = [dev(q0)] + [torch.empty(tokens * 32, 128, dtype=torch.float32, device="cuda") for _ in range(4)]
+    for i in range(4):
+        ops.rmsnorm_imrope_q(bufs[i], g_d, p_d, theta, out=bufs[i + 1], pdl=True, const_aux=const_aux)
+    prev = q0
+    for i in range(4):
+        got = bufs[i + 1].cpu().numpy()
+        for t in range(tokens):
+            ref = orc.imrope(prev[t * 32:(t + 1) * 32], gamma, pos[t], orc.runtime_theta_scale())
+            assert_within_tolerance(got[t * 32:(t + 1) * 32].reshape(-1), ref.reshape(-1), f"step {i} token {t}")
+        prev = got  # the next step starts from the GPU's fp32 values, as the chain did
+    assert ops.device_error() == 0

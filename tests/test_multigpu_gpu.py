@@ -140,7 +140,7 @@ def test_peer_allgather_matches_local_quantisation(tmp_path):
     assert torch.load(out) == [True] * 4
 
 
-def _decode_worker(rank, world, port, out, gather="peer"):
+def _decode_worker(rank, world, port, out, gather="peer", gather_tail=True):
     import torch
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0",
@@ -155,8 +155,9 @@ def _decode_worker(rank, world, port, out, gather="peer"):
         k, v = D.generate_kv_cache(cfg, "cuda")
         s = torch.cuda.Stream()
         with torch.cuda.stream(s):
-            dec = D.Decoder(w, k, v, group=dist.group.WORLD, gather=gather)
+            dec = D.Decoder(w, k, v, group=dist.group.WORLD, gather=gather, gather_tail=gather_tail)
             assert (dec.peer is not None) == (gather == "peer")
+            assert dec.gather_tail == (gather == "peer" and gather_tail)
             dec.reset(17)
             dec.capture()
             tokens = dec.generate(17, 5)
@@ -171,8 +172,8 @@ def _decode_worker(rank, world, port, out, gather="peer"):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("gather", ["peer", "nccl"])
-def test_sharded_decode_matches_single_gpu(tmp_path, gather):
+@pytest.mark.parametrize("gather,gather_tail", [("peer", True), ("peer", False), ("nccl", True)])
+def test_sharded_decode_matches_single_gpu(tmp_path, gather, gather_tail):
     """gate/up + vocab row-sharded over the GPUs: the same tokens and logits as one GPU."""
     import torch
     from mojo_llm_lab_b200 import decode as D
@@ -180,7 +181,7 @@ def test_sharded_decode_matches_single_gpu(tmp_path, gather):
     if world < 2:
         pytest.skip("needs at least 2 GPUs")
     out = tmp_path / "decode.pt"
-    _spawn(_decode_worker, world, out, gather)
+    _spawn(_decode_worker, world, out, gather, gather_tail)
     got = torch.load(out)
     cfg = D.DecodeConfig(layers=2, vocab=4096, context=300, new_tokens=6)
     w = D.generate_weights(cfg, "cuda")

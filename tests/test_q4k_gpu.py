@@ -83,6 +83,48 @@ def test_seeded_matvec_against_oracle(orc, rows, k):
     assert ratio < 0.1
 
 
+@pytest.mark.parametrize("rows,k", [(4736, 2560), (4737, 2560), (2560, 4096), (1024, 2560), (29, 4096),
+                                    (296, 2560)])
+def test_resident_shapes_against_oracle(orc, rows, k):
+    """Shapes around the resident-weights kernel's limits (at most 32 rows per
+    SM, K = 2560 / 4096; 4737 rows fall back to the streaming kernel), odd
+    rows per CTA (an idle half-warp) and a partial last CTA."""
+    w = fx.seeded_q4k_matrix(rows, k, seed=rows + 3 * k)
+    a = orc.quantize_q8_1(fx.seeded_activation(k, seed=k + 1))
+    ref = orc.q4k_matvec(w, a, rows, k)
+    buf, out = with_canaries(rows)
+    ops.q4_k_q8_1_matvec(dev(w), dev_bytes(a), out)
+    ratio = assert_within_tolerance(out.cpu().numpy(), ref, f"{rows}x{k}")
+    assert canaries_intact(buf)
+    assert ratio < 0.1
+
+
+@pytest.mark.parametrize("rows,k", [(4096, 2560), (2560, 4096)])
+def test_pdl_chain_reads_each_activation_after_its_producer(orc, rows, k):
+    """quantiser -> matvec -> quantiser -> ... on ONE activation buffer, every
+    launch PDL-chained: each matvec prefetches its weights before the
+    quantiser that feeds it has finished, and must still use that
+    quantiser's output (a stale read shows as the previous step's answer)."""
+    import ctypes as C
+    from mojo_llm_lab_b200._lib import LAUNCH_PDL, S_D_SUMQ, check, lib
+    steps = 6
+    w = fx.seeded_q4k_matrix(rows, k, seed=77)
+    xs = np.stack([fx.seeded_activation(k, seed=300 + i) * (1 + i) for i in range(steps)])
+    wd, xd = dev(w), dev(xs)
+    act = torch.empty(k // 32 * 36, dtype=torch.uint8, device="cuda")
+    outs = torch.empty(steps, rows, dtype=torch.float32, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for i in range(steps):
+        check(lib().mllb_q8_1_quantize_ex(xd[i].data_ptr(), act.data_ptr(), k, S_D_SUMQ, LAUNCH_PDL,
+                                          C.c_void_p(stream)), "quantize")
+        ops.q4_k_q8_1_matvec(wd, act, outs[i], pdl=True)
+    got = outs.cpu().numpy()
+    for i in range(steps):
+        ref = orc.q4k_matvec(w, orc.quantize_q8_1(xs[i]), rows, k)
+        assert_within_tolerance(got[i], ref, f"step {i}")
+    assert ops.device_error() == 0
+
+
 def test_seeded_gate_up_full_config(orc):
     rows, k = 9728, 2560
     up_w = fx.seeded_q4k_matrix(rows, k, seed=101)
