@@ -327,11 +327,13 @@ int mllb_q8_1_quantize_allgather(const float *x, int64_t k, const mllb_peer_gath
  * rows, a multiple of 32) with the all-gather built in: each completed
  * 32-row group's Q8_1 block of the product goes straight into every rank's
  * buffer (peers->buffers[r] + (rank * n / 32 + group) * 36, NVLink stores),
- * each CTA then arrives on every rank's counter for this rank, and the launch
+ * the rank then arrives once on every rank's counter for it, and the launch
  * completes only when every rank's blocks are in this GPU's buffer (a rank
  * that does not arrive within ~1 s sets device error bit 6, mask 0x40).  So
  * the down projection, launched next, reads the whole product's Q8_1 from
- * peers->buffers[rank].  counters: n / 32 zeroed uint32, left zero.  peers as
+ * peers->buffers[rank].  counters: n / 32 + 1 zeroed uint32 (the groups, then
+ * the CTAs' arrivals), left zero.  Each gather adds 1 to every rank's
+ * flags[rank].  peers as
  * for mllb_q8_1_quantize_allgather; every rank issues the same sequence of
  * these launches with the same n and k.  One launch in place of the gate/up
  * launch plus mllb_q8_1_quantize_allgather.  No reference counterpart (the

@@ -186,6 +186,14 @@ __device__ __forceinline__ uint32_t atom_add_release_gpu(uint32_t* addr, uint32_
   return old;
 }
 
+// Arrival that both publishes this thread's earlier writes (release) and,
+// for the thread that sees the final count, acquires everyone else's.
+__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* addr, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(addr), "r"(v) : "memory");
+  return old;
+}
+
 __device__ __forceinline__ uint32_t ld_acquire_gpu_u32(const uint32_t* addr) {
   uint32_t v;
   asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");

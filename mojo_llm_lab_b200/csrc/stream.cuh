@@ -81,14 +81,16 @@ struct ActSource {
 //    kEpiQuantProduct, but each completed group's Q8_1 block is stored into
 //    EVERY rank's buffer (peer.buffers[r], at this rank's slice: rank x
 //    n_rows/32 blocks, then the group) over NVLink.  After its groups each
-//    CTA fences at system scope and arrives once on every rank's counter for
-//    this rank (peer.flags[r][rank]); CTA 0 then waits (bounded, ~1 s, then
-//    kErrPeerWaitTimeout) until every rank's CTAs have arrived for this
-//    gather ((gathers so far + 1) x gridDim.x, counters cumulative) and
-//    counts the gather -- so the launch completes only when the whole
-//    product's Q8_1 is in this GPU's buffer, and the next kernel's
-//    dependency wait covers it.  Every rank launches the same sequence with
-//    the same shapes (the same grid); plain peer stores, no multicast.
+//    CTA arrives (release, GPU scope) on a local counter, counters[n_rows /
+//    32]; the last CTA to arrive (acquiring every other CTA's release) resets
+//    it, fences once at system scope and arrives on every rank's counter for
+//    this rank (peer.flags[r][rank]).  CTA 0 then waits (bounded, ~1 s, then
+//    kErrPeerWaitTimeout) until every rank has arrived for this gather
+//    (gathers so far + 1; counters cumulative) and counts the gather -- so
+//    the launch completes only when the whole product's Q8_1 is in this
+//    GPU's buffer, and the next kernel's dependency wait covers it.  Every
+//    rank launches the same sequence with the same shapes; plain peer stores
+//    only.
 // Counters must be zero before the first launch; every launch leaves them
 // zero.  Launches that share counters must not overlap on the GPU.
 struct Epilogue {
@@ -745,13 +747,18 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     }
     if constexpr (EPI == kEpiQuantProductPeer) {
       // The barrier above orders this CTA's peer stores before thread 0's
-      // system-scope fence and arrivals.
+      // release; the last CTA's acquire + system-scope fence carries every
+      // CTA's stores ahead of its arrivals on the ranks' counters.
       if (tid == 0) {
         const PeerGather& pg = epi.peer;
-        fence_sys();
-        for (int r = 0; r < pg.world; ++r) red_relaxed_sys_add(pg.flags[r] + pg.rank, 1u);
+        uint32_t* arrived = epi.counters + n_rows / 32;
+        if (atom_add_acq_rel_gpu(arrived, 1u) == gridDim.x - 1) {
+          *arrived = 0u;
+          fence_sys();
+          for (int r = 0; r < pg.world; ++r) red_relaxed_sys_add(pg.flags[r] + pg.rank, 1u);
+        }
         if (blockIdx.x == 0) {
-          const uint32_t target = (*pg.count + 1u) * gridDim.x;
+          const uint32_t target = *pg.count + 1u;
           const uint32_t* mine = pg.flags[pg.rank];
           const uint64_t start = global_timer_ns();
           bool ok = true;

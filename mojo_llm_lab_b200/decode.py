@@ -405,8 +405,8 @@ class Decoder:
         # place of the separate all-gather launch.
         self.gather_tail = (gather_tail and self.peer is not None and not self.fused and nb_h in (8, 10, 16)
                             and ffn_local % 32 == 0)
-        if self.quant_tail or self.gather_tail:
-            self.b.extra["prod_counters"] = torch.zeros(ffn_local // 32, dtype=torch.int32, device=dev)
+        if self.quant_tail or self.gather_tail:  # the groups (+ the CTAs' arrivals for the gather)
+            self.b.extra["prod_counters"] = torch.zeros(ffn_local // 32 + 1, dtype=torch.int32, device=dev)
         # norm_tail: the O and down projections (hidden rows each) also do the
         # residual add + RMSNorm + Q8_1 that follows them (mllb_q4k_matvec_norm)
         # where a streaming configuration exists for their K: two launches
