@@ -57,7 +57,7 @@ FALLBACK_HBM_GBS = 6650.0
 
 WORKLOADS = {
     # the headline metric's configuration: Q4_K x Q8_1, 4096 x 2560
-    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="team_stream_kernel<Q4kFormat,10,1,8,2,2>",
+    "q4k_matvec": dict(kind="q4k", rows=4096, k=2560, kernel="resident_q4k_kernel<10>",
                        profile="q4k_matvec_n4096_k2560"),
     # fused gate/up, two 9728x2560 matrices, outputs up, gate, up*silu(gate)
     "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,4,6,3>",
@@ -1711,23 +1711,31 @@ def main():
                                 device_id=torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0"))))
         try:
             line = runner(args, rank, world)
+            if args.workload == "q4k_matvec" and not args.headline_only:
+                # the row-sharded configurations at this N (every rank runs them, in the same order)
+                others = other_configs(args, rank, world, OTHER_CONFIGS_SHARDED)
+                if line is not None:
+                    line["other_configs"] = others
         finally:
             dist.destroy_process_group()
     else:
         line = runner(args, rank, world)
         if line is not None and args.workload == "q4k_matvec" and not args.headline_only:
-            line["other_configs"] = other_configs(args, rank, world)
+            line["other_configs"] = other_configs(args, rank, world, OTHER_CONFIGS)
     if line is not None:
         print(json.dumps(line), flush=True)
 
 
-# The other benchmark configurations, measured in the same run as the headline
-# (one GPU): each entry is that workload's own line, trimmed.
+# The other benchmark configurations, measured in the same run as the headline:
+# each entry is that workload's own line, trimmed.  One GPU: all of them;
+# N GPUs: the row-sharded ones (gate/up and the vocabulary projection with an
+# NCCL all-gather, the 36-layer decode with both sharded).
 OTHER_CONFIGS = (("imrope", {}), ("imrope_batched", {}), ("q8_1", {}), ("gate_up", {}), ("q6k_vocab", {}),
                  ("decode", {"steps": 3, "warmup": 3}))
+OTHER_CONFIGS_SHARDED = (("gate_up", {}), ("q6k_vocab", {}), ("decode", {"steps": 3, "warmup": 3}))
 
 
-def other_configs(args, rank: int, world: int) -> dict:
+def other_configs(args, rank: int, world: int, which) -> dict:
     import gc
 
     import torch
@@ -1737,17 +1745,23 @@ def other_configs(args, rank: int, world: int) -> dict:
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "vs_baseline", "dtype",
             "config", "e2e", "roofline", "clocks", "gpu_launches", "us_per_op")
     out = {}
-    for name, over in OTHER_CONFIGS:
+    for name, over in which:
         sub = argparse.Namespace(**vars(args))
         sub.workload, sub.no_cpu_baseline, sub.copies = name, True, 0
         sub.steps, sub.warmup = over.get("steps", args.steps), over.get("warmup", args.warmup)
         t0 = time.perf_counter()
-        try:
+        if world > 1:  # collectives inside: every rank runs it to the end or the job fails together
             line = runners.get(name, run_ours)(sub, rank, world)
-            out[name] = {kk: line[kk] for kk in keep if kk in line}
-        except SystemExit as e:  # a failed correctness gate: recorded, the headline stands
-            out[name] = {"error": str(e)}
-        out[name]["wall_s"] = round(time.perf_counter() - t0, 1)
+            if line is not None:
+                out[name] = {kk: line[kk] for kk in keep if kk in line}
+        else:
+            try:
+                line = runners.get(name, run_ours)(sub, rank, world)
+                out[name] = {kk: line[kk] for kk in keep if kk in line}
+            except SystemExit as e:  # a failed correctness gate: recorded, the headline stands
+                out[name] = {"error": str(e)}
+        if name in out:
+            out[name]["wall_s"] = round(time.perf_counter() - t0, 1)
         gc.collect()
         torch.cuda.empty_cache()
     return out

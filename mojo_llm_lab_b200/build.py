@@ -7,6 +7,9 @@
 * lib/libmllb200_interpose.so -- LD_PRELOAD library that sends GGML's fused
                               Q4_K gate/up launch to libmllb200.so
                               (csrc/interpose.cpp, host code only)
+* lib/mllb200_harness       -- native timing / correctness harness (CUDA
+                              graphs of serialised reps, ABBA arms, NVML
+                              clocks, red zones; csrc/harness.cpp)
 
 Both target `-gencode arch=compute_100a,code=sm_100a` only (B200).  The build
 is incremental on source mtimes; `python -m mojo_llm_lab_b200.build` forces it.
@@ -27,6 +30,7 @@ INCLUDE = ROOT / "include"
 LIB = LIBDIR / "libmllb200.so"
 CUBIN = LIBDIR / "mllb200_compat.cubin"
 INTERPOSE = LIBDIR / "libmllb200_interpose.so"
+HARNESS = LIBDIR / "mllb200_harness"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xptxas", "-v", f"-I{INCLUDE}", f"-I{CSRC}"]
@@ -81,6 +85,13 @@ def build(force: bool = False, verbose: bool = False) -> dict:
               "-Wl,-rpath,$ORIGIN"], LIBDIR / "build_interpose.log", verbose)
         tmp.replace(INTERPOSE)
         built["interpose"] = str(INTERPOSE)
+    if force or _stale(HARNESS) or HARNESS.stat().st_mtime < LIB.stat().st_mtime:
+        tmp = HARNESS.with_suffix(".tmp")
+        _run([nvcc(), "-O2", "-std=c++17", f"-I{INCLUDE}", "-o", str(tmp), str(CSRC / "harness.cpp"),
+              f"-L{LIBDIR}", "-lmllb200", "-ldl",
+              "-Xlinker", "-rpath,$ORIGIN"], LIBDIR / "build_harness.log", verbose)
+        tmp.replace(HARNESS)
+        built["harness"] = str(HARNESS)
     if force or _stale(CUBIN):
         tmp = CUBIN.with_suffix(".cubin.tmp")
         _run([nvcc(), *COMMON, *ARCH, "-cubin", "-o", str(tmp), str(CSRC / "compat.cu")],
