@@ -1130,8 +1130,12 @@ def run_decode(args, rank: int, world: int):
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
     cfg = D.DecodeConfig(context=args.context)
-    group = dist.group.WORLD if world > 1 else None
-    weights = D.generate_weights(cfg, device, world=world, rank=rank)
+    # Replicas: every rank decodes its own sequence on the whole model (no
+    # sharding, no collective in the step); value = all ranks' tokens/s.
+    replicas = getattr(args, "decode_replicas", False) and world > 1
+    shard_world = 1 if replicas else world
+    group = dist.group.WORLD if shard_world > 1 else None
+    weights = D.generate_weights(cfg, device, world=shard_world, rank=rank if shard_world > 1 else 0)
     if args.kv == "q4_0":
         k_cache, v_cache = D.generate_kv_cache_q4_0(cfg, device), None
     else:
@@ -1147,7 +1151,7 @@ def run_decode(args, rank: int, world: int):
     dec.reset(start_token)
     dec.step()
     torch.cuda.synchronize()
-    if world > 1:
+    if shard_world > 1:
         logits = torch.empty(weights.vocab_shard.per_rank * world, dtype=torch.float32, device=device)
         dist.all_gather_into_tensor(logits, dec.b.logits)
         logits = logits[:cfg.vocab]
@@ -1156,7 +1160,7 @@ def run_decode(args, rank: int, world: int):
     agreement = None
     if rank == 0 and not args.skip_check:
         from oracle import decode as OD
-        full = weights if world == 1 else D.generate_weights(cfg, device)
+        full = weights if shard_world == 1 else D.generate_weights(cfg, device)
         host = OD.host_model(full)
         del full
         kh, vh, planes = decode_host_cache(cfg, args.kv, device)
@@ -1201,7 +1205,7 @@ def run_decode(args, rank: int, world: int):
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = DECODE_TOKENS / (ms * 1e-3)
+    value = DECODE_TOKENS / (ms * 1e-3) * (world if replicas else 1)
 
     # e2e through the public API: Decoder.generate (H2D of the seed state,
     # 128 graph replays, D2H of the generated tokens).
@@ -1247,7 +1251,7 @@ def run_decode(args, rank: int, world: int):
         line = {
             "metric": "36-layer synthetic Q4_K decode tokens/s", "value": round(value, 2), "unit": "tokens/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "weak" if replicas else "strong", "vs_baseline": None,
             "dtype": "Q4_K/Q6_K x Q8_1 dp4a, f64 accumulate; " + ("fp16" if args.kv == "f16" else "Q4_0")
                      + " KV, f64 attention",
             "data": "synthetic (seeded random weights, N(0,1) KV prefill)",
@@ -1256,11 +1260,14 @@ def run_decode(args, rank: int, world: int):
                                    + ("" if args.kv == "f16" else ", Q4_0 KV cache"),
                        "kv_cache": args.kv,
                        "us_per_token": round(us_per_token, 3), "bytes_per_token_per_gpu": int(rank_bytes),
-                       "parallelism": ((f"gate/up + vocab rows/{world} per rank; " + ("peer-store Q8_1 all-gather over NVLink" if dec.peer is not None else "NCCL all-gather") + ", NCCL all-reduce of the argmax key") if world > 1 else "single GPU"),
+                       "parallelism": (f"replicas x{world}: one independent sequence per GPU, whole model on each"
+                                       if replicas else
+                                       (f"gate/up + vocab rows/{world} per rank; " + ("peer-store Q8_1 all-gather over NVLink" if dec.peer is not None else "NCCL all-gather") + ", NCCL all-reduce of the argmax key") if world > 1 else "single GPU"),
                        "l2": "2.4 GB of weights per token > L2; no flush", "pdl": not args.no_pdl,
                        "fused_activations": dec.fused,
                        "logit_agreement": agreement},
-            "e2e": {"value": round(DECODE_TOKENS / (e_ms * 1e-3), 2), "unit": "tokens/s", "h2d_bytes_per_step": 32,
+            "e2e": {"value": round(DECODE_TOKENS / (e_ms * 1e-3) * (world if replicas else 1), 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 32,
                     "d2h_bytes_per_step": 32 + DECODE_TOKENS * 4, "ms_per_step": round(e_ms, 4),
                     "path": "Decoder.generate (C-ABI launches captured in a CUDA graph), host seed state in, tokens out"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
@@ -1666,6 +1673,8 @@ def main():
                                                                "attention", "q8_1", "q8_1_batched"],
                     default="q4k_matvec")
     ap.add_argument("--fused", action="store_true", help="decode: norms / quantisers built into the matvecs")
+    ap.add_argument("--decode-replicas", action="store_true",
+                    help="decode at N GPUs: one independent sequence per GPU (no sharding); tokens/s of all")
     ap.add_argument("--context", type=int, default=4096, help="decode: prefilled KV rows")
     ap.add_argument("--kv", choices=["f16", "q4_0"], default="f16",
                     help="decode: KV cache type (q4_0: GGML Q4_0, the reference's llama.cpp setting)")
@@ -1732,14 +1741,16 @@ def main():
 # NCCL all-gather, the 36-layer decode with both sharded).
 OTHER_CONFIGS = (("imrope", {}), ("imrope_batched", {}), ("q8_1", {}), ("gate_up", {}), ("q6k_vocab", {}),
                  ("decode", {"steps": 3, "warmup": 3}))
-OTHER_CONFIGS_SHARDED = (("gate_up", {}), ("q6k_vocab", {}), ("decode", {"steps": 3, "warmup": 3}))
+OTHER_CONFIGS_SHARDED = (("gate_up", {}), ("q6k_vocab", {}), ("decode", {"steps": 3, "warmup": 3}),
+                         ("decode_replicas", {"steps": 3, "warmup": 3}))
 
 
 def other_configs(args, rank: int, world: int, which) -> dict:
     import gc
 
     import torch
-    runners = {"decode": run_decode, "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
+    runners = {"decode": run_decode, "decode_replicas": run_decode,
+               "imrope": lambda a, r, w: run_imrope(a, r, w, batched=False),
                "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True),
                "q8_1": lambda a, r, w: run_q8_1(a, r, w, batched=False)}
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "vs_baseline", "dtype",
@@ -1748,6 +1759,7 @@ def other_configs(args, rank: int, world: int, which) -> dict:
     for name, over in which:
         sub = argparse.Namespace(**vars(args))
         sub.workload, sub.no_cpu_baseline, sub.copies = name, True, 0
+        sub.decode_replicas = name == "decode_replicas"
         sub.steps, sub.warmup = over.get("steps", args.steps), over.get("warmup", args.warmup)
         t0 = time.perf_counter()
         if world > 1:  # collectives inside: every rank runs it to the end or the job fails together

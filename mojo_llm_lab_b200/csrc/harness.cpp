@@ -157,13 +157,15 @@ struct Nvml {
   void* lib = nullptr;
   void* dev = nullptr;
   int (*clock)(void*, int, unsigned*) = nullptr;
-  bool open(int index) {
+  // The NVML device of the CUDA device in use, matched by PCI bus id (NVML
+  // numbers the GPUs without regard to CUDA_VISIBLE_DEVICES).
+  bool open(const char* pci_bus_id) {
     lib = dlopen("libnvidia-ml.so.1", RTLD_NOW | RTLD_LOCAL);
     if (!lib) return false;
     auto init = reinterpret_cast<int (*)()>(dlsym(lib, "nvmlInit_v2"));
-    auto handle = reinterpret_cast<int (*)(unsigned, void**)>(dlsym(lib, "nvmlDeviceGetHandleByIndex_v2"));
+    auto handle = reinterpret_cast<int (*)(const char*, void**)>(dlsym(lib, "nvmlDeviceGetHandleByPciBusId_v2"));
     clock = reinterpret_cast<int (*)(void*, int, unsigned*)>(dlsym(lib, "nvmlDeviceGetClockInfo"));
-    return init && handle && clock && init() == 0 && handle(static_cast<unsigned>(index), &dev) == 0;
+    return init && handle && clock && init() == 0 && handle(pci_bus_id, &dev) == 0;
   }
   unsigned read(int which) {  // 0 graphics, 1 SM, 2 memory
     unsigned mhz = 0;
@@ -244,8 +246,10 @@ int main(int argc, char** argv) {
   // ---- device, NVML, module
   cuda_ok(cudaSetDevice(0), "cudaSetDevice");
   cuda_ok(cudaFree(nullptr), "context");
+  char bus_id[32] = {0};
+  cuda_ok(cudaDeviceGetPCIBusId(bus_id, sizeof(bus_id), 0), "cudaDeviceGetPCIBusId");
   Nvml nvml;
-  if (!nvml.open(0)) die(14, "NVML unavailable%s%s");
+  if (!nvml.open(bus_id)) die(14, "NVML unavailable for %s%s", bus_id);
   if (!drv.open()) die(20, "the CUDA driver (libcuda.so.1) is not available%s%s");
   CUmodule module;
   CUfunction fn;
