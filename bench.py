@@ -165,6 +165,35 @@ class ClockSampler:
                           "and the timed region"}
 
 
+# A step lasts at least this long: the clock sampler's nvidia-smi queries
+# (every 20 ms) can stall the GPU for tens of microseconds, which must stay a
+# small fraction of a step.
+STEP_TARGET_MS = 1.0
+
+
+def passes_for(graph, stream, world: int, device) -> int:
+    """Passes over a workload's copies per step so that a step lasts about
+    STEP_TARGET_MS: one replay of `graph` (one pass) is timed on the device;
+    at N ranks the maximum is taken (every rank must replay alike)."""
+    import torch
+    import torch.distributed as dist
+    for _ in range(2):
+        graph.replay()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(3):
+        graph.replay()
+    b.record(stream)
+    torch.cuda.synchronize()
+    pass_ms = a.elapsed_time(b) / 3
+    passes = max(1, int(-(-STEP_TARGET_MS // max(pass_ms, 1e-3))))
+    if world > 1:
+        t = torch.tensor([passes], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        passes = int(t.item())
+    return passes
+
+
 def preroll(graph, seconds: float = 1.0) -> None:
     """Replay `graph` for about `seconds` (untimed) so that the clock samples
     taken around the timed region describe the same load.  For graphs with no
@@ -307,10 +336,10 @@ def matvec_config(workload: str, world: int, pdl: bool, copies: int = 0) -> dict
     my_rows = rows // world if sharded else rows
     wbytes = weight_bytes(kind, my_rows, k)
     copies = copies or max(2, -(-int(2.2 * L2_BYTES) // wbytes))
-    return {"workload": describe(workload), "rows": rows, "k": k, "launches_per_step": copies,
+    return {"workload": describe(workload), "rows": rows, "k": k, "weight_copies": copies,
             "bytes_per_op": algorithmic_bytes(kind, rows, k),
-            "l2": f"{copies} distinct weight copies ({copies * wbytes / 2**20:.0f} MiB per GPU) > 2x L2 per step; "
-                  f"no flush",
+            "l2": f"{copies} distinct weight copies ({copies * wbytes / 2**20:.0f} MiB per GPU) > 2x L2 per pass "
+                  f"over them; no flush; a step is as many passes as make ~{STEP_TARGET_MS:g} ms",
             "parallelism": (f"rows/{world} per rank + NCCL all-gather" if sharded else
                             (f"replicas x{world}" if world > 1 else "single GPU")),
             "pdl": pdl}
@@ -420,15 +449,22 @@ def run_ours(args, rank: int, world: int):
             if not np.array_equal(g[rank], outs[0].cpu().numpy()):
                 raise SystemExit("all-gather placed this rank's rows wrongly")
 
-    # Capture the step in a CUDA graph: host launch overhead out of the device timing.
+    # Capture the step in a CUDA graph: host launch overhead out of the device
+    # timing.  A step is `passes` passes over the copies (at least ~1 ms).
     for _ in range(2):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
+    one_pass = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(one_pass, stream=stream):
+        step()
+    passes = passes_for(one_pass, stream, world, device)
+    del one_pass
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
-        step()
+        for _ in range(passes):
+            step()
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
@@ -468,7 +504,7 @@ def run_ours(args, rank: int, world: int):
         kgraph = torch.cuda.CUDAGraph()
         saved = sharded
         with torch.cuda.graph(kgraph, stream=stream):
-            for i in range(copies):
+            for i in [c for _ in range(passes) for c in range(copies)]:
                 w, o = weights[i], outs[i]
                 if kind == "q6k":
                     ops.q6_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
@@ -492,9 +528,9 @@ def run_ours(args, rank: int, world: int):
         ms, kernel_ms = float(t[0].item()), float(t[1].item())
         dist.barrier()
     torch.cuda.synchronize()
-    launch_ms = kernel_ms / copies
+    launch_ms = kernel_ms / (copies * passes)
     achieved = my_bytes / (launch_ms * 1e-3) / 1e9
-    job_ops = copies * (1 if sharded else world)
+    job_ops = copies * passes * (1 if sharded else world)
     value = job_ops * per_op / (ms * 1e-3) / 1e9
 
     # e2e through the public API with host buffers: every step copies its fp32
@@ -567,7 +603,7 @@ def run_ours(args, rank: int, world: int):
         t = torch.tensor([e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
-    e2e_value = job_ops * per_op / (e_ms * 1e-3) / 1e9
+    e2e_value = copies * (1 if sharded else world) * per_op / (e_ms * 1e-3) / 1e9
     derr = ops.device_error()
     if derr:
         raise SystemExit(f"device error word set: {derr:#x}")
@@ -585,7 +621,8 @@ def run_ours(args, rank: int, world: int):
             "higher_is_better": True, "scaling": "strong" if sharded else "weak", "vs_baseline": None,
             "dtype": "u8/s8 dp4a, f64 accumulate", "data": "synthetic (seeded; the reference benchmark's value distributions)",
             "config": matvec_config(args.workload, world, pdl, args.copies),
-            "us_per_op": round(ms * 1e3 / copies, 4),
+            "passes_per_step": passes, "launches_per_step": copies * passes,
+            "us_per_op": round(ms * 1e3 / (copies * passes), 4),
             "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": copies * k * 4,
                     "d2h_bytes_per_step": int(result.numel() * 4), "ms_per_step": round(e_ms, 6),
                     "path": "ops.quantize_q8_1 over a chunk's activations, then ops.<matvec> per launch "
@@ -597,7 +634,7 @@ def run_ours(args, rank: int, world: int):
                          "us_per_launch": round(launch_ms * 1e3, 4)},
             "cpu_baseline": cpu,
             "clocks": clk,
-            "gpu_launches": args.steps * copies,
+            "gpu_launches": args.steps * copies * passes,
         }
         return line
 
@@ -1297,11 +1334,22 @@ def run_imrope_reference(args, rank: int, world: int, batched: bool):
     line = {"metric": metric, "value": round(value, 4), "unit": unit, "impl": "reference", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": c["per_token_s"] * 1e3,
             "higher_is_better": hib, "scaling": "weak", "vs_baseline": None, "dtype": "f64",
-            "data": "synthetic (seeded)", "config": {"workload": "imrope batched" if batched else "imrope 32x128"},
+            "data": "synthetic (seeded)", "config": imrope_config(batched, world),
             "cpu_baseline": {"value": round(value, 4), "unit": unit, "cores": 1, "kind": "port",
                              "sample": c["sample"]},
             "e2e": {"value": round(value, 4), "unit": unit, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+def imrope_config(batched: bool, world: int) -> dict:
+    from mojo_llm_lab_b200 import fixtures as fx
+    tokens = 4096 if batched else 1
+    return {"workload": "imrope batched" if batched else "imrope 32x128", "tokens": tokens, "heads": 32,
+            "bytes_per_op": imrope_bytes(tokens), "positions": list(fx.SEEDED_IMROPE_CASES["distinct_axes"]),
+            "chain": "PDL-chained launches in one CUDA graph",
+            "l2": ("4 copies x 67 MB in > 2x L2; no flush" if batched else
+                   "128 distinct 16 KB inputs (L2-resident, like the reference's graph)"),
+            "parallelism": f"replicas x{world}" if world > 1 else "single GPU"}
+
 
 IMROPE_PUBLISHED_US = 2.072   # reference, Mojo fused kernel on RTX A2000 (README.md:17-21)
 
@@ -1388,15 +1436,23 @@ def run_imrope(args, rank: int, world: int, batched: bool):
     for i in range(copies):
         launch(i)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
+    one_pass = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(one_pass, stream=stream):
         for i in range(copies):
             launch(i)
+    passes = passes_for(one_pass, stream, world, device)  # a step lasts ~1 ms or more
+    del one_pass
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(passes):
+            for i in range(copies):
+                launch(i)
     # The reference's own measurement: serial launches of its entry in a graph.
     serial = torch.cuda.CUDAGraph()
     with torch.cuda.graph(serial, stream=stream):
-        for i in range(copies):
-            launch(i, pdl=False)
+        for _ in range(passes):
+            for i in range(copies):
+                launch(i, pdl=False)
     for _ in range(args.warmup):
         graph.replay()
         serial.replay()
@@ -1407,7 +1463,7 @@ def run_imrope(args, rank: int, world: int, batched: bool):
         serial.replay()
     s1.record(stream)
     torch.cuda.synchronize()
-    serial_us = s0.elapsed_time(s1) / args.steps * 1e3 / copies
+    serial_us = s0.elapsed_time(s1) / args.steps * 1e3 / (copies * passes)
     del serial
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(local) as clocks:
@@ -1422,7 +1478,7 @@ def run_imrope(args, rank: int, world: int, batched: bool):
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    us_op = ms * 1e3 / copies
+    us_op = ms * 1e3 / (copies * passes)
     per_op = imrope_bytes(tokens, heads)
     gbs = per_op / (us_op * 1e-6) / 1e9
 
@@ -1473,20 +1529,14 @@ def run_imrope(args, rank: int, world: int, batched: bool):
             "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
             "scaling": "weak", "vs_baseline": None if batched else round(us_op / IMROPE_PUBLISHED_US, 4),
             "dtype": "f32 in/out, f64 norm and angles", "data": "synthetic (seeded N(0,1) q, U(0.5,1.5) gamma)",
-            "config": {"workload": ("imrope batched" if batched else "imrope 32x128"), "tokens": tokens,
-                       "heads": heads, "launches_per_step": copies, "us_per_op": round(us_op, 4),
-                       "bytes_per_op": per_op, "positions": list(fx.SEEDED_IMROPE_CASES["distinct_axes"]),
-                       "chain": "PDL-chained launches in one CUDA graph",
-                       "us_per_op_serial_graph": round(serial_us, 4),
-                       "l2": ("4 copies x 67 MB in > 2x L2; no flush" if batched else
-                              "128 distinct 16 KB inputs (L2-resident, like the reference's graph)"),
-                       "parallelism": f"replicas x{world}" if world > 1 else "single GPU"},
-            "e2e": e2e,
+            "config": imrope_config(batched, world), "us_per_op": round(us_op, 4),
+            "us_per_op_serial_graph": round(serial_us, 4), "passes_per_step": passes,
+            "launches_per_step": copies * passes, "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 5), "peak_source": peak_kind,
                          "traffic": profiled_traffic("imrope_q_32x128_and_4096_tokens") if batched else None,
                          "kernel": "imrope_q_kernel", "us_per_launch": round(us_op, 4)},
-            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
+            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies * passes}
     return line
 
 
@@ -1541,7 +1591,7 @@ def run_q8_1_reference(args, rank: int, world: int, batched: bool):
 def q8_1_config(batched: bool, k: int, world: int) -> dict:
     tokens = Q8_1_TOKENS_BATCHED if batched else 1
     copies = 6 if batched else 128
-    return {"workload": q8_1_describe(batched, k), "k": k, "tokens": tokens, "launches_per_step": copies,
+    return {"workload": q8_1_describe(batched, k), "k": k, "tokens": tokens, "inputs": copies,
             "bytes_per_op": q8_1_bytes_per_op(k, tokens),
             "l2": (f"{copies} inputs x {tokens * k * 4 / 2**20:.0f} MiB > 2x L2; no flush" if batched else
                    f"{copies} distinct {k * 4 // 1024} KB inputs (L2-resident, as a decode step's activations)"),
@@ -1566,7 +1616,7 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
     k = args.k
     tokens = Q8_1_TOKENS_BATCHED if batched else 1
     cfg = q8_1_config(batched, k, world)
-    copies = cfg["launches_per_step"]
+    copies = cfg["inputs"]
     stream = torch.cuda.Stream(device)
     torch.cuda.set_stream(stream)
     gen = torch.Generator(device=device)
@@ -1589,10 +1639,17 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
     for i in range(copies):
         launch(i)
     torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph, stream=stream):
+    one_pass = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(one_pass, stream=stream):
         for i in range(copies):
             launch(i)
+    passes = passes_for(one_pass, stream, world, device)  # a step lasts ~1 ms or more
+    del one_pass
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(passes):
+            for i in range(copies):
+                launch(i)
     for _ in range(args.warmup):
         graph.replay()
     torch.cuda.synchronize()
@@ -1609,7 +1666,7 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
         t = torch.tensor([ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    us_op = ms * 1e3 / copies
+    us_op = ms * 1e3 / (copies * passes)
     per_op = q8_1_bytes_per_op(k, tokens)
     gbs = per_op / (us_op * 1e-6) / 1e9
 
@@ -1650,16 +1707,17 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
         e2e = {"value": round(e_us, 3), "unit": "us/op"}
     e2e.update({"h2d_bytes_per_step": tokens * k * 4, "d2h_bytes_per_step": tokens * k // 32 * 36,
                 "path": "ops.quantize_q8_1 with pinned H2D/D2H, eager, one op per step"})
-    cfg["us_per_op"] = round(us_op, 4)
+
     line = {"metric": f"{q8_1_describe(batched, k)} {unit}", "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32 -> s8 + f16", "data": "synthetic (seeded N(0,1))",
-            "config": cfg, "e2e": e2e,
+            "config": cfg, "us_per_op": round(us_op, 4), "passes_per_step": passes,
+            "launches_per_step": copies * passes, "e2e": e2e,
             "roofline": {"bound": "hbm", "achieved": round(gbs, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(gbs / peak, 5), "peak_source": peak_kind,
                          "traffic": profiled_traffic("q8_1_quantize_k2560_and_4096x2560") if batched else None,
                          "kernel": "q8_1_quantize_x4_kernel", "us_per_launch": round(us_op, 4)},
-            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies}
+            "cpu_baseline": cpu, "clocks": clocks.summary(), "gpu_launches": args.steps * copies * passes}
     return line
 
 
@@ -1754,7 +1812,8 @@ def other_configs(args, rank: int, world: int, which) -> dict:
                "imrope_batched": lambda a, r, w: run_imrope(a, r, w, batched=True),
                "q8_1": lambda a, r, w: run_q8_1(a, r, w, batched=False)}
     keep = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "higher_is_better", "vs_baseline", "dtype",
-            "config", "e2e", "roofline", "clocks", "gpu_launches", "us_per_op")
+            "config", "e2e", "roofline", "clocks", "gpu_launches", "us_per_op", "passes_per_step",
+            "launches_per_step")
     out = {}
     for name, over in which:
         sub = argparse.Namespace(**vars(args))

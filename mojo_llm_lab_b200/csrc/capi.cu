@@ -561,7 +561,8 @@ int mllb_rmsnorm_imrope_q_batched_ex(const float* q, const float* gamma, const i
   const int64_t per_cta = heads_per_token < mllb::kImropeMaxHeadsPerCta ? heads_per_token : mllb::kImropeMaxHeadsPerCta;
   const int64_t grid = tokens * ((heads_per_token + per_cta - 1) / per_cta);
   if (grid > 0x7fffffff) return fail(MLLB_EUNSUPPORTED, "too many heads");
-  return launched(launch(mllb::imrope_q_kernel, dim3(static_cast<unsigned>(grid)), dim3(static_cast<unsigned>(per_cta * 32)),
+  return launched(launch(tokens > 1 ? mllb::imrope_q_kernel<true> : mllb::imrope_q_kernel<false>,
+                         dim3(static_cast<unsigned>(grid)), dim3(static_cast<unsigned>(per_cta * 32)),
                          0, static_cast<cudaStream_t>(stream), flags & MLLB_LAUNCH_PDL, q, gamma, positions,
                          theta_scale, theta_value, out, tokens, heads_per_token,
                          (flags & MLLB_LAUNCH_CONST_AUX) ? 1 : 0),

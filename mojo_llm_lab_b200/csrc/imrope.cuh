@@ -88,6 +88,28 @@ __device__ __forceinline__ void imrope_head_regs(float x0, float x1, float x2, f
   }
 }
 
+// imrope_head_regs with gamma already in fp64 (gd[i] = gamma[i], shared by
+// the CTA's heads, converted once per CTA).
+__device__ __forceinline__ void imrope_head_regs_gd(float x0, float x1, float x2, float x3, const double* gd,
+                                                    const double2* rot, int lane, double (&o)[4]) {
+  const double xd[4] = {static_cast<double>(x0), static_cast<double>(x1), static_cast<double>(x2),
+                        static_cast<double>(x3)};
+  double ss = xd[0] * xd[0];
+  ss = fma(xd[1], xd[1], ss);
+  ss = fma(xd[2], xd[2], ss);
+  ss = fma(xd[3], xd[3], ss);
+  ss = warp_sum_double(ss);
+  const double r = 1.0 / sqrt(ss / kHeadDim + 1e-6);
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const double2 cs = rot[lane + 32 * half];
+    const double ya = xd[half] * r * gd[lane + 32 * half];
+    const double yb = xd[2 + half] * r * gd[lane + 64 + 32 * half];
+    o[2 * half] = ya * cs.x - yb * cs.y;
+    o[2 * half + 1] = ya * cs.y + yb * cs.x;
+  }
+}
+
 // imrope_head_regs loading the head's values itself.
 __device__ __forceinline__ void imrope_head_table(const float* __restrict__ x, const float* __restrict__ gamma,
                                                   const double2* rot, int lane, double (&o)[4]) {
@@ -121,11 +143,17 @@ __device__ __forceinline__ void imrope_head_warp(const float* __restrict__ x, co
 // waits for the preceding kernel.
 constexpr int kImropeMaxHeadsPerCta = 8;
 
+// kGammaShared (the many-token form): gamma converted to fp64 once per CTA
+// into shared memory, which takes a third of the conversion-unit work (that
+// form's limit) off the heads; one token keeps gamma in each lane's
+// registers, loaded before the wait, so nothing is added after it.
+template <bool kGammaShared>
 __global__ void __launch_bounds__(kImropeMaxHeadsPerCta * 32) imrope_q_kernel(
     const float* __restrict__ q, const float* __restrict__ gamma, const int32_t* __restrict__ positions,
     const float* __restrict__ theta_ptr, double theta_value, float* __restrict__ out, int64_t tokens,
     int64_t heads_per_token, int early_aux) {
   __shared__ double2 rot[kHeadDim / 2];
+  __shared__ double gd[kGammaShared ? kHeadDim : 1];  // gamma in fp64, converted once per CTA
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int heads_per_cta = static_cast<int>(blockDim.x >> 5);
   const int64_t ctas_per_token = (heads_per_token + heads_per_cta - 1) / heads_per_cta;
@@ -136,7 +164,11 @@ __global__ void __launch_bounds__(kImropeMaxHeadsPerCta * 32) imrope_q_kernel(
   float g0 = 0.0f, g1 = 0.0f, g2 = 0.0f, g3 = 0.0f;
   auto build_table = [&] {
     if (token < tokens) {
-      g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
+      if constexpr (kGammaShared) {
+        for (int i = threadIdx.x; i < kHeadDim; i += blockDim.x) gd[i] = static_cast<double>(gamma[i]);
+      } else {
+        g0 = gamma[lane], g1 = gamma[lane + 32], g2 = gamma[lane + 64], g3 = gamma[lane + 96];
+      }
       for (int p = threadIdx.x; p < kHeadDim / 2; p += blockDim.x) {
         const double theta = theta_ptr ? static_cast<double>(*theta_ptr) : theta_value;
         const int32_t* pos = positions + 4 * token;
@@ -156,7 +188,8 @@ __global__ void __launch_bounds__(kImropeMaxHeadsPerCta * 32) imrope_q_kernel(
   __syncthreads();
   if (!active) return;
   double o[4];
-  imrope_head_regs(x0, x1, x2, x3, g0, g1, g2, g3, rot, lane, o);
+  if constexpr (kGammaShared) imrope_head_regs_gd(x0, x1, x2, x3, gd, rot, lane, o);
+  else imrope_head_regs(x0, x1, x2, x3, g0, g1, g2, g3, rot, lane, o);
   float* dst = out + head * kHeadDim;
   dst[lane] = static_cast<float>(o[0]);
   dst[lane + 64] = static_cast<float>(o[1]);

@@ -63,3 +63,13 @@ def test_reference_arm_reports_every_cpu_arm_and_the_gpu_arms_config():
     assert [o["cores"] for o in others] == [1, 1]
     assert "pyport" in others[1]["sample"] and all(o["value"] > 0 for o in others)
     assert line["config"] == bench.matvec_config("q4k_matvec", 1, True)
+
+
+@pytest.mark.parametrize("workload,config", [
+    ("imrope", lambda bench: bench.imrope_config(False, 1)),
+    ("q8_1", lambda bench: bench.q8_1_config(False, 2560, 1)),
+])
+def test_reference_arm_config_is_the_gpu_arms(workload, config):
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert run_bench(["--workload", workload])[0]["config"] == config(bench)
