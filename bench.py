@@ -66,7 +66,7 @@ WORKLOADS = {
     "q5k_matvec": dict(kind="q5k", rows=4096, k=2560, kernel="team_stream_kernel<Q5kFormat,10,1,8,2,2>",
                        profile="q5k_matvec_n4096_k2560"),
     # Q6_K vocabulary projection 151936x2560
-    "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,8,6>",
+    "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,6,5>",
                       profile="q6k_vocab_n151936_k2560"),
 }
 

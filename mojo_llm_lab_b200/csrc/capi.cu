@@ -74,7 +74,7 @@
 #define MLLB_CFG_Q6K_8 4, 8, 6
 #endif
 #ifndef MLLB_CFG_Q6K_10
-#define MLLB_CFG_Q6K_10 4, 8, 6
+#define MLLB_CFG_Q6K_10 4, 6, 5
 #endif
 #ifndef MLLB_CFG_Q6K_16
 #define MLLB_CFG_Q6K_16 4, 6, 3

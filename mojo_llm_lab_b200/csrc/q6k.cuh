@@ -9,17 +9,23 @@
 //   q6 = nibble(ql[64h + 32*(k&1) + l], k>>1) | bits(qh[32h + l], 2k) << 4.
 //
 // Same streaming structure as the Q4_K kernel (persistent CTAs, TMA bulk
-// copies of 16-row tiles into a 3-stage shared-memory ring, activation quants
-// resident in registers).  Work unit = 8 consecutive l of one (half h,
-// 16-column run): 8 bytes each of ql-low, ql-high and qh feed 32 weights in
-// four Q8_1 groups.  Blocks start every 210 bytes, so odd blocks sit 2 bytes
-// off a word boundary in shared memory; each 8-byte field is read as three
-// aligned words and funnel-shifted.  q6 stays unsigned in dp4a.u32.s32 and
-// the -32 offset enters as the accumulator start -32 * sum(a).  Lane pairs
-// hold the two 8-column halves of a 16-column run (same scale); one shuffle
-// per group pair completes each group's integer sum, then each lane forms two
-// groups' fp64 terms (exact products) -- so, as for Q4_K, the row sum is the
-// exactly rounded value before the final fp32 rounding.
+// copies of row tiles into a shared-memory ring, activation quants resident
+// in registers).  Work unit = one 16-column run of one half h: 16 bytes each
+// of ql-low, ql-high and qh feed 64 weights in four Q8_1 groups, one scale
+// each, so a lane finishes its four groups alone.  Blocks start every 210
+// bytes, so odd blocks sit 2 bytes off a word boundary in shared memory; each
+// 16-byte field is read as five aligned words and funnel-shifted (rows are
+// whole words apart, so a lane's word offsets and shift are the same in every
+// row).  The q6 bytes of a group are one bit-select of a nibble word and a
+// shifted high-pair word under the nibble mask:
+//   k0: ql-low  & 0x0f | qh bits 0-1 << 4    k1: ql-high & 0x0f | qh bits 2-3 << 2
+//   k2: ql-low >> 4    | qh bits 4-5         k3: ql-high >> 4   | qh bits 6-7 >> 2
+// with qh pre-masked to its (0-1, 4-5) and (2-3, 6-7) pairs so no shifted
+// neighbour bit survives the select.  q6 stays unsigned in dp4a.u32.s32 and
+// the -32 offset enters as the accumulator start -32 * sum(a).  Each group's
+// integer sum times its scale is exact; the fp64 terms are exact products, so
+// the row sum is the exactly rounded value to ~1e-16 before the final fp32
+// rounding.
 #pragma once
 
 #include "common.cuh"
@@ -29,34 +35,35 @@ namespace mllb {
 
 constexpr int kQ6kBlockBytes = 210;
 
-// Two words from an 8-byte field that starts 0 or 2 bytes past a word
-// boundary (sh = 0 or 16 bits).
-__device__ __forceinline__ void load_field8(const uint8_t* p, uint32_t sh, uint32_t* x0, uint32_t* x1) {
-  const uint32_t* a = reinterpret_cast<const uint32_t*>(reinterpret_cast<uintptr_t>(p) & ~uintptr_t(3));
-  const uint32_t w0 = a[0], w1 = a[1], w2 = a[2];
-  *x0 = __funnelshift_r(w0, w1, sh);
-  *x1 = __funnelshift_r(w1, w2, sh);
-}
-
-// Integer partial sums t[k] = sc_k * sum(q6 * a) - 32 * sc_k * sum(a) over
-// the unit's 8 columns of groups 4h+k (c[k] = -32 * sum(a) is precomputed).
-__device__ __forceinline__ void q6k_unit_ints(const uint8_t* blk, int h, int l0, const uint32_t (&a)[4][2],
-                                              const int (&c)[4], int (&t)[4]) {
-  const uint32_t sh = (reinterpret_cast<uintptr_t>(blk) & 2u) ? 16u : 0u;
-  uint32_t lo0, lo1, hi0, hi1, qh0, qh1;
-  load_field8(blk + 64 * h + l0, sh, &lo0, &lo1);
-  load_field8(blk + 64 * h + 32 + l0, sh, &hi0, &hi1);
-  load_field8(blk + 128 + 32 * h + l0, sh, &qh0, &qh1);
-  const int8_t* sc = reinterpret_cast<const int8_t*>(blk + 192 + 8 * h + (l0 >> 4));
-  const uint32_t m4 = 0x0f0f0f0fu, m2 = 0x30303030u;
-  const uint32_t q00 = (lo0 & m4) | ((qh0 << 4) & m2), q01 = (lo1 & m4) | ((qh1 << 4) & m2);
-  const uint32_t q10 = (hi0 & m4) | ((qh0 << 2) & m2), q11 = (hi1 & m4) | ((qh1 << 2) & m2);
-  const uint32_t q20 = ((lo0 >> 4) & m4) | (qh0 & m2), q21 = ((lo1 >> 4) & m4) | (qh1 & m2);
-  const uint32_t q30 = ((hi0 >> 4) & m4) | ((qh0 >> 2) & m2), q31 = ((hi1 >> 4) & m4) | ((qh1 >> 2) & m2);
-  t[0] = static_cast<int>(sc[0]) * dp4a_us(q01, a[0][1], dp4a_us(q00, a[0][0], c[0]));
-  t[1] = static_cast<int>(sc[2]) * dp4a_us(q11, a[1][1], dp4a_us(q10, a[1][0], c[1]));
-  t[2] = static_cast<int>(sc[4]) * dp4a_us(q21, a[2][1], dp4a_us(q20, a[2][0], c[2]));
-  t[3] = static_cast<int>(sc[6]) * dp4a_us(q31, a[3][1], dp4a_us(q30, a[3][0], c[3]));
+// The four groups' raw integer dots of a 16-column run (the streaming
+// kernel's unit): u[k] = sum(q6 * a) - 32 * sum(a) over columns
+// [l0, l0 + 16) of group 4h + k (c[k] = -32 * sum(a) precomputed).  `lo_w`
+// is the word holding the run's first ql-low byte (its ql-high bytes lie 32
+// bytes on, at the same alignment), `qh_w` the word of its first qh byte;
+// each field starts sh = 0 or 16 bits past its word.
+__device__ __forceinline__ void q6k_run_dots(const uint8_t* lo_w, const uint8_t* qh_w, uint32_t sh,
+                                             const uint32_t (&a)[4][4], const int (&c)[4], int (&u)[4]) {
+  const uint32_t* pl = reinterpret_cast<const uint32_t*>(lo_w);
+  const uint32_t* ph = reinterpret_cast<const uint32_t*>(qh_w);
+  const uint32_t m4 = 0x0f0f0f0fu;
+  int acc[4] = {c[0], c[1], c[2], c[3]};
+  uint32_t lw = pl[0], hw = pl[8], qw = ph[0];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t ln = pl[j + 1], hn = pl[j + 9], qn = ph[j + 1];
+    const uint32_t lo = __funnelshift_r(lw, ln, sh), hi = __funnelshift_r(hw, hn, sh);
+    const uint32_t qh = __funnelshift_r(qw, qn, sh);
+    lw = ln;
+    hw = hn;
+    qw = qn;
+    const uint32_t qa = qh & 0x33333333u, qb = qh & 0xccccccccu;
+    acc[0] = dp4a_us((lo & m4) | ((qa << 4) & ~m4), a[0][j], acc[0]);
+    acc[1] = dp4a_us((hi & m4) | ((qb << 2) & ~m4), a[1][j], acc[1]);
+    acc[2] = dp4a_us(((lo >> 4) & m4) | (qa & ~m4), a[2][j], acc[2]);
+    acc[3] = dp4a_us(((hi >> 4) & m4) | ((qb >> 2) & ~m4), a[3][j], acc[3]);
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) u[k] = acc[k];
 }
 
 // Row-per-CTA fallback for any K and any row count (plain global loads; the

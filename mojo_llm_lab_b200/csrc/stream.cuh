@@ -110,6 +110,7 @@ enum : int { kEpiNone = 0, kEpiQuantProduct = 1, kEpiResidualNorm = 2, kEpiQuant
 // Q4_K: unit = 16 nibble bytes (halves h of groups 2j, 2j+1 of a super-block).
 struct Q4kFormat {
   static constexpr int kBlockBytes = kQ4kBlockBytes;
+  static constexpr int kUnitsPerBlock = 8;
   static constexpr int kDecBytes = 32;  // per super-block: fp64 d, dmin, (scale,min) x 8
 
   template <int NB>
@@ -193,6 +194,7 @@ struct Q4kFormat {
 // dp4a, so the dots are exact integers of the 5-bit quants.
 struct Q5kFormat {
   static constexpr int kBlockBytes = 176;
+  static constexpr int kUnitsPerBlock = 8;
   static constexpr int kDecBytes = 32;
 
   template <int NB>
@@ -258,22 +260,34 @@ struct Q5kFormat {
   }
 };
 
-// Q6_K: unit = 8 consecutive l of one (half, 16-column run): 32 weights in
-// four Q8_1 groups; lane pairs hold the two 8-column halves of a run.
+// Q6_K: unit = one 16-column run of one half: columns [l0, l0 + 16) of the
+// four Q8_1 groups 4h + k (64 weights, one scale per group); a lane finishes
+// its groups alone, so no lane exchange.
 struct Q6kFormat {
   static constexpr int kBlockBytes = kQ6kBlockBytes;
-  static constexpr int kDecBytes = 8;  // per super-block: fp64 d
+  static constexpr int kUnitsPerBlock = 4;
+  // No header stage: a unit reads its block's fp16 d itself (one 2-byte load
+  // per row), so a tile needs no decode pass and no team barrier before it.
+  static constexpr int kDecBytes = 0;
 
   template <int NB>
   struct ActLayout {  // raw Q8_1 copy
     static constexpr int kBytes = (NB * 8 * kQ8BlockBytes + 15) / 16 * 16;
   };
 
+  // A lane's unit in every row: its quants, group sums and deltas, and the
+  // offsets of its fields from the row start (rows of an even number of
+  // 210-byte blocks are whole words apart in the stage, so the offsets and
+  // the shift hold for every row).
   struct Slot {
-    uint32_t a[4][2];
-    int c[4];
-    double da, db;
-    int blk_off, h, l0, odd;
+    uint32_t a[4][4];  // group 4h + k, columns l0 .. l0 + 15
+    int c[4];          // -32 * sum of those quants
+    double dl[4];      // the groups' Q8_1 deltas
+    int lo_off;        // word holding the first ql-low byte
+    int qh_off;        // word holding the first qh byte
+    int sc_off;        // scale of group 4h (groups 4h + k: + 2k)
+    int d_off;         // fp16 d of the block
+    uint32_t sh;       // bit offset of the fields in their words: 0 or 16
   };
 
   template <int NB>
@@ -290,37 +304,44 @@ struct Q6kFormat {
 
   template <int NB>
   __device__ static Slot load_slot(const uint8_t* act, int p) {
+    static_assert(NB % 2 == 0, "rows must be whole words apart in the stage");
     Slot sl;
-    const int b = p >> 3, u8 = p & 7;
-    sl.h = u8 >> 2;
-    sl.l0 = ((u8 >> 1) & 1) * 16 + (u8 & 1) * 8;
-    sl.odd = u8 & 1;
-    sl.blk_off = b * kBlockBytes;
+    const int b = p >> 2, u = p & 3;
+    const int h = u >> 1, l0 = (u & 1) * 16;
+    const int blk_off = b * kBlockBytes;
+    sl.lo_off = (blk_off + 64 * h + l0) & ~3;
+    sl.qh_off = (blk_off + 128 + 32 * h + l0) & ~3;
+    sl.sc_off = blk_off + 192 + 8 * h + (l0 >> 4);
+    sl.d_off = blk_off + 208;
+    sl.sh = (blk_off & 2) ? 16u : 0u;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const uint8_t* g = act + (b * 8 + 4 * sl.h + k) * kQ8BlockBytes + 4 + sl.l0;
-      sl.a[k][0] = lds32(g);
-      sl.a[k][1] = lds32(g + 4);
-      sl.c[k] = -32 * byte_sum_s8(sl.a[k][1], byte_sum_s8(sl.a[k][0], 0));
+      const uint8_t* g = act + (b * 8 + 4 * h + k) * kQ8BlockBytes;
+      int sum = 0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sl.a[k][i] = lds32(g + 4 + l0 + 4 * i);
+        sum = byte_sum_s8(sl.a[k][i], sum);
+      }
+      sl.c[k] = -32 * sum;
+      sl.dl[k] = half_bits_to_double(lds32(g) & 0xffffu);
     }
-    const uint8_t* ga = act + (b * 8 + 4 * sl.h + 2 * sl.odd) * kQ8BlockBytes;
-    sl.da = half_bits_to_double(lds32(ga) & 0xffffu);
-    sl.db = half_bits_to_double(lds32(ga + kQ8BlockBytes) & 0xffffu);
     return sl;
   }
 
-  __device__ static void decode(const uint8_t* raw_block, uint8_t* dec) {
-    *reinterpret_cast<double*>(dec) = half_bits_to_double(*reinterpret_cast<const unsigned short*>(raw_block + 208));
-  }
+  __device__ static void decode(const uint8_t*, uint8_t*) {}
 
-  __device__ static double term(const uint8_t* row_raw, const uint8_t* row_dec, const Slot& sl) {
-    int t[4];
-    q6k_unit_ints(row_raw + sl.blk_off, sl.h, sl.l0, sl.a, sl.c, t);
-    // Even lanes finish groups 0,1 of the unit, odd lanes groups 2,3.
-    const int m0 = (sl.odd ? t[2] : t[0]) + __shfl_xor_sync(0xffffffffu, sl.odd ? t[0] : t[2], 1);
-    const int m1 = (sl.odd ? t[3] : t[1]) + __shfl_xor_sync(0xffffffffu, sl.odd ? t[1] : t[3], 1);
-    const double d = *reinterpret_cast<const double*>(row_dec + (sl.blk_off / kBlockBytes) * kDecBytes);
-    return d * fma(i2d_exact(m0), sl.da, i2d_exact(m1) * sl.db);
+  __device__ static double term(const uint8_t* row_raw, const uint8_t*, const Slot& sl) {
+    int u[4];
+    q6k_run_dots(row_raw + sl.lo_off, row_raw + sl.qh_off, sl.sh, sl.a, sl.c, u);
+    const int8_t* sc = reinterpret_cast<const int8_t*>(row_raw + sl.sc_off);
+    // Each group's integer sum times its scale is exact in int32 (|.| < 2^24)
+    // and in fp64; the four products, then d, each take one fp64 rounding.
+    double t = static_cast<double>(static_cast<int>(sc[0]) * u[0]) * sl.dl[0];
+#pragma unroll
+    for (int k = 1; k < 4; ++k) t = fma(static_cast<double>(static_cast<int>(sc[2 * k]) * u[k]), sl.dl[k], t);
+    const double d = half_bits_to_double(*reinterpret_cast<const unsigned short*>(row_raw + sl.d_off));
+    return d * t;
   }
 };
 
@@ -398,7 +419,7 @@ __device__ __forceinline__ void produce_activation(const ActSource& src, uint8_t
 
 template <class Fmt, int NB, int MATS, int V, int S, int TEAMS>
 struct TeamConfig {
-  static constexpr int kP = NB * 8;                          // units per row
+  static constexpr int kP = NB * Fmt::kUnitsPerBlock;        // units per row
   static constexpr int kRG = 32 / gcd_constexpr(kP, 32);     // rows per row group
   static constexpr int kW = kP * kRG / 32;                   // consumer warps per team
   static constexpr int kConsumers = TEAMS * kW * 32;
@@ -408,7 +429,10 @@ struct TeamConfig {
   static constexpr int kTileBytes = kT * kRowBytes;          // per matrix
   static constexpr int kStageBytes = kTileBytes * MATS;
   static constexpr int kDecTile = MATS * kT * NB * Fmt::kDecBytes;  // decoded headers of one tile
-  static constexpr int kSegs = 2 * kW;                       // half-warp partial segments
+  // Lanes per partial segment: a half-warp, or 8 lanes when rows do not
+  // start on half-warps (the V = 4 reduction then stops after lane bit 2).
+  static constexpr int kSegLanes = kP % 16 == 0 ? 16 : 8;
+  static constexpr int kSegs = (32 / kSegLanes) * kW;        // partial segments per team
   static constexpr int kTeamPartials = 2 * MATS * kT * kSegs;  // doubles, double-buffered
   static constexpr int kDecOffset = S * kStageBytes;                 // one decode buffer per team
   static constexpr int kActOffset = kDecOffset + TEAMS * kDecTile;
@@ -422,6 +446,7 @@ struct TeamConfig {
   static constexpr int kMinBlocks = kSmemBytes <= 112 * 1024 ? 2 : 1;
   static_assert(kStageBytes % 16 == 0 && kTileBytes % 16 == 0, "TMA tiles must be whole 16-byte runs");
   static_assert(V == 4 || V == 8, "row groups per tile");
+  static_assert(kP % 8 == 0 && (kSegLanes == 16 || V == 4), "rows start on 8-lane segments; V = 8 needs 16");
   static_assert(kT <= 32, "one lane per row in the final combine");
   static_assert(kThreads <= 1024 && TEAMS + 1 < 16, "CTA size / named barriers");
   // A team waits on the ready barrier of tile k only after its previous tile
@@ -574,12 +599,16 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
   const int r_in_group = vp / P;
   const typename Fmt::Slot slot = Fmt::template load_slot<NB>(act, vp % P);
   const int f = (lane >> 1) & (V - 1);  // row-group visiting order
-  // Half-warps with the same row-in-group are combined before the partials.
-  const bool merge_halves = (twarp * 32) / P == (twarp * 32 + 16) / P;
-  const int seg = 2 * twarp + (merge_halves ? 0 : (lane >> 4));
+  // Half-warps with the same row-in-group are combined before the partials
+  // (16-lane segments; with 8-lane segments each keeps its own partial).
+  constexpr int SL = C::kSegLanes;
+  const bool merge_halves = SL == 16 && (twarp * 32) / P == (twarp * 32 + 16) / P;
+  const int seg = SL == 16 ? 2 * twarp + (merge_halves ? 0 : (lane >> 4)) : 4 * twarp + (lane >> 3);
   // One lane per (row, segment) writes: bit 0 and the lane bits outside f(l)
   // must be zero; bit 4 selects the half unless the halves were merged.
-  const bool writer = (lane & 1) == 0 && (lane & (0x0e & ~((V - 1) << 1))) == 0 && (!merge_halves || lane < 16);
+  const bool writer = SL == 16 ? (lane & 1) == 0 && (lane & (0x0e & ~((V - 1) << 1))) == 0 &&
+                                     (!merge_halves || lane < 16)
+                               : (lane & 1) == 0;
   double* partials = reinterpret_cast<double*>(smem + C::kPartOffset) + team * C::kTeamPartials;
   uint8_t* dec = smem + C::kDecOffset + team * C::kDecTile;
   const int team_barrier = 2 + team;
@@ -596,15 +625,17 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
     const int parity = (k / TEAMS) & 1;
     double* part = partials + parity * (MATS * T * C::kSegs);
     const uint8_t* stage = smem + s * C::kStageBytes;
-    if (have) {
-      // The team decodes this tile's super-block headers (about one per lane).
-      const int rows = min(T, n_rows - tile * T);
-      for (int e = vp; e < MATS * T * NB; e += W * 32) {
-        const int m = e / (T * NB), rest = e % (T * NB), row = rest / NB, b = rest % NB;
-        if (row < rows) Fmt::decode(stage + m * C::kTileBytes + row * ROWB + b * Fmt::kBlockBytes, dec + e * DECB);
+    if constexpr (DECB > 0) {
+      if (have) {
+        // The team decodes this tile's super-block headers (about one per lane).
+        const int rows = min(T, n_rows - tile * T);
+        for (int e = vp; e < MATS * T * NB; e += W * 32) {
+          const int m = e / (T * NB), rest = e % (T * NB), row = rest / NB, b = rest % NB;
+          if (row < rows) Fmt::decode(stage + m * C::kTileBytes + row * ROWB + b * Fmt::kBlockBytes, dec + e * DECB);
+        }
       }
+      named_barrier(team_barrier, W * 32);
     }
-    named_barrier(team_barrier, W * 32);
     if (have) {
       double v[MATS][V];
 #pragma unroll
@@ -626,14 +657,17 @@ __global__ void __launch_bounds__(TeamConfig<Fmt, NB, MATS, V, S, TEAMS>::kThrea
           for (int t = 0; t < half; ++t) v[m][t] += __shfl_xor_sync(0xffffffffu, v[m][t + half], off);
         double x = v[m][0];
         x += __shfl_xor_sync(0xffffffffu, x, 1);
-        if (V == 4) x += __shfl_xor_sync(0xffffffffu, x, 8);
+        if (V == 4 && SL == 16) x += __shfl_xor_sync(0xffffffffu, x, 8);
         if (merge_halves) x += __shfl_xor_sync(0xffffffffu, x, 16);
         if (writer) part[(m * T + f * RG + r_in_group) * C::kSegs + seg] = x;
       }
     }
     named_barrier(team_barrier, W * 32);
     if (*abort_flag) break;
-    if (twarp == 0) {
+    // The warp that adds the tile's partials: warp 0 when a header pass
+    // follows (it overlaps the others' decoding of the next tile); otherwise
+    // each warp in turn, so no warp lags the team by every tile's sum.
+    if (twarp == (DECB > 0 ? 0 : (k / TEAMS) % W)) {
       double sq = 0.0;  // kEpiResidualNorm: h^2 of this lane's row
       if (lane < T) {
         const int row = tile * T + lane;
