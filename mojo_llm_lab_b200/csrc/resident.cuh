@@ -11,17 +11,20 @@
 //   Before griddepcontrol.wait, one thread brings the run into shared memory
 //   with a single cp.async.bulk (R x NB x 144 bytes, L2 evict-first), and
 //   every lane decodes the 6-bit (scale, min) pair of the groups it
-//   finalises into exact fp32 products d*sc and dmin*m (11 + 6 significant
-//   bits) and (NB = 10) loads its weight nibbles into registers.  The CTA triggers
-//   launch_dependents at once, so the next launch of a chain starts its own
-//   prefetch on the SM's second CTA slot while this one waits and computes.
+//   finalises into exact products d*sc and dmin*m (11 + 6 significant bits),
+//   held in fp64 with the 1/16 of its unshifted high nibbles folded into
+//   d*sc, and (NB = 10) loads its weight nibbles into registers.  The CTA
+//   triggers launch_dependents at once, so the next launch of a chain starts
+//   its own prefetch on the SM's second CTA slot while this one waits and
+//   computes.
 // * After the wait only activation-dependent work remains: one thread per
 //   Q8_1 group re-lays the activation into shared memory (its 32 quants at a
-//   bank-spread 16-byte-aligned slot, then fp32 delta and the exact int sum
-//   of its quants), one CTA barrier, and each lane reads per unit two 16-byte
-//   quant vectors and one (delta, sum) pair, forms 8 dp4a, swaps one partial
-//   dot with its partner lane, adds its terms in fp64, and the half-warp
-//   reduces by xor-shuffles; lane 0 stores the row.
+//   bank-spread 16-byte-aligned slot, then its fp64 delta and the exact int
+//   sum of its quants), one CTA barrier, and each lane reads per unit two
+//   16-byte quant vectors, a delta and a sum, forms 8 dp4a, swaps one partial
+//   dot with its partner lane, adds its terms in fp64 (no conversion after
+//   the wait but the exact int -> fp64 adds), and the half-warp reduces by
+//   xor-shuffles; lane 0 stores the row.
 //
 // Layout: a half-warp per row (warp w: rows 2w, 2w+1), 16 lanes x NB/2 units
 // of 16 nibble bytes.  Lane l16 (h = l16 & 1, m = l16 >> 1) takes the units
@@ -44,6 +47,11 @@
 
 namespace mllb {
 
+// Units per lane up to which a lane keeps its weight nibbles in registers.
+#ifndef MLLB_RESIDENT_WQ_REGS_MAX
+#define MLLB_RESIDENT_WQ_REGS_MAX 5
+#endif
+
 constexpr int kResidentMaxRowsPerCta = 32;
 constexpr int kResidentThreads = 32 * (kResidentMaxRowsPerCta / 2);
 
@@ -56,7 +64,7 @@ template <int NB>
 struct ResidentAct {
   static constexpr int kGroups = NB * 8;
   static constexpr int kQuantBytes = resident_act_slot(kGroups);
-  static constexpr int kBytes = kQuantBytes + kGroups * 8;  // + (fp32 delta, int32 sum q) per group
+  static constexpr int kBytes = kQuantBytes + kGroups * 12;  // + fp64 delta, then int32 sum q, per group
 };
 
 template <int NB>
@@ -70,7 +78,8 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
   __shared__ __align__(16) uint8_t act[ResidentAct<NB>::kBytes];
-  float2* act_ds = reinterpret_cast<float2*>(act + ResidentAct<NB>::kQuantBytes);  // (delta, sum q as int bits)
+  double* act_delta = reinterpret_cast<double*>(act + ResidentAct<NB>::kQuantBytes);
+  int* act_sum = reinterpret_cast<int*>(act + ResidentAct<NB>::kQuantBytes + G * 8);
 
   MLLB_TRACE_POINT(0);
   const int row0 = blockIdx.x * rows_per_cta;
@@ -101,9 +110,9 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
   const uint8_t* row = smem + (r < rows ? r : rows - 1) * ROWB;
   // Nibbles in registers before the wait when they fit the 64-register
   // budget (NB = 10); wider rows re-read them from shared memory after it.
-  constexpr bool kWeightsInRegs = UPL <= 5;
+  constexpr bool kWeightsInRegs = UPL <= MLLB_RESIDENT_WQ_REGS_MAX;
   uint4 wq[kWeightsInRegs ? UPL : 1];
-  float dsc[UPL], dmn[UPL];
+  double dsc[UPL], dmn[UPL];
 #pragma unroll
   for (int i = 0; i < UPL; ++i) {
     const int q = m + 8 * i, b = q >> 2, j = q & 3, s = 2 * j + h;
@@ -120,8 +129,13 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
       mn = (sm[s + 4] >> 4) | ((sm[s] >> 6) << 4);
     }
     // fp16 d (11 significant bits) x 6-bit scale: exact in fp32.
-    dsc[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu))) * static_cast<float>(sc);
-    dmn[i] = __half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16))) * static_cast<float>(mn);
+    // The lane's high-nibble dots are 16x (unshifted nibbles): 1/16 enters
+    // its d * sc here, exactly, so no conversion or scaling remains after
+    // the wait.
+    dsc[i] = static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu))) *
+                                 static_cast<float>(sc)) * (h ? 0.0625 : 1.0);
+    dmn[i] = static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16))) *
+                                 static_cast<float>(mn));
   }
 
   pdl_wait_prerequisite();  // the activation may come from the preceding kernel
@@ -139,8 +153,8 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
     uint4* dst = reinterpret_cast<uint4*>(act + resident_act_slot(g));
     dst[0] = make_uint4(v[1], v[2], v[3], v[4]);
     dst[1] = make_uint4(v[5], v[6], v[7], v[8]);
-    act_ds[g] = make_float2(__half2float(__ushort_as_half(static_cast<unsigned short>(v[0] & 0xffffu))),
-                            __int_as_float(sum));
+    act_delta[g] = half_bits_to_double(v[0]);
+    act_sum[g] = sum;
   }
   __syncthreads();
   MLLB_TRACE_POINT(3);
@@ -150,7 +164,8 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
     const int q = m + 8 * i;  // group pair: groups 2q (low nibbles) and 2q + 1 (high nibbles)
     const uint4 al = lds128(act + resident_act_slot(2 * q) + 16 * h);
     const uint4 ah = lds128(act + resident_act_slot(2 * q + 1) + 16 * h);
-    const float2 ds = act_ds[2 * q + h];
+    const double delta = act_delta[2 * q + h];
+    const int sum = act_sum[2 * q + h];
     uint4 wv;
     if constexpr (kWeightsInRegs) wv = wq[i];
     else wv = lds128(row + (q >> 2) * kQ4kBlockBytes + 16 + 32 * (q & 3) + 16 * h);
@@ -165,11 +180,7 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
     dhi = dp4a_us(wv.w & 0xf0f0f0f0u, ah.w, dhi);
     // Lane h keeps group 2q+h and takes the partner's half of it.
     const int dot = (h ? dhi : dlo) + __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
-    const int sum = __float_as_int(ds.y);
-    // h = 1: the dot is 16x (high nibbles unshifted); scale the sum and the delta to match.
-    const double delta = static_cast<double>(ds.x) * (h ? 0.0625 : 1.0);
-    const double t = fma(static_cast<double>(dsc[i]), i2d_exact(dot),
-                         -static_cast<double>(dmn[i]) * i2d_exact(sum << (4 * h)));
+    const double t = fma(dsc[i], i2d_exact(dot), -dmn[i] * i2d_exact(sum));
     acc = fma(delta, t, acc);
   }
 #pragma unroll
