@@ -377,7 +377,8 @@ int mllb_decode_embed(const void *q6k_weights, int64_t vocab, int64_t k, mllb_de
  *   q8 = Q8_1(y) (s_mode as mllb_q8_1_quantize).  k: multiple of 32, <= 32768.
  * x_out may be x itself (in place; then one CTA does all the work) but must
  * not otherwise overlap x or delta.  A separate x_out spreads the blocks over
- * k/256 CTAs.
+ * k/256 CTAs.  With MLLB_LAUNCH_PDL, gamma (a weight) is read before the
+ * wait on the preceding kernel; x and delta after it.
  * GGML add -> rms_norm -> mul -> quantize_q8_1 (benchmark/q4_compare.c:328-330
  * is the quantise node this absorbs).
  */

@@ -114,13 +114,23 @@ __global__ void __launch_bounds__(256) rmsnorm_q8_1_kernel(const float* x, const
                                                            double eps, uint8_t* __restrict__ q8, int k, int s_mode,
                                                            DecodeState* advance) {
   __shared__ double partial[8];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
+  // gamma is a weight: this warp's first block's value is read before the
+  // dependency wait.
+  const int b0 = blockIdx.x * warps + warp;
+  const float gamma0 = b0 < k / 32 ? __ldg(gamma + b0 * 32 + lane) : 0.0f;
   pdl_wait_prerequisite();
   pdl_launch_dependents();
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, warps = blockDim.x >> 5;
   // Loads in batches of 16 per thread, all issued before their first use:
-  // one round trip to L2 for k <= 4096 with 256 threads.
+  // one round trip to L2 for k <= 4096 with 256 threads.  Thread t's batch
+  // holds elements t + 256 u; block b = blockIdx.x * warps + warp, which its
+  // warp quantises below, is element blockIdx.x * 256 + t, i.e. u =
+  // blockIdx.x: with a single batch (k <= 16 * blockDim) and blockDim = 256
+  // that h is kept rather than read again after the reduction.
   constexpr int kBatch = 16;
   double ss = 0.0;
+  float h_mine = 0.0f;
+  const bool single = k <= kBatch * static_cast<int>(blockDim.x) && blockDim.x == 256;
   for (int base = threadIdx.x; base < k; base += kBatch * blockDim.x) {
     float xv[kBatch], dv[kBatch];
 #pragma unroll
@@ -133,6 +143,7 @@ __global__ void __launch_bounds__(256) rmsnorm_q8_1_kernel(const float* x, const
     for (int u = 0; u < kBatch; ++u) {
       const float h = delta ? xv[u] + dv[u] : xv[u];
       ss = fma(static_cast<double>(h), static_cast<double>(h), ss);
+      if (u == static_cast<int>(blockIdx.x)) h_mine = h;
     }
   }
   ss = warp_sum_double(ss);
@@ -144,12 +155,18 @@ __global__ void __launch_bounds__(256) rmsnorm_q8_1_kernel(const float* x, const
   // Every thread has read all of x above; only then may an aliasing x_out
   // (single CTA) be written.
   __syncthreads();
-  for (int b = blockIdx.x * warps + warp; b < k / 32; b += gridDim.x * warps) {
+  for (int b = b0; b < k / 32; b += gridDim.x * warps) {
     const int i = b * 32 + lane;
-    float h = x[i];
-    if (delta) h += delta[i];
+    float h;
+    if (single && b == b0) {
+      h = h_mine;
+    } else {
+      h = x[i];
+      if (delta) h += delta[i];
+    }
     if (x_out) x_out[i] = h;
-    const float y = static_cast<float>(static_cast<double>(h) * r * static_cast<double>(gamma[i]));
+    const float g = b == b0 ? gamma0 : gamma[i];
+    const float y = static_cast<float>(static_cast<double>(h) * r * static_cast<double>(g));
     uint32_t d16, s16;
     const int q = q8_1_quantize_lane(y, s_mode, &d16, &s16);
     q8_1_store_block(q8 + static_cast<size_t>(b) * 36, q, d16, s16, lane);
