@@ -549,9 +549,11 @@ def run_ours(args, rank: int, world: int):
     # when the chain reaches them; the outputs of all but the last ~16 % of
     # the launches go back on a side stream while those run.  (Five equal
     # chunks with a join each: 1666-1687 GB/s against 1851 on one box.)
-    split = not sharded and copies >= 10
-    n_in = max(1, round(0.3 * copies)) if split else copies
-    tail = copies - max(1, round(0.16 * copies)) if split else 0
+    # (With fewer than 10 copies -- the 319 MB vocabulary matrix -- all
+    # activations come in first and only the last output's copy stays exposed:
+    # 4543-4617 against 4231 GB/s.)
+    n_in = max(1, round(0.3 * copies)) if not sharded and copies >= 10 else copies
+    tail = copies - max(1, round(0.16 * copies)) if not sharded and copies >= 2 else 0
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = torch.cuda.Event()
 
