@@ -210,6 +210,60 @@ def preroll(graph, seconds: float = 1.0) -> None:
     torch.cuda.synchronize()
 
 
+def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, steps):
+    """Device time (ms) of one end-to-end step over n independent items:
+    pinned H2D of their inputs, the op on each (a PDL chain), D2H of their
+    outputs, all captured in one CUDA graph.  The copies overlap the chain
+    with two stream joins only: the first ~30 % of the inputs come in on the
+    compute stream, the rest on a side stream before the chain reaches them,
+    and the outputs of all but the last ~16 % go back on a side stream while
+    those run.  copy_in(a, b) / copy_out(a, b) issue the copies of items
+    [a, b) on the current stream; op(i) launches item i.  Returns (ms, items
+    copied in before the chain, items copied out after it)."""
+    n_in = max(1, round(0.3 * n)) if n >= 10 else n
+    tail = n - max(1, round(0.16 * n)) if n >= 2 else 0
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    ev_in = torch.cuda.Event()
+
+    def step():
+        cur = torch.cuda.current_stream(device)
+        copy_in(0, n_in)
+        if n_in < n:
+            s_in.wait_stream(cur)
+            with torch.cuda.stream(s_in):
+                copy_in(n_in, n)
+                ev_in.record(s_in)
+        for i in range(n):
+            if i == n_in:
+                cur.wait_event(ev_in)
+            if i == tail and tail > 0:
+                s_out.wait_stream(cur)
+                with torch.cuda.stream(s_out):
+                    copy_out(0, tail)
+            op(i)
+        copy_out(tail, n)
+        if tail > 0:
+            cur.wait_stream(s_out)
+
+    step()  # eager once: launch attributes set outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=stream):
+        step()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    del g
+    return ms, n_in, n - tail
+
+
 # ----------------------------------------------------------------------------- inputs
 
 def host_weights(kind: str, rows: int, k: int, seed: int):
@@ -1483,25 +1537,28 @@ def run_imrope(args, rank: int, world: int, batched: bool):
     per_op = imrope_bytes(tokens, heads)
     gbs = per_op / (us_op * 1e-6) / 1e9
 
-    # e2e through the public API with host buffers: H2D of q, the op, D2H of the output.
-    q_pin = torch.from_numpy(inp["q"]).reshape(-1).pin_memory()
-    out_pin = torch.empty(tokens * heads * 128, dtype=torch.float32).pin_memory()
-    q_stage = torch.empty(tokens * heads * 128, device=device)
-    e_times = []
-    for i in range(args.warmup + args.steps):
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        for _ in range(copies if not batched else 1):
-            q_stage.copy_(q_pin, non_blocking=True)
-            if batched:
-                ops.rmsnorm_imrope_q(q_stage, gamma, pos, theta, out=outs[0], heads_per_token=heads)
-            else:
-                ops.fused_q_imrope_runtime_fastpow(q_stage, gamma, pos, outs[0], theta)
-            out_pin.copy_(outs[0], non_blocking=True)
-        torch.cuda.synchronize()
-        if i >= args.warmup:
-            e_times.append((time.perf_counter() - t1) / (copies if not batched else 1))
-    e_us = statistics.median(e_times) * 1e6
+    # e2e through the public API with host buffers: pinned H2D of each q, the
+    # op (the PDL-chained entry), D2H of its output; the step captured in a
+    # CUDA graph, copies overlapping the chain (one op a step in the
+    # many-token form).
+    n_e = 1 if batched else copies
+    q_pin = torch.stack([qs[i].cpu() for i in range(n_e)]).pin_memory()
+    q_stage = torch.empty(n_e, tokens * heads * 128, device=device)
+    out_pin = torch.empty(n_e, tokens * heads * 128, dtype=torch.float32).pin_memory()
+
+    def e2e_in(a, b):
+        q_stage[a:b].copy_(q_pin[a:b], non_blocking=True)
+
+    def e2e_op(i):
+        ops.rmsnorm_imrope_q(q_stage[i], gamma, pos, theta, out=outs[i], heads_per_token=heads, pdl=True,
+                             const_aux=True)
+
+    def e2e_out(a, b):
+        out_pin[a:b].copy_(outs[a:b], non_blocking=True)
+
+    e_ms, e_first, e_last = overlapped_e2e(torch, device, stream, n_e, e2e_in, e2e_op, e2e_out, args.warmup,
+                                          args.steps)
+    e_us = e_ms * 1e3 / n_e
     if ops.device_error():
         raise SystemExit("device error word set")
     del graph
@@ -1523,9 +1580,10 @@ def run_imrope(args, rank: int, world: int, batched: bool):
         value, unit, hib = round(us_op, 4), "us/op", False
         e2e = {"value": round(e_us, 3), "unit": "us/op"}
         metric = "fused RMSNorm+gamma+IMROPE 32x128 us/op"
-    e2e.update({"h2d_bytes_per_step": tokens * heads * 512 * (1 if batched else copies),
-                "d2h_bytes_per_step": tokens * heads * 512 * (1 if batched else copies),
-                "path": "ops.fused_q_imrope_runtime_fastpow / ops.rmsnorm_imrope_q with pinned H2D/D2H, eager"})
+    e2e.update({"h2d_bytes_per_step": tokens * heads * 512 * n_e, "d2h_bytes_per_step": tokens * heads * 512 * n_e,
+                "ops_per_step": n_e,
+                "path": f"ops.rmsnorm_imrope_q (PDL-chained) over {n_e} pinned inputs a step, H2D / D2H overlapping "
+                        f"the chain (first {e_first} in before it, last {e_last} out after it), in a CUDA graph"})
     line = {"metric": metric, "value": value, "unit": unit, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
             "scaling": "weak", "vs_baseline": None if batched else round(us_op / IMROPE_PUBLISHED_US, 4),
@@ -1671,22 +1729,29 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
     per_op = q8_1_bytes_per_op(k, tokens)
     gbs = per_op / (us_op * 1e-6) / 1e9
 
-    # e2e through the public API with host buffers: pinned H2D of x, the
-    # quantiser, D2H of the Q8_1 bytes, one op per step, eager.
-    x_pin = xs[0].cpu().pin_memory()
-    o_pin = torch.empty(outs.shape[1], dtype=torch.uint8).pin_memory()
-    x_stage = torch.empty_like(xs[0])
-    e_times = []
-    for i in range(args.warmup + args.steps):
-        torch.cuda.synchronize()
-        t1 = time.perf_counter()
-        x_stage.copy_(x_pin, non_blocking=True)
-        ops.quantize_q8_1(x_stage, outs[0])
-        o_pin.copy_(outs[0], non_blocking=True)
-        torch.cuda.synchronize()
-        if i >= args.warmup:
-            e_times.append(time.perf_counter() - t1)
-    e_us = statistics.median(e_times) * 1e6
+    # e2e through the public API with host buffers: pinned H2D of each x, the
+    # quantiser (the C ABI, PDL-chained), D2H of its Q8_1 bytes; the step
+    # captured in a CUDA graph, copies overlapping the chain (one op a step in
+    # the many-token form).
+    n_e = 1 if batched else copies
+    x_pin = xs[:n_e].cpu().pin_memory()
+    o_pin = torch.empty(n_e, outs.shape[1], dtype=torch.uint8).pin_memory()
+    x_stage = torch.empty_like(xs[:n_e])
+
+    def e2e_in(a, b):
+        x_stage[a:b].copy_(x_pin[a:b], non_blocking=True)
+
+    def e2e_op(i):
+        check(lib_.mllb_q8_1_quantize_ex(x_stage[i].data_ptr(), outs[i].data_ptr(), tokens * k, S_D_SUMQ,
+                                         LAUNCH_PDL, C.c_void_p(torch.cuda.current_stream(device).cuda_stream)),
+              "q8_1")
+
+    def e2e_out(a, b):
+        o_pin[a:b].copy_(outs[a:b], non_blocking=True)
+
+    e_ms, e_first, e_last = overlapped_e2e(torch, device, stream, n_e, e2e_in, e2e_op, e2e_out, args.warmup,
+                                          args.steps)
+    e_us = e_ms * 1e3 / n_e
     if ops.device_error():
         raise SystemExit("device error word set")
     del graph
@@ -1706,8 +1771,10 @@ def run_q8_1(args, rank: int, world: int, batched: bool):
     else:
         value, unit, hib = round(us_op, 4), "us/op", False
         e2e = {"value": round(e_us, 3), "unit": "us/op"}
-    e2e.update({"h2d_bytes_per_step": tokens * k * 4, "d2h_bytes_per_step": tokens * k // 32 * 36,
-                "path": "ops.quantize_q8_1 with pinned H2D/D2H, eager, one op per step"})
+    e2e.update({"h2d_bytes_per_step": tokens * k * 4 * n_e, "d2h_bytes_per_step": tokens * k // 32 * 36 * n_e,
+                "ops_per_step": n_e,
+                "path": f"mllb_q8_1_quantize_ex (PDL-chained) over {n_e} pinned inputs a step, H2D / D2H overlapping "
+                        f"the chain (first {e_first} in before it, last {e_last} out after it), in a CUDA graph"})
 
     line = {"metric": f"{q8_1_describe(batched, k)} {unit}", "value": value, "unit": unit, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 6), "higher_is_better": hib,
