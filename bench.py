@@ -210,7 +210,8 @@ def preroll(graph, seconds: float = 1.0) -> None:
     torch.cuda.synchronize()
 
 
-def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, steps):
+def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, steps, overlap=True,
+                   before_timing=None):
     """Device time (ms) of one end-to-end step over n independent items:
     pinned H2D of their inputs, the op on each (a PDL chain), D2H of their
     outputs, all captured in one CUDA graph.  The copies overlap the chain
@@ -218,10 +219,15 @@ def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, step
     compute stream, the rest on a side stream before the chain reaches them,
     and the outputs of all but the last ~16 % go back on a side stream while
     those run.  copy_in(a, b) / copy_out(a, b) issue the copies of items
-    [a, b) on the current stream; op(i) launches item i.  Returns (ms, items
-    copied in before the chain, items copied out after it)."""
-    n_in = max(1, round(0.3 * n)) if n >= 10 else n
-    tail = n - max(1, round(0.16 * n)) if n >= 2 else 0
+    [a, b) on the current stream; op(i) launches item i (item 0 and item
+    n_in start their input halves).  overlap=False (steps with collectives):
+    all inputs, the chain, all outputs, in order.  Returns (ms, items copied
+    in before the chain, items copied out after it).  (Five equal chunks with
+    a join each measured 1666-1687 GB/s against 1851 for this arrangement on
+    the Q4_K matvec, one box; with fewer than 10 items all inputs come in
+    first and only the last output's copy stays exposed.)"""
+    n_in = max(1, round(0.3 * n)) if overlap and n >= 10 else n
+    tail = n - max(1, round(0.16 * n)) if overlap and n >= 2 else 0
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = torch.cuda.Event()
 
@@ -253,6 +259,8 @@ def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, step
     for _ in range(warmup):
         g.replay()
     torch.cuda.synchronize()
+    if before_timing:
+        before_timing()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record(stream)
     for _ in range(steps):
@@ -260,7 +268,7 @@ def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, step
     e1.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / steps
-    del g
+    del g  # before any process group goes away: the graph may hold collectives
     return ms, n_in, n - tail
 
 
@@ -597,62 +605,26 @@ def run_ours(args, rank: int, world: int):
     x_stage = torch.empty(copies, k, dtype=torch.float32, device=device)
 
     # Without collectives in the launches (replicas), the copies overlap the
-    # chain with two stream joins only (each join costs more than a chunk's
-    # copy): the first ~30 % of the activations come in on the compute stream
-    # and are quantised while the rest travels on a side stream, quantised
-    # when the chain reaches them; the outputs of all but the last ~16 % of
-    # the launches go back on a side stream while those run.  (Five equal
-    # chunks with a join each: 1666-1687 GB/s against 1851 on one box.)
-    # (With fewer than 10 copies -- the 319 MB vocabulary matrix -- all
-    # activations come in first and only the last output's copy stays exposed:
-    # 4543-4617 against 4231 GB/s.)
-    n_in = max(1, round(0.3 * copies)) if not sharded and copies >= 10 else copies
-    tail = copies - max(1, round(0.16 * copies)) if not sharded and copies >= 2 else 0
-    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    ev_in = torch.cuda.Event()
+    # chain (overlapped_e2e); the first item of each input half also
+    # quantises that half's activations in one launch.
+    def e2e_in(a, b):
+        x_stage[a:b].copy_(x_pin[a:b], non_blocking=True)
 
-    def e2e_step():
-        cur = torch.cuda.current_stream(device)
-        x_stage[:n_in].copy_(x_pin[:n_in], non_blocking=True)
-        if n_in < copies:
-            s_in.wait_stream(cur)
-            with torch.cuda.stream(s_in):
-                x_stage[n_in:].copy_(x_pin[n_in:], non_blocking=True)
-                ev_in.record(s_in)
-        ops.quantize_q8_1(x_stage[:n_in].reshape(-1), acts[:n_in].reshape(-1))
-        for i in range(copies):
-            if i == n_in:
-                cur.wait_event(ev_in)
-                ops.quantize_q8_1(x_stage[n_in:].reshape(-1), acts[n_in:].reshape(-1))
-            if i == tail and tail > 0:
-                s_out.wait_stream(cur)
-                with torch.cuda.stream(s_out):
-                    out_pin[:tail].copy_(result[:tail], non_blocking=True)
-            launch(i)
-        out_pin[tail:].copy_(result[tail:], non_blocking=True)
-        if tail > 0:
-            cur.wait_stream(s_out)
+    def e2e_op(i):
+        if i == 0 or i == e2e_halves[1]:
+            b = e2e_halves[1] if i == 0 else copies
+            ops.quantize_q8_1(x_stage[i:b].reshape(-1), acts[i:b].reshape(-1))
+        launch(i)
 
-    # One eager pass (launch attributes set outside any capture), then the
-    # step -- copies included -- captured in a CUDA graph, as a serving loop
-    # would run it: host launch overhead stays out, the PCIe copies stay in.
-    e2e_step()
-    torch.cuda.synchronize()
-    e2e_graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(e2e_graph, stream=stream):
-        e2e_step()
-    for _ in range(args.warmup):
-        e2e_graph.replay()
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e_start.record(stream)
-    for _ in range(args.steps):
-        e2e_graph.replay()
-    e_stop.record(stream)
-    torch.cuda.synchronize()
-    e_ms = e_start.elapsed_time(e_stop) / args.steps
+    def e2e_out(a, b):
+        out_pin[a:b].copy_(result[a:b], non_blocking=True)
+
+    overlap = not sharded
+    e2e_halves = [0, max(1, round(0.3 * copies)) if overlap and copies >= 10 else copies]
+    e_ms, n_in, n_out = overlapped_e2e(torch, device, stream, copies, e2e_in, e2e_op, e2e_out, args.warmup,
+                                       args.steps, overlap=overlap,
+                                       before_timing=dist.barrier if world > 1 else None)
+    assert n_in == e2e_halves[1]
     if world > 1:
         t = torch.tensor([e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -661,7 +633,7 @@ def run_ours(args, rank: int, world: int):
     derr = ops.device_error()
     if derr:
         raise SystemExit(f"device error word set: {derr:#x}")
-    del graph, e2e_graph
+    del graph
     if world > 1:
         dist.barrier()
 
@@ -681,7 +653,7 @@ def run_ours(args, rank: int, world: int):
                     "d2h_bytes_per_step": int(result.numel() * 4), "ms_per_step": round(e_ms, 6),
                     "path": "ops.quantize_q8_1 over the activations (two launches), then ops.<matvec> per launch "
                             "(ctypes C-ABI), with the pinned H2D/D2H copies overlapping the chain "
-                            f"(first {n_in} activations in before it, last {copies - tail} outputs out after it); "
+                            f"(first {n_in} activations in before it, last {n_out} outputs out after it); "
                             "the step captured in a CUDA graph"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
