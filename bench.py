@@ -478,18 +478,20 @@ def run_ours(args, rank: int, world: int):
     outs = torch.empty(copies, n_out, my_rows, dtype=torch.float32, device=device)
     gathered = torch.empty(copies, world, n_out, my_rows, dtype=torch.float32, device=device) if sharded else None
 
-    def launch(i: int):
-        w, o = weights[i], outs[i]
+    def launch_on(w, a, o, g):
         if kind == "q6k":
-            ops.q6_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+            ops.q6_k_q8_1_matvec(w[0], a, o[0], pdl=pdl)
         elif kind == "q5k":
-            ops.q5_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+            ops.q5_k_q8_1_matvec(w[0], a, o[0], pdl=pdl)
         elif kind == "gate_up":
-            ops.q4k_gate_up(w[0], w[1], acts[i], o[0], o[1], o[2], pdl=pdl)
+            ops.q4k_gate_up(w[0], w[1], a, o[0], o[1], o[2], pdl=pdl)
         else:
-            ops.q4_k_q8_1_matvec(w[0], acts[i], o[0], pdl=pdl)
+            ops.q4_k_q8_1_matvec(w[0], a, o[0], pdl=pdl)
         if sharded:
-            dist.all_gather_into_tensor(gathered[i].view(-1), o.view(-1))  # = shard.all_gather_rows layout
+            dist.all_gather_into_tensor(g.view(-1), o.view(-1))  # = shard.all_gather_rows layout
+
+    def launch(i: int):
+        launch_on(weights[i], acts[i], outs[i], gathered[i] if sharded else None)
 
     def step():
         for i in range(copies):
@@ -595,41 +597,45 @@ def run_ours(args, rank: int, world: int):
     job_ops = copies * passes * (1 if sharded else world)
     value = job_ops * per_op / (ms * 1e-3) / 1e9
 
-    # e2e through the public API with host buffers: every step copies its fp32
-    # activations from pinned host memory, quantises them on the device (one
-    # quantiser launch over the step's contiguous activations), runs the
-    # launches (and all-gathers) and copies the gathered outputs back.
-    x_pin = torch.from_numpy(xs_host).pin_memory()
-    result = gathered if sharded else outs
-    out_pin = torch.empty(result.shape, dtype=torch.float32).pin_memory()
-    x_stage = torch.empty(copies, k, dtype=torch.float32, device=device)
+    # e2e through the public API with host buffers: the same step as the
+    # timed one (passes x copies launches over the weight copies), each launch
+    # with its own fp32 activation copied from pinned host memory, quantised
+    # on the device, and its own outputs (all-gathered) copied back.  Without
+    # collectives in the launches (replicas) the copies overlap the chain
+    # (overlapped_e2e); the first launch of each input half also quantises
+    # that half's activations in one launch.
+    n_e = passes * copies
+    x_pin = torch.from_numpy(np.tile(xs_host, (passes, 1))).pin_memory()
+    x_stage = torch.empty(n_e, k, dtype=torch.float32, device=device)
+    e_acts = torch.empty(n_e, acts.shape[1], dtype=acts.dtype, device=device)
+    e_outs = torch.empty(n_e, n_out, my_rows, dtype=torch.float32, device=device)
+    e_gath = torch.empty(n_e, world, n_out, my_rows, dtype=torch.float32, device=device) if sharded else None
+    e_result = e_gath if sharded else e_outs
+    out_pin = torch.empty(e_result.shape, dtype=torch.float32).pin_memory()
+    overlap = not sharded
+    e2e_halves = [0, max(1, round(0.3 * n_e)) if overlap and n_e >= 10 else n_e]
 
-    # Without collectives in the launches (replicas), the copies overlap the
-    # chain (overlapped_e2e); the first item of each input half also
-    # quantises that half's activations in one launch.
     def e2e_in(a, b):
         x_stage[a:b].copy_(x_pin[a:b], non_blocking=True)
 
     def e2e_op(i):
         if i == 0 or i == e2e_halves[1]:
-            b = e2e_halves[1] if i == 0 else copies
-            ops.quantize_q8_1(x_stage[i:b].reshape(-1), acts[i:b].reshape(-1))
-        launch(i)
+            b = e2e_halves[1] if i == 0 else n_e
+            ops.quantize_q8_1(x_stage[i:b].reshape(-1), e_acts[i:b].reshape(-1))
+        launch_on(weights[i % copies], e_acts[i], e_outs[i], e_gath[i] if sharded else None)
 
     def e2e_out(a, b):
-        out_pin[a:b].copy_(result[a:b], non_blocking=True)
+        out_pin[a:b].copy_(e_result[a:b], non_blocking=True)
 
-    overlap = not sharded
-    e2e_halves = [0, max(1, round(0.3 * copies)) if overlap and copies >= 10 else copies]
-    e_ms, n_in, n_out = overlapped_e2e(torch, device, stream, copies, e2e_in, e2e_op, e2e_out, args.warmup,
-                                       args.steps, overlap=overlap,
-                                       before_timing=dist.barrier if world > 1 else None)
+    e_ms, n_in, n_last = overlapped_e2e(torch, device, stream, n_e, e2e_in, e2e_op, e2e_out, args.warmup,
+                                        args.steps, overlap=overlap,
+                                        before_timing=dist.barrier if world > 1 else None)
     assert n_in == e2e_halves[1]
     if world > 1:
         t = torch.tensor([e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e_ms = float(t.item())
-    e2e_value = copies * (1 if sharded else world) * per_op / (e_ms * 1e-3) / 1e9
+    e2e_value = n_e * (1 if sharded else world) * per_op / (e_ms * 1e-3) / 1e9
     derr = ops.device_error()
     if derr:
         raise SystemExit(f"device error word set: {derr:#x}")
@@ -649,11 +655,12 @@ def run_ours(args, rank: int, world: int):
             "config": matvec_config(args.workload, world, pdl, args.copies),
             "passes_per_step": passes, "launches_per_step": copies * passes,
             "us_per_op": round(ms * 1e3 / (copies * passes), 4),
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": copies * k * 4,
-                    "d2h_bytes_per_step": int(result.numel() * 4), "ms_per_step": round(e_ms, 6),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": n_e * k * 4,
+                    "d2h_bytes_per_step": int(e_result.numel() * 4), "ms_per_step": round(e_ms, 6),
+                    "launches_per_step": n_e,
                     "path": "ops.quantize_q8_1 over the activations (two launches), then ops.<matvec> per launch "
                             "(ctypes C-ABI), with the pinned H2D/D2H copies overlapping the chain "
-                            f"(first {n_in} activations in before it, last {n_out} outputs out after it); "
+                            f"(first {n_in} activations in before it, last {n_last} outputs out after it); "
                             "the step captured in a CUDA graph"},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
