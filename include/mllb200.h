@@ -37,7 +37,7 @@ extern "C" {
 #define MLLB_EINVAL (-1)       /* null pointer, bad size or shape (reference harness exit 4) */
 #define MLLB_EALIGN (-2)       /* pointer alignment below the contract */
 #define MLLB_ECUDA (-3)        /* CUDA launch or runtime error (reference harness exit 20) */
-#define MLLB_EUNSUPPORTED (-4) /* shape outside what this build implements */
+#define MLLB_EUNSUPPORTED (-4) /* shape outside what the library implements */
 
 /*
  * Launch flags of the *_ex entry points.
