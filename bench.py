@@ -63,7 +63,7 @@ WORKLOADS = {
     "gate_up": dict(kind="gate_up", rows=9728, k=2560, kernel="team_stream_kernel<Q4kFormat,10,2,4,6,3>",
                     profile="q4k_gate_up_n9728_k2560"),
     # the Q5_K matvec at the headline shape (4096 x 2560)
-    "q5k_matvec": dict(kind="q5k", rows=4096, k=2560, kernel="team_stream_kernel<Q5kFormat,10,1,8,2,2>",
+    "q5k_matvec": dict(kind="q5k", rows=4096, k=2560, kernel="resident_q5k_kernel<10>",
                        profile="q5k_matvec_n4096_k2560"),
     # Q6_K vocabulary projection 151936x2560
     "q6k_vocab": dict(kind="q6k", rows=151936, k=2560, kernel="team_stream_kernel<Q6kFormat,10,1,4,6,5>",

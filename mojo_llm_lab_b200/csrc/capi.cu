@@ -318,32 +318,34 @@ int q4k_norm_team(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, in
   return fail(MLLB_EUNSUPPORTED, "no streaming configuration for K=%lld", static_cast<long long>(k));
 }
 
-// Resident-weights path (csrc/resident.cuh): a plain Q4_K matvec of at most
-// 32 rows per SM with K = 2560 or 4096 runs with all its weights in shared
-// memory, brought in before the dependency wait.  MLLB_EUNSUPPORTED (nothing
-// launched) for other shapes.  MLLB_Q4K_RESIDENT=0 turns it off (the
+// Resident-weights path (csrc/resident.cuh): a plain Q4_K or Q5_K matvec of
+// at most 32 rows per SM with K = 2560 or 4096 runs with all its weights in
+// shared memory, brought in before the dependency wait.  MLLB_EUNSUPPORTED
+// (nothing launched) for other shapes.  MLLB_Q4K_RESIDENT=0 turns it off (the
 // streaming kernels then take every shape).
-template <int NB>
+template <int NB, bool kQ5>
 int launch_resident(int dev, const uint8_t* w, const uint8_t* q8, float* out, int rows, int per_cta,
                     cudaStream_t stream, bool pdl) {
-  auto kernel = mllb::resident_q4k_kernel<NB>;
+  auto kernel = kQ5 ? mllb::resident_q5k_kernel<NB> : mllb::resident_q4k_kernel<NB>;
+  constexpr int block_bytes = mllb::ResidentBlock<kQ5>::kBytes;
   static std::once_flag once[kMaxDevices];
   static cudaError_t attr_err[kMaxDevices];
   std::call_once(once[dev], [&] {
     attr_err[dev] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         mllb::kResidentMaxRowsPerCta * NB * mllb::kQ4kBlockBytes);
+                                         mllb::kResidentMaxRowsPerCta * NB * block_bytes);
   });
   if (attr_err[dev] != cudaSuccess)
     return fail(MLLB_ECUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(attr_err[dev]));
   const int grid = (rows + per_cta - 1) / per_cta;
   const int threads = 32 * ((per_cta + 1) / 2);
-  const size_t smem = static_cast<size_t>(per_cta) * NB * mllb::kQ4kBlockBytes;
+  const size_t smem = static_cast<size_t>(per_cta) * NB * block_bytes;
   return launched(launch(kernel, dim3(grid), dim3(threads), smem, stream, pdl, w, q8, out, rows, per_cta),
-                  "resident Q4_K matvec kernel");
+                  kQ5 ? "resident Q5_K matvec kernel" : "resident Q4_K matvec kernel");
 }
 
-int q4k_resident(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int64_t k, cudaStream_t stream,
-                 bool pdl) {
+template <bool kQ5>
+int k_resident(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int64_t k, cudaStream_t stream,
+               bool pdl) {
   static const bool enabled = [] {
     const char* env = getenv("MLLB_Q4K_RESIDENT");
     return !(env && env[0] == '0');
@@ -356,10 +358,15 @@ int q4k_resident(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int
   const int rows = static_cast<int>(n);
   const int per_cta = (rows + sms - 1) / sms;
   switch (k / 256) {
-    case 10: return launch_resident<10>(dev, w, q8, out, rows, per_cta, stream, pdl);
-    case 16: return launch_resident<16>(dev, w, q8, out, rows, per_cta, stream, pdl);
+    case 10: return launch_resident<10, kQ5>(dev, w, q8, out, rows, per_cta, stream, pdl);
+    case 16: return launch_resident<16, kQ5>(dev, w, q8, out, rows, per_cta, stream, pdl);
     default: return MLLB_EUNSUPPORTED;
   }
+}
+
+int q4k_resident(const uint8_t* w, const uint8_t* q8, float* out, int64_t n, int64_t k, cudaStream_t stream,
+                 bool pdl) {
+  return k_resident<false>(w, q8, out, n, k, stream, pdl);
 }
 
 int q4k_dispatch(const uint8_t* w0, const uint8_t* w1, const uint8_t* q8, float* o0, float* o1, float* o2,
@@ -1323,6 +1330,8 @@ extern "C" int mllb_q5k_matvec_ex(const void* weights, const void* q8, float* ou
   const int rows = static_cast<int>(n);
   const cudaStream_t s = static_cast<cudaStream_t>(stream);
   const bool pdl = flags & MLLB_LAUNCH_PDL;
+  rc = k_resident<true>(w, static_cast<const uint8_t*>(q8), out, n, k, s, pdl);
+  if (rc != MLLB_EUNSUPPORTED) return rc;
   switch (k / 256) {
     case 8: return launch_team<F, 8, 1, MLLB_CFG_Q5K_8>(w, nullptr, src, out, nullptr, nullptr, rows, s, pdl);
     case 10: {

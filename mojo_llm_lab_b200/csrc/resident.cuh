@@ -67,13 +67,24 @@ struct ResidentAct {
   static constexpr int kBytes = kQuantBytes + kGroups * 12;  // + fp64 delta, then int32 sum q, per group
 };
 
-template <int NB>
-__global__ void __launch_bounds__(kResidentThreads, 2)
-    resident_q4k_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8, float* __restrict__ out,
-                        int n_rows, int rows_per_cta) {
+// Super-block layout of the two formats: Q4_K (144 B: d, dmin, 12 scale
+// bytes, 128 nibble bytes) and Q5_K (176 B: the same header, qh[32] -- bit g
+// of qh[l] is the fifth bit of element l of group g -- then the 128 nibble
+// bytes).
+template <bool kQ5>
+struct ResidentBlock {
+  static constexpr int kBytes = kQ5 ? 176 : kQ4kBlockBytes;
+  static constexpr int kQsOffset = kQ5 ? 48 : 16;
+  static constexpr int kQhOffset = 16;
+};
+
+template <int NB, bool kQ5>
+__device__ __forceinline__ void resident_body(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8,
+                                              float* __restrict__ out, int n_rows, int rows_per_cta) {
   static_assert(NB % 2 == 0, "two units per group pair: NB must be even");
+  using B = ResidentBlock<kQ5>;
   constexpr int UPL = NB / 2;  // units per lane
-  constexpr int ROWB = NB * kQ4kBlockBytes;
+  constexpr int ROWB = NB * B::kBytes;
   constexpr int G = NB * 8;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ uint64_t bar;
@@ -110,14 +121,16 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
   const uint8_t* row = smem + (r < rows ? r : rows - 1) * ROWB;
   // Nibbles in registers before the wait when they fit the 64-register
   // budget (NB = 10); wider rows re-read them from shared memory after it.
-  constexpr bool kWeightsInRegs = UPL <= MLLB_RESIDENT_WQ_REGS_MAX;
+  // (Q5_K reads its nibbles and fifth bits from shared memory after the
+  // wait: the two would not fit beside the fp64 scales.)
+  constexpr bool kWeightsInRegs = !kQ5 && UPL <= MLLB_RESIDENT_WQ_REGS_MAX;
   uint4 wq[kWeightsInRegs ? UPL : 1];
   double dsc[UPL], dmn[UPL];
 #pragma unroll
   for (int i = 0; i < UPL; ++i) {
     const int q = m + 8 * i, b = q >> 2, j = q & 3, s = 2 * j + h;
-    const uint8_t* blk = row + b * kQ4kBlockBytes;
-    if constexpr (kWeightsInRegs) wq[i] = lds128(blk + 16 + 32 * j + 16 * h);
+    const uint8_t* blk = row + b * B::kBytes;
+    if constexpr (kWeightsInRegs) wq[i] = lds128(blk + B::kQsOffset + 32 * j + 16 * h);
     const uint32_t dd = lds32(blk);
     const uint8_t* sm = blk + 4;
     int sc, mn;
@@ -129,11 +142,12 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
       mn = (sm[s + 4] >> 4) | ((sm[s] >> 6) << 4);
     }
     // fp16 d (11 significant bits) x 6-bit scale: exact in fp32.
-    // The lane's high-nibble dots are 16x (unshifted nibbles): 1/16 enters
-    // its d * sc here, exactly, so no conversion or scaling remains after
-    // the wait.
+    // Q4_K: the lane's high-nibble dots are 16x (unshifted nibbles): 1/16
+    // enters its d * sc here, exactly, so no conversion or scaling remains
+    // after the wait.  Q5_K shifts its high nibbles down to merge the fifth
+    // bits, so its dots are 1x.
     dsc[i] = static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(dd & 0xffffu))) *
-                                 static_cast<float>(sc)) * (h ? 0.0625 : 1.0);
+                                 static_cast<float>(sc)) * ((h && !kQ5) ? 0.0625 : 1.0);
     dmn[i] = static_cast<double>(__half2float(__ushort_as_half(static_cast<unsigned short>(dd >> 16))) *
                                  static_cast<float>(mn));
   }
@@ -167,17 +181,34 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
     const double delta = act_delta[2 * q + h];
     const int sum = act_sum[2 * q + h];
     uint4 wv;
+    const uint8_t* blk = row + (q >> 2) * B::kBytes;
     if constexpr (kWeightsInRegs) wv = wq[i];
-    else wv = lds128(row + (q >> 2) * kQ4kBlockBytes + 16 + 32 * (q & 3) + 16 * h);
-    // Low nibbles x group 2q; high nibbles (unshifted, 16x) x group 2q + 1.
-    int dlo = dp4a_us(wv.x & 0x0f0f0f0fu, al.x, 0);
-    int dhi = dp4a_us(wv.x & 0xf0f0f0f0u, ah.x, 0);
-    dlo = dp4a_us(wv.y & 0x0f0f0f0fu, al.y, dlo);
-    dhi = dp4a_us(wv.y & 0xf0f0f0f0u, ah.y, dhi);
-    dlo = dp4a_us(wv.z & 0x0f0f0f0fu, al.z, dlo);
-    dhi = dp4a_us(wv.z & 0xf0f0f0f0u, ah.z, dhi);
-    dlo = dp4a_us(wv.w & 0x0f0f0f0fu, al.w, dlo);
-    dhi = dp4a_us(wv.w & 0xf0f0f0f0u, ah.w, dhi);
+    else wv = lds128(blk + B::kQsOffset + 32 * (q & 3) + 16 * h);
+    int dlo, dhi;
+    if constexpr (kQ5) {
+      // 5-bit values: low nibbles | fifth bit 2j, high nibbles >> 4 | fifth bit 2j + 1.
+      const uint4 hv = lds128(blk + B::kQhOffset + 16 * h);
+      const int lb = 2 * (q & 3);
+      const uint32_t wa[4] = {wv.x, wv.y, wv.z, wv.w}, ha[4] = {hv.x, hv.y, hv.z, hv.w};
+      const uint32_t xl[4] = {al.x, al.y, al.z, al.w}, xh[4] = {ah.x, ah.y, ah.z, ah.w};
+      dlo = 0;
+      dhi = 0;
+#pragma unroll
+      for (int t = 0; t < 4; ++t) {
+        dlo = dp4a_us((wa[t] & 0x0f0f0f0fu) | (((ha[t] >> lb) & 0x01010101u) << 4), xl[t], dlo);
+        dhi = dp4a_us(((wa[t] >> 4) & 0x0f0f0f0fu) | (((ha[t] >> (lb + 1)) & 0x01010101u) << 4), xh[t], dhi);
+      }
+    } else {
+      // Low nibbles x group 2q; high nibbles (unshifted, 16x) x group 2q + 1.
+      dlo = dp4a_us(wv.x & 0x0f0f0f0fu, al.x, 0);
+      dhi = dp4a_us(wv.x & 0xf0f0f0f0u, ah.x, 0);
+      dlo = dp4a_us(wv.y & 0x0f0f0f0fu, al.y, dlo);
+      dhi = dp4a_us(wv.y & 0xf0f0f0f0u, ah.y, dhi);
+      dlo = dp4a_us(wv.z & 0x0f0f0f0fu, al.z, dlo);
+      dhi = dp4a_us(wv.z & 0xf0f0f0f0u, ah.z, dhi);
+      dlo = dp4a_us(wv.w & 0x0f0f0f0fu, al.w, dlo);
+      dhi = dp4a_us(wv.w & 0xf0f0f0f0u, ah.w, dhi);
+    }
     // Lane h keeps group 2q+h and takes the partner's half of it.
     const int dot = (h ? dhi : dlo) + __shfl_xor_sync(0xffffffffu, h ? dlo : dhi, 1);
     const double t = fma(dsc[i], i2d_exact(dot), -dmn[i] * i2d_exact(sum));
@@ -187,6 +218,20 @@ __global__ void __launch_bounds__(kResidentThreads, 2)
   for (int off = 8; off >= 1; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   if (l16 == 0 && r < rows) out[row0 + r] = static_cast<float>(acc);
   MLLB_TRACE_POINT(7);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kResidentThreads, 2)
+    resident_q4k_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8, float* __restrict__ out,
+                        int n_rows, int rows_per_cta) {
+  resident_body<NB, false>(w, q8, out, n_rows, rows_per_cta);
+}
+
+template <int NB>
+__global__ void __launch_bounds__(kResidentThreads, 2)
+    resident_q5k_kernel(const uint8_t* __restrict__ w, const uint8_t* __restrict__ q8, float* __restrict__ out,
+                        int n_rows, int rows_per_cta) {
+  resident_body<NB, true>(w, q8, out, n_rows, rows_per_cta);
 }
 
 }  // namespace mllb
