@@ -1,5 +1,8 @@
-// Resident-weights Q4_K x Q8_1 matvec for matrices that fit in the SMs' shared
-// memory (a decode step's Q / K / V / O projections: N <= 32 rows per SM).
+// Resident-weights Q4_K (and Q5_K) x Q8_1 matvec for matrices that fit in the
+// SMs' shared memory (a decode step's Q / K / V / O projections: N <= 32 rows
+// per SM).  One body for both formats: Q5_K's 176-byte blocks carry the same
+// header and nibbles plus qh[32], whose fifth bits are merged into the
+// nibbles after the wait (resident_q5k_kernel).
 //
 // A matvec launched right after the kernel that produces its activation is
 // latency-bound, not bandwidth-bound: one 5.9 MB matrix streams in ~0.9 us,
