@@ -210,14 +210,28 @@ def preroll(graph, seconds: float = 1.0) -> None:
     torch.cuda.synchronize()
 
 
+def e2e_split(n: int, overlap: bool = True) -> tuple[int, int]:
+    """(items copied in before the chain, first item whose output is copied
+    out after it) for an overlapped e2e step of n items: ~30 % in / ~16 % out
+    for short steps, ~10 % / ~12 % from 100 items on (the rest of the inputs
+    still arrives well before the chain reaches it; 400-launch Q4_K step:
+    2214-2223 against 2191-2197 GB/s with the short-step fractions)."""
+    if not overlap:
+        return n, 0
+    f_in, f_out = (0.1, 0.12) if n >= 100 else (0.3, 0.16)
+    n_in = max(1, round(f_in * n)) if n >= 10 else n
+    tail = n - max(1, round(f_out * n)) if n >= 2 else 0
+    return n_in, tail
+
+
 def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, steps, overlap=True,
                    before_timing=None):
     """Device time (ms) of one end-to-end step over n independent items:
     pinned H2D of their inputs, the op on each (a PDL chain), D2H of their
     outputs, all captured in one CUDA graph.  The copies overlap the chain
-    with two stream joins only: the first ~30 % of the inputs come in on the
+    with two stream joins only: the first inputs (e2e_split) come in on the
     compute stream, the rest on a side stream before the chain reaches them,
-    and the outputs of all but the last ~16 % go back on a side stream while
+    and the outputs of all but the last few go back on a side stream while
     those run.  copy_in(a, b) / copy_out(a, b) issue the copies of items
     [a, b) on the current stream; op(i) launches item i (item 0 and item
     n_in start their input halves).  overlap=False (steps with collectives):
@@ -226,8 +240,7 @@ def overlapped_e2e(torch, device, stream, n, copy_in, op, copy_out, warmup, step
     a join each measured 1666-1687 GB/s against 1851 for this arrangement on
     the Q4_K matvec, one box; with fewer than 10 items all inputs come in
     first and only the last output's copy stays exposed.)"""
-    n_in = max(1, round(0.3 * n)) if overlap and n >= 10 else n
-    tail = n - max(1, round(0.16 * n)) if overlap and n >= 2 else 0
+    n_in, tail = e2e_split(n, overlap)
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     ev_in = torch.cuda.Event()
 
@@ -613,7 +626,7 @@ def run_ours(args, rank: int, world: int):
     e_result = e_gath if sharded else e_outs
     out_pin = torch.empty(e_result.shape, dtype=torch.float32).pin_memory()
     overlap = not sharded
-    e2e_halves = [0, max(1, round(0.3 * n_e)) if overlap and n_e >= 10 else n_e]
+    e2e_halves = [0, e2e_split(n_e, overlap)[0]]
 
     def e2e_in(a, b):
         x_stage[a:b].copy_(x_pin[a:b], non_blocking=True)

@@ -73,3 +73,18 @@ def test_reference_arm_config_is_the_gpu_arms(workload, config):
     sys.path.insert(0, str(ROOT))
     import bench
     assert run_bench(["--workload", workload])[0]["config"] == config(bench)
+
+
+def test_e2e_split_keeps_every_item_and_both_joins_inside_the_step():
+    """The overlapped e2e step's split: inputs [0, n_in) before the chain,
+    outputs [tail, n) after it; no split with collectives in the step."""
+    sys.path.insert(0, str(ROOT))
+    import bench
+    assert bench.e2e_split(50) == (15, 42)
+    assert bench.e2e_split(400) == (40, 352)
+    assert bench.e2e_split(2) == (2, 1)
+    assert bench.e2e_split(1) == (1, 0)
+    assert bench.e2e_split(400, overlap=False) == (400, 0)
+    for n in range(1, 600):
+        n_in, tail = bench.e2e_split(n)
+        assert 1 <= n_in <= n and 0 <= tail < n
