@@ -213,12 +213,14 @@ def preroll(graph, seconds: float = 1.0) -> None:
 def e2e_split(n: int, overlap: bool = True) -> tuple[int, int]:
     """(items copied in before the chain, first item whose output is copied
     out after it) for an overlapped e2e step of n items: ~30 % in / ~16 % out
-    for short steps, ~10 % / ~12 % from 100 items on (the rest of the inputs
+    for short steps, ~10 % / ~12 % from 200 items on (the rest of the inputs
     still arrives well before the chain reaches it; 400-launch Q4_K step:
-    2214-2223 against 2191-2197 GB/s with the short-step fractions)."""
+    2214-2223 against 2191-2197 GB/s with the short-step fractions; the
+    132-launch gate/up step, whose outputs are 117 KB a launch, needs the
+    longer tail for its copy back: 3157 against 3222-3244)."""
     if not overlap:
         return n, 0
-    f_in, f_out = (0.1, 0.12) if n >= 100 else (0.3, 0.16)
+    f_in, f_out = (0.1, 0.12) if n >= 200 else (0.3, 0.16)
     n_in = max(1, round(f_in * n)) if n >= 10 else n
     tail = n - max(1, round(f_out * n)) if n >= 2 else 0
     return n_in, tail

@@ -82,6 +82,7 @@ def test_e2e_split_keeps_every_item_and_both_joins_inside_the_step():
     import bench
     assert bench.e2e_split(50) == (15, 42)
     assert bench.e2e_split(400) == (40, 352)
+    assert bench.e2e_split(132) == (40, 111)
     assert bench.e2e_split(2) == (2, 1)
     assert bench.e2e_split(1) == (1, 0)
     assert bench.e2e_split(400, overlap=False) == (400, 0)
